@@ -1,0 +1,470 @@
+"""Benchmark of the B200 Conformer conv-module kernels.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload stack|module|module_i8|dw] [--impl ours|reference]
+
+Default workload ("stack"): 16 conv-module layers (independent seeds) over 512 synthetic utterances per rank with
+lognormal lengths (median 600 frames, sigma 0.5, clipped to [64, 1536]), sorted by length, logical batches of 128
+cut into execution chunks of <= 48 padded to the 128-frame grid.  One step = every chunk through all 16 layers.
+Each rank owns its own 512 utterances (weak scaling, no collective in the loop); value = valid frames x 16 layers
+of all ranks / the slowest rank's time.  Inputs are resident in HBM and larger than L2 (~0.7 GB per step).
+
+Other workloads (single-GPU measurements): "module" = one conv module on one B=48 chunk (lognormal lengths, T on
+the 128 grid), "module_i8" = the same with int8 weights, "dw" = the depthwise kernel alone on [48, 1024, 2048].
+
+``--impl reference`` times the CPU oracle (numpy restatement of the reference eager module) on the host cores on a
+bounded sample of the same workload and prints the same JSON line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "granite-speech-4.1-2b-nar-turbo_b200"))
+
+from granite_conv_b200 import dispatch, synth  # noqa: E402
+
+N_LAYERS = 16
+N_UTTS = 512
+D, I = synth.D_MODEL, synth.D_INNER
+GEMM1_FLOP_PER_FRAME = 2 * D * 2 * I          # 8.389 MFLOP
+GEMM2_FLOP_PER_FRAME = 2 * I * D              # 4.194 MFLOP
+DW_BYTES_PER_FRAME = 2 * I * 2                # read + write bf16: 8192 B
+METRIC = "conv-module frames/s at 1/2/4/8 B200; % of HBM / tensor-pipe roofline"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU through NVML every 200 ms while running."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap", 0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown", 0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown", 0x0000000000000002: "applications_clocks_setting",
+    }
+
+    def __init__(self, torch_device_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        self._handle = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(torch_device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            self._nvml = pynvml
+        except Exception as e:  # noqa: BLE001
+            self.error = f"nvml unavailable: {e}"
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "note": getattr(self, "error", "no samples")}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------------------------------------------
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _workload_plan(rank: int, workload: str):
+    """Chunks of this rank (list of dispatch.Chunk) for the workload."""
+    if workload == "stack":
+        lens = synth.sample_lengths(1005 + 7919 * rank, N_UTTS)
+        return dispatch.plan_chunks(lens, exec_batch=dispatch.EXEC_BATCH, logical_batch=dispatch.LOGICAL_BATCH,
+                                    frame_grid=dispatch.FRAME_GRID)
+    if workload in ("module", "module_i8"):
+        lens = synth.sample_lengths(1003 + 7919 * rank, 48)
+        T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
+        return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
+    if workload == "dw":
+        return [dispatch.Chunk(index=np.arange(48), lengths=np.full(48, 1024, np.int32), T=1024)]
+    raise ValueError(workload)
+
+
+def _layers_for(workload: str) -> int:
+    return N_LAYERS if workload == "stack" else 1
+
+
+# ----------------------------------------------------------------------------------------------------------------
+def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
+    """frames/s (valid frames x layers per second) of the numpy oracle (float32, all host threads through BLAS) on a
+    bounded sample of the workload: the shortest chunks of the plan, one layer each, until budget_s is spent."""
+    from oracle import conv_module as O
+    chunks = _workload_plan(rank, workload)
+    if workload == "dw":
+        w, b = synth.make_dw_weights(1002)
+        wb, bb = O.bf16_round(w), O.bf16_round(b)
+    else:
+        params = synth.make_params(1005)
+        prep = O.prepare_fp32(params)
+    frames = 0
+    t0 = time.perf_counter()
+    done = 0
+    sample_desc = []
+    i = 0
+    while True:
+        c = chunks[i % len(chunks)]
+        B = min(c.B, 4)
+        T = int(c.lengths[:B].max())
+        x = synth.make_activations(77 + i, (B, T, I if workload == "dw" else D))
+        lens = c.lengths[:B]
+        if workload == "dw":
+            O.dwconv_silu(x, wb, bb, lengths=lens, round_out=False)
+        else:
+            O.conv_module(x, prep, lengths=lens, mode="fp32", dtype=np.float32)
+        frames += int(lens.sum())
+        done += 1
+        sample_desc.append((B, T))
+        i += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = len(os.sched_getaffinity(0))
+    desc = (f"{done} chunk slices (first 4 utterances of each chunk, 1 layer each, float32 numpy oracle), "
+            f"{frames} valid frames in {dt:.1f} s")
+    return frames / dt, cores, desc
+
+
+def run_reference(args):
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return 0
+    budget = max(0.5, min(20.0, 60.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_oracle_rate(args.workload, min(budget, 1.0))
+    rates = []
+    for _ in range(args.steps):
+        r, cores, desc = cpu_oracle_rate(args.workload, budget)
+        rates.append(r)
+    v = float(statistics.median(rates))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "frames/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config(args, world),
+        "cpu_baseline": {"value": v, "unit": "frames/s", "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _config(args, world):
+    w = args.workload
+    cfg = {"workload": {
+        "stack": "16-layer Conformer conv-module stack (LN, 1024->4096 GEMM+GLU, dw k15+SiLU, 2048->1024 GEMM+"
+                 "residual), 512 utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid",
+        "module": "one conv module, B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
+        "module_i8": "one conv module with int8 per-channel weights, B=48 chunk, lognormal lengths, length mask",
+        "dw": "depthwise k15 + bias + SiLU alone, bf16 [48, 1024, 2048] channels-last, all frames valid"}[w],
+        "d_model": D, "d_inner": I, "kernel": 15, "layers": _layers_for(w),
+        "utterances_per_rank": N_UTTS if w == "stack" else 48, "exec_batch": dispatch.EXEC_BATCH,
+        "frame_grid": dispatch.FRAME_GRID, "parallelism": f"dp{world} (independent shards, no collective)",
+        "l2": "inputs larger than L2 (no flush)",
+        "frames": "valid encoder frames x layers (padding excluded)"}
+    return cfg
+
+
+# ----------------------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from granite_conv_b200 import _lib, ops
+    from granite_conv_b200.weights import prepare_from_params
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    workload = args.workload
+    int8 = workload == "module_i8"
+    n_layers = _layers_for(workload)
+
+    chunks = _workload_plan(rank, workload)
+    valid_frames = sum(c.valid_frames for c in chunks) * n_layers
+    padded_frames = sum(c.padded_frames for c in chunks) * n_layers
+
+    # ---- resident inputs and weights
+    gen = torch.Generator(device=dev).manual_seed(1005 + rank)
+    if workload == "dw":
+        w, b = synth.make_dw_weights(1002)
+        dw_w = torch.from_numpy(w).to(torch.bfloat16).to(dev)
+        dw_b = torch.from_numpy(b).to(torch.bfloat16).to(dev)
+        xs = [torch.randn((c.B, c.T, I), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+        ys = [torch.empty_like(x) for x in xs]
+        layers = []
+    else:
+        layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8) for l in range(n_layers)]
+        xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+    lens_dev = [torch.from_numpy(c.lengths).to(dev) for c in chunks]
+    max_m = max(c.padded_frames for c in chunks)
+    ws_bytes = int(L.gsn_conv_module_workspace_bytes(1, max_m, D, I))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    h_buf = ws                                                         # [M, I] GLU output
+    t_off = ((max_m * I * 2 + 255) // 256) * 256
+    act = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]   # ping-pong buffers
+    act2 = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
+
+    g1_events = []
+
+    def layer_kernels(x, out, c, p, lens, record):
+        """The four kernels of one conv module (the same launches gsn_conv_module_* makes), with CUDA events
+        around the up_conv GEMM when `record`."""
+        M = c.padded_frames
+        hp = h_buf.data_ptr()
+        tp = h_buf.data_ptr() + t_off
+        _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
+                                        p.ln_eps, sp), "layernorm")
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        if int8:
+            _lib.check(L.gsn_gemm1_glu_i8w(tp, p.w1q_glu.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), hp,
+                                           M, D, 2 * I, sp), "gemm1")
+        else:
+            _lib.check(L.gsn_gemm1_glu_bf16(tp, p.w1_glu.data_ptr(), p.b1_glu.data_ptr(), hp, M, D, 2 * I, sp),
+                       "gemm1")
+        if record:
+            e1.record(stream)
+            g1_events.append((e0, e1, M))
+        _lib.check(L.gsn_dwconv_silu_bf16(hp, p.dw_w.data_ptr(), p.dw_b.data_ptr(), tp, c.B, I, c.T, 15,
+                                          c.T * I, 1, I, c.T * I, 1, I, lens.data_ptr(), sp), "dwconv")
+        if int8:
+            _lib.check(L.gsn_gemm2_residual_i8w(tp, p.w2q.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(), x.data_ptr(),
+                                                D, out.data_ptr(), D, M, I, D, sp), "gemm2")
+        else:
+            _lib.check(L.gsn_gemm2_residual_bf16(tp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
+                                                 out.data_ptr(), D, M, I, D, sp), "gemm2")
+
+    dw_events = []
+
+    def step(record=False):
+        n = 0
+        for ci, c in enumerate(chunks):
+            if workload == "dw":
+                x, y = xs[ci], ys[ci]
+                if record:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                _lib.check(L.gsn_dwconv_silu_bf16(x.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), y.data_ptr(),
+                                                  c.B, I, c.T, 15, c.T * I, 1, I, c.T * I, 1, I, 0, sp), "dwconv")
+                if record:
+                    e1.record(stream)
+                    dw_events.append((e0, e1, c.padded_frames))
+                n += 1
+                continue
+            src = xs[ci]
+            for li, p in enumerate(layers):
+                dst = act[ci] if li % 2 == 0 else act2[ci]
+                layer_kernels(src, dst, c, p, lens_dev[ci], record)
+                src = dst
+                n += 4
+        return n
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    status = _lib.device_status(sp)
+    if status:
+        raise RuntimeError(f"kernel status word {status:#x} after warm-up")
+
+    launches = 0
+    with ClockSampler(dev.index) as clocks:
+        barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for _ in range(args.steps):
+            launches += step(record=True)
+        t_end.record(stream)
+        barrier()
+    ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        tot = torch.tensor([valid_frames, padded_frames], device=dev, dtype=torch.float64)
+        dist.all_reduce(tot)
+        valid_all, padded_all = float(tot[0].item()), float(tot[1].item())
+    else:
+        valid_all, padded_all = float(valid_frames), float(padded_frames)
+    ms_per_step = ms / args.steps
+    value = valid_all * args.steps / (ms / 1e3)
+
+    peaks = _peaks()
+    if workload == "dw":
+        dur = sum(a.elapsed_time(b) for a, b, _ in dw_events) / len(dw_events)
+        frames = sum(m for _, _, m in dw_events) / len(dw_events)
+        achieved = frames * DW_BYTES_PER_FRAME / (dur / 1e3) / 1e9
+        roof = {"kernel": "dwconv_cl_kernel", "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
+                "peak_source": f"hbm_gbs of {peaks['source']}"}
+    else:
+        dur = sum(a.elapsed_time(b) for a, b, _ in g1_events) / len(g1_events)
+        frames = sum(m for _, _, m in g1_events) / len(g1_events)
+        achieved = frames * GEMM1_FLOP_PER_FRAME / (dur / 1e3) / 1e12
+        pk = peaks["bf16_tflops_sustained"]
+        roof = {"kernel": "gemm_kernel<GLU> (up_conv 1024->4096 + GLU)", "bound": "tensor", "achieved": achieved,
+                "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk, "traffic": None, "per_launch_ms": dur,
+                "algorithmic_flop_per_frame": GEMM1_FLOP_PER_FRAME,
+                "peak_source": f"bf16_tflops_sustained of {peaks['source']}"}
+
+    # ---- end to end through the public op with pinned host buffers
+    e2e = None
+    if workload != "dw" and not args.no_e2e:
+        e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r, cores, desc = cpu_oracle_rate(workload, args.cpu_seconds)
+        cpu = {"value": r, "unit": "frames/s", "cores": cores, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if not int8 else "bf16 x int8-weight", "data": "synthetic",
+            "config": dict(_config(args, world), padded_frames_per_s=padded_all * args.steps / (ms / 1e3)),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
+    """Same work through the public op (torch.ops.granite.conv_module per layer) with each chunk's input copied
+    from pinned host memory and its output copied back inside the timed region."""
+    import torch
+
+    from granite_conv_b200 import ConvModuleStack
+    stack = ConvModuleStack(layers, int8=int8)
+    g = torch.Generator().manual_seed(4242)
+    hx = [torch.randn((c.B, c.T, D), generator=g).to(torch.bfloat16).pin_memory() for c in chunks]
+    hl = [torch.from_numpy(c.lengths).pin_memory() for c in chunks]
+    ho = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16).pin_memory() for c in chunks]
+    h2d = sum(x.numel() * 2 + l.numel() * 4 for x, l in zip(hx, hl))
+    d2h = sum(o.numel() * 2 for o in ho)
+
+    def step():
+        for ci in range(len(chunks)):
+            x = hx[ci].to(dev, non_blocking=True)
+            lens = hl[ci].to(dev, non_blocking=True)
+            y = stack(x, lens)
+            ho[ci].copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    valid = sum(c.valid_frames for c in chunks) * len(layers)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        v = torch.tensor([float(valid)], device=dev, dtype=torch.float64)
+        dist.all_reduce(v)
+        valid = float(v.item())
+    return {"value": valid * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
+            "path": "torch.ops.granite.conv_module per layer, pinned host in/out"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw"], default="stack")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("note: --warmup raised to 3", file=sys.stderr)
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

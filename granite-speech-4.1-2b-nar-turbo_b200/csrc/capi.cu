@@ -1,0 +1,346 @@
+// extern "C" entry points of libgsn_conv.so (declared in include/gsn_conv.h): argument checks, TMA descriptor
+// encoding through the driver entry point, and the composite conv-module launch sequence.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "gsn_conv.h"
+#include "gsn_kernels.cuh"
+#include "gsn_ptx.cuh"
+
+#define GSN_VERSION 10000
+
+namespace gsn {
+
+namespace capi_impl {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = '\0';
+  return GSN_OK;
+}
+
+int cuda_fail(int rc, const char* what) {
+  return fail(GSN_ERR_CUDA, "%s: CUDA error %d (%s)", what, rc, cudaGetErrorString((cudaError_t)rc));
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+
+__global__ void wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // nothing ever arrives on `bar`: the bounded wait must give up, record the status and return
+  mbar_wait_bounded(&bar, 0, &abort_flag, kStatusTimeoutSelftest, limit_ns);
+  __syncthreads();
+}
+
+}  // namespace capi_impl
+using namespace capi_impl;
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(GSN_ERR_DRIVER, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GSN_ERR_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", (int)r);
+  return 0;
+}
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+  if (dev < kMaxDevices) {
+    int c = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int c = 0;
+  if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+  if (dev < kMaxDevices) g_sm_count[dev].store(c, std::memory_order_relaxed);
+  return c;
+}
+
+int launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace gsn
+
+using namespace gsn;
+
+namespace {
+
+// a launcher status is either a GSN_* code already described in g_err, or a raw cudaError_t
+int finish(int rc, const char* what) {
+  if (rc == 0) return ok();
+  if (rc == GSN_ERR_DRIVER) return rc;
+  return cuda_fail(rc, what);
+}
+
+// returns -1 for a valid empty problem (nothing to launch), 0 to launch, or a GSN_ERR_* code
+int check_dw(const void* x, const void* w, const void* b, const void* y, int B, int C, int T, int K) {
+  if (B < 0 || C < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "dwconv: negative size B=%d C=%d T=%d", B, C, T);
+  if (K != 15) return fail(GSN_ERR_UNSUPPORTED, "dwconv: kernel size %d, only 15 is supported", K);
+  if ((int64_t)B * C * T == 0) return -1;
+  if (!x || !w || !b || !y) return fail(GSN_ERR_INVALID_ARG, "dwconv: null pointer");
+  if (!aligned(x, 2) || !aligned(y, 2) || !aligned(w, 2) || !aligned(b, 2))
+    return fail(GSN_ERR_UNSUPPORTED, "dwconv: bf16 pointers must be 2-byte aligned");
+  return 0;
+}
+
+// returns -1 for a valid empty problem (M == 0), 0 to launch, or a GSN_ERR_* code
+int check_gemm(const char* name, const void* a, const void* w, const float* bias, const void* out, int M, int K,
+               int N) {
+  if (M < 0 || K <= 0 || N <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: bad sizes M=%d K=%d N=%d", name, M, K, N);
+  if (K % 64 != 0) return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d must be a multiple of 64", name, K);
+  if (N % 256 != 0) return fail(GSN_ERR_UNSUPPORTED, "%s: N=%d must be a multiple of 256", name, N);
+  if (M == 0) return -1;
+  if (!a || !w || !bias || !out) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned(a, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(bias, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: pointers must be 16-byte aligned", name);
+  return 0;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+bool ln_dim_ok(int D) { return D == 256 || D == 512 || D == 1024 || D == 2048; }
+
+}  // namespace
+
+extern "C" {
+
+int gsn_version(void) { return GSN_VERSION; }
+
+const char* gsn_last_error_string(void) { return g_err; }
+
+int gsn_dwconv_silu_bf16(const void* x, const void* weight, const void* bias, void* y, int B, int C, int T, int K,
+                         int64_t sxB, int64_t sxC, int64_t sxT, int64_t syB, int64_t syC, int64_t syT,
+                         const int32_t* lengths, gsn_stream_t stream) {
+  if (int rc = check_dw(x, weight, bias, y, B, C, T, K)) return rc < 0 ? ok() : rc;
+  DwArgs a{(const __nv_bfloat16*)x, (const __nv_bfloat16*)weight, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y,
+           lengths, sxB, sxC, sxT, syB, syC, syT, B, C, T, 0};
+  return finish(launch_dwconv(a, (cudaStream_t)stream), "gsn_dwconv_silu_bf16");
+}
+
+int gsn_dwconv_silu_glu_bf16(const void* x2, const void* weight, const void* bias, void* y, int B, int C, int T,
+                             int K, int64_t sxB, int64_t sxC, int64_t sxT, int64_t syB, int64_t syC, int64_t syT,
+                             const int32_t* lengths, gsn_stream_t stream) {
+  if (int rc = check_dw(x2, weight, bias, y, B, C, T, K)) return rc < 0 ? ok() : rc;
+  DwArgs a{(const __nv_bfloat16*)x2, (const __nv_bfloat16*)weight, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y,
+           lengths, sxB, sxC, sxT, syB, syC, syT, B, C, T, 1};
+  return finish(launch_dwconv(a, (cudaStream_t)stream), "gsn_dwconv_silu_glu_bf16");
+}
+
+int gsn_layernorm_bf16(const void* x, int64_t ld_x, const void* gamma, const void* beta, void* y, int64_t ld_y,
+                       int M, int D, float eps, gsn_stream_t stream) {
+  if (M < 0) return fail(GSN_ERR_INVALID_ARG, "layernorm: M=%d", M);
+  if (!ln_dim_ok(D)) return fail(GSN_ERR_UNSUPPORTED, "layernorm: D=%d not in {256,512,1024,2048}", D);
+  if (M == 0) return ok();
+  if (!x || !gamma || !beta || !y) return fail(GSN_ERR_INVALID_ARG, "layernorm: null pointer");
+  if (ld_x % 8 || ld_y % 8 || ld_x < D || ld_y < D || !aligned(x, 16) || !aligned(y, 16) || !aligned(gamma, 16) ||
+      !aligned(beta, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "layernorm: rows must be 16-byte aligned (ld %% 8 == 0)");
+  return finish(launch_layernorm((const __nv_bfloat16*)x, ld_x, (const __nv_bfloat16*)gamma,
+                                 (const __nv_bfloat16*)beta, (__nv_bfloat16*)y, ld_y, M, D, eps, (cudaStream_t)stream),
+                "gsn_layernorm_bf16");
+}
+
+static int gemm1(const void* a, const void* w, const float* scale, const float* b, void* h, int M, int K, int N,
+                 int i8, gsn_stream_t stream, const char* name) {
+  if (int rc = check_gemm(name, a, w, b, h, M, K, N)) return rc < 0 ? ok() : rc;
+  if (i8 && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
+  GemmArgs g{(const __nv_bfloat16*)a, w, b, i8 ? scale : nullptr, nullptr, (__nv_bfloat16*)h, (int64_t)(N / 2), 0,
+             M, N, K, i8};
+  return finish(launch_gemm(g, kEpiGlu, (cudaStream_t)stream), name);
+}
+
+static int gemm2(const void* d, const void* w, const float* scale, const float* b, const void* res, int64_t ld_res,
+                 void* out, int64_t ld_out, int M, int K, int N, int i8, gsn_stream_t stream, const char* name) {
+  if (int rc = check_gemm(name, d, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
+  if (res && !aligned(res, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: residual must be 16-byte aligned", name);
+  if (i8 && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
+  if (ld_out % 8 || ld_out < N || (res && (ld_res % 8 || ld_res < N)))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: row strides must be >= N and multiples of 8", name);
+  GemmArgs g{(const __nv_bfloat16*)d, w, b, i8 ? scale : nullptr, (const __nv_bfloat16*)res, (__nv_bfloat16*)out,
+             ld_out, ld_res, M, N, K, i8};
+  return finish(launch_gemm(g, kEpiResidual, (cudaStream_t)stream), name);
+}
+
+int gsn_gemm1_glu_bf16(const void* a, const void* w1_glu, const float* b1_glu, void* h, int M, int K, int N,
+                       gsn_stream_t stream) {
+  return gemm1(a, w1_glu, nullptr, b1_glu, h, M, K, N, 0, stream, "gsn_gemm1_glu_bf16");
+}
+
+int gsn_gemm1_glu_i8w(const void* a, const void* w1q_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
+                      int K, int N, gsn_stream_t stream) {
+  return gemm1(a, w1q_glu, s1_glu, b1_glu, h, M, K, N, 1, stream, "gsn_gemm1_glu_i8w");
+}
+
+int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, const void* residual, int64_t ld_res,
+                            void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream) {
+  return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, 0, stream, "gsn_gemm2_residual_bf16");
+}
+
+int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, const float* b2, const void* residual,
+                           int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream) {
+  return gemm2(d, w2q, s2, b2, residual, ld_res, out, ld_out, M, K, N, 1, stream, "gsn_gemm2_residual_i8w");
+}
+
+size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
+  if (B <= 0 || T <= 0 || D <= 0 || inner <= 0) return 0;
+  const size_t M = (size_t)B * (size_t)T;
+  const size_t wide = (size_t)(inner > D ? inner : D);
+  return align256(M * (size_t)inner * 2) + align256(M * wide * 2);
+}
+
+static int conv_module(const void* x, const void* ln_w, const void* ln_b, const void* w1, const float* s1,
+                       const float* b1, const void* dw_w, const void* dw_b, const void* w2, const float* s2,
+                       const float* b2, const int32_t* lengths, int add_residual, void* out, int B, int T, int D,
+                       int inner, float eps, void* ws, size_t ws_bytes, int i8, gsn_stream_t stream,
+                       const char* name) {
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if ((int64_t)B * T == 0) return ok();
+  if (!x || !ln_w || !ln_b || !w1 || !b1 || !dw_w || !dw_b || !w2 || !b2 || !out)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (i8 && (!s1 || !s2)) return fail(GSN_ERR_INVALID_ARG, "%s: null scale pointer", name);
+  if (!ln_dim_ok(D) || (2 * inner) % 256 != 0 || inner % 128 != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d inner=%d (D in {256..2048}, inner %% 128 == 0)", name, D, inner);
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  const int M = B * T;
+  if (M == 0) return ok();
+  const size_t need = gsn_conv_module_workspace_bytes(B, T, D, inner);
+  if (!ws || ws_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, ws_bytes, need);
+  if (!aligned(ws, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
+  if (!aligned(x, 16) || !aligned(out, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: x/out must be 16-byte aligned", name);
+
+  // workspace: h = GLU output [M, inner]; t = LayerNorm output [M, D], later reused for the depthwise output
+  __nv_bfloat16* h = (__nv_bfloat16*)ws;
+  __nv_bfloat16* t = (__nv_bfloat16*)((char*)ws + align256((size_t)M * inner * 2));
+  const cudaStream_t st = (cudaStream_t)stream;
+
+  int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
+                            M, D, eps, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, i8};
+  rc = launch_gemm(g1, kEpiGlu, st);
+  if (rc) return finish(rc, name);
+  DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
+            (int64_t)T * inner, 1, inner, (int64_t)T * inner, 1, inner, B, inner, T, 0};
+  rc = launch_dwconv(dw, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g2{t, w2, b2, i8 ? s2 : nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr, (__nv_bfloat16*)out,
+              D, D, M, D, inner, i8};
+  rc = launch_gemm(g2, kEpiResidual, st);
+  return finish(rc, name);
+}
+
+int gsn_conv_module_bf16(const void* x, const void* ln_w, const void* ln_b, const void* w1_glu,
+                         const float* b1_glu, const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                         const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
+                         float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  return conv_module(x, ln_w, ln_b, w1_glu, nullptr, b1_glu, dw_w, dw_b, w2, nullptr, b2, lengths, add_residual, out,
+                     B, T, D, inner, ln_eps, workspace, workspace_bytes, 0, stream, "gsn_conv_module_bf16");
+}
+
+int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const void* w1q_glu,
+                        const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,
+                        const void* w2q, const float* s2, const float* b2, const int32_t* lengths,
+                        int add_residual, void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
+                        size_t workspace_bytes, gsn_stream_t stream) {
+  return conv_module(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, add_residual, out, B,
+                     T, D, inner, ln_eps, workspace, workspace_bytes, 1, stream, "gsn_conv_module_i8w");
+}
+
+int gsn_interleave_glu_rows(const void* src, void* dst, int rows, int64_t row_bytes, gsn_stream_t stream) {
+  if (!src || !dst) return fail(GSN_ERR_INVALID_ARG, "interleave: null pointer");
+  if (rows <= 0 || rows % 256 != 0 || row_bytes <= 0)
+    return fail(GSN_ERR_UNSUPPORTED, "interleave: rows=%d must be a positive multiple of 256", rows);
+  const int half = rows / 2;
+  const size_t blk = (size_t)128 * (size_t)row_bytes;
+  for (int j = 0; j < rows / 256; ++j) {
+    const char* s = (const char*)src;
+    char* d = (char*)dst + (size_t)j * 2 * blk;
+    cudaError_t e = cudaMemcpyAsync(d, s + (size_t)j * blk, blk, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(d + blk, s + ((size_t)half + (size_t)j * 128) * (size_t)row_bytes, blk,
+                          cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail((int)e, "gsn_interleave_glu_rows");
+  }
+  return ok();
+}
+
+int gsn_device_status(int* status, int clear, gsn_stream_t stream) {
+  if (!status) return fail(GSN_ERR_INVALID_ARG, "device_status: null pointer");
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail((int)e, "gsn_device_status (stream sync)");
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, gsn::g_device_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail((int)e, "gsn_device_status (read)");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(gsn::g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail((int)e, "gsn_device_status (clear)");
+  }
+  *status = v;
+  return ok();
+}
+
+int gsn_selftest_bounded_wait(uint64_t limit_ns, gsn_stream_t stream) {
+  if (limit_ns == 0 || limit_ns > 2000000000ull)
+    return fail(GSN_ERR_INVALID_ARG, "selftest: limit_ns must be in (0, 2e9]");
+  return finish(launch_wait_selftest(limit_ns, (cudaStream_t)stream), "gsn_selftest_bounded_wait");
+}
+
+}  // extern "C"

@@ -1,0 +1,398 @@
+// Pointwise (1x1) convolutions of the Conformer conv module as tcgen05 GEMMs on sm_100a.
+//
+//   up_conv   (models/granite_speech_nar/conformer.py:165,177) + GLU (:166,:181)  -> kEpiGlu
+//   down_conv (conformer.py:170,187) + the block's residual add (conformer.py:207)  -> kEpiResidual
+//
+// Layout: A = activations [M, K] bf16 row-major (M = B*T frames, channels-last), W = weights [N, K] (the Conv1d
+// weight [N, K, 1] as stored), both K-major, so D = A * W^T accumulates in TMEM in fp32.
+//
+// Kernel shape: persistent, one CTA per SM (the shared-memory ring is sized so only one CTA fits, which also
+// guarantees the 512 TMEM columns are free), warp-specialised:
+//   warp 0      TMA producer: A tile 128x64 and W tile 256x64 per stage, 128-byte swizzle, 4-stage ring
+//   warp 1      TMEM allocator + single-thread UMMA issuer (M=128, N=256, K=16 per instruction)
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator, bias (+scale) (+GLU | +residual), bf16 stores
+//   warps 6-9   (int8 weights only) dequantise the staged int8 W tile into the swizzled bf16 layout
+// The accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of tile i overlaps the
+// main loop of tile i+1.  Tiles are visited N-fastest so the 16 (or 4) CTAs sharing an A row-block run at
+// the same time and read it from L2.
+#include "gsn_kernels.cuh"
+#include "gsn_ptx.cuh"
+
+namespace gsn {
+
+namespace gemm_impl {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+constexpr int B_BYTES = BN * BK * 2;      // 32 KB (bf16, swizzled)
+constexpr int B8_BYTES = BN * BK;         // 16 KB (int8 staging)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
+
+template <bool W_I8>
+struct Cfg {
+  static constexpr int STAGES = W_I8 ? 3 : 4;
+  static constexpr int THREADS = W_I8 ? 320 : 192;
+};
+
+template <bool W_I8>
+struct __align__(1024) Smem {
+  uint8_t a[Cfg<W_I8>::STAGES][A_BYTES];
+  uint8_t b[Cfg<W_I8>::STAGES][B_BYTES];
+  uint8_t b8[W_I8 ? Cfg<W_I8>::STAGES : 1][W_I8 ? B8_BYTES : 16];
+  uint64_t full[Cfg<W_I8>::STAGES];
+  uint64_t full_b[Cfg<W_I8>::STAGES];     // int8: converted W tile ready
+  uint64_t empty[Cfg<W_I8>::STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct KParams {
+  const float* bias;
+  const float* col_scale;
+  const __nv_bfloat16* residual;
+  __nv_bfloat16* out;
+  int64_t ld_out, ld_res;
+  int M, N, K;
+};
+
+__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
+  uint4 lo, hi;
+  lo.x = pack_bf16x2(v[0], v[1]);
+  lo.y = pack_bf16x2(v[2], v[3]);
+  lo.z = pack_bf16x2(v[4], v[5]);
+  lo.w = pack_bf16x2(v[6], v[7]);
+  hi.x = pack_bf16x2(v[8], v[9]);
+  hi.y = pack_bf16x2(v[10], v[11]);
+  hi.z = pack_bf16x2(v[12], v[13]);
+  hi.w = pack_bf16x2(v[14], v[15]);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  d[0] = lo;
+  d[1] = hi;
+}
+
+// Four signed int8 (one 32-bit word) -> two bf16x2 words, exactly.  Each byte is biased to unsigned
+// (v + 128), placed in the low mantissa bits of the fp32 2^23, and the bias 2^23 + 128 is subtracted; every
+// |v| <= 127 is exact in bf16.
+__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
+  lo = pack_bf16x2(f0, f1);
+  hi = pack_bf16x2(f2, f3);
+}
+
+template <int EPI, bool W_I8>
+__global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, KParams p) {
+  constexpr int STAGES = Cfg<W_I8>::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  Smem<W_I8>& s =
+      *reinterpret_cast<Smem<W_I8>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = p.N / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.full_b[i], 4);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 4);
+    }
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    const uint64_t pol_w = l2_policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int m_blk = tile / num_n;
+      const int n_blk = tile - m_blk * num_n;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        bool got = mbar_wait_bounded(&s.empty[stage], phase ^ 1u, abort_flag, kStatusTimeoutProducer);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          if (W_I8) {
+            mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B8_BYTES);
+            tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, m_blk * BM);
+            tma_load_2d_hint(s.b8[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
+          } else {
+            mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES);
+            tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, m_blk * BM);
+            tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
+          }
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      // Unwinding after a timeout: let the copies still in flight land before the CTA releases its shared
+      // memory.  Only the last STAGES loads can be outstanding; wait for each with a short bound.
+      for (int back = 1; back <= STAGES && back <= issued; ++back) {
+        const int idx = issued - back;
+        mbar_wait_bounded(&s.full[idx % STAGES], (uint32_t)((idx / STAGES) & 1), nullptr, kStatusTimeoutProducer,
+                          100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- UMMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+      bool got = mbar_wait_bounded(&s.tempty[acc], use_par ^ 1u, abort_flag, kStatusTimeoutMma);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        bool ready = mbar_wait_bounded(&s.full[stage], phase, abort_flag, kStatusTimeoutMma);
+        if (W_I8 && ready) ready = mbar_wait_bounded(&s.full_b[stage], phase, abort_flag, kStatusTimeoutMma);
+        ready = __shfl_sync(0xffffffffu, ready, 0);
+        if (!ready) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(s.a[stage]));
+          const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.b[stage]));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 bytes per K=16 slice inside the 128-byte swizzled row: +2 in the (addr >> 4) field
+            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC,
+                     (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&s.empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&s.tfull[acc]);
+      __syncwarp();
+    }
+    // every MMA issued by this CTA has completed once mma_done flips (bounded: also the unwind path)
+    if (lane == 0) umma_commit(&s.mma_done);
+    __syncwarp();
+    mbar_wait_bounded(&s.mma_done, 0, nullptr, kStatusTimeoutMma, 100000000ull);
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // a warp may only read its own 32-lane quarter of TMEM
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int m_blk = tile / num_n;
+      const int n_blk = tile - m_blk * num_n;
+      const int acc = local & 1;
+      const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+      bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      tc_fence_after();
+      const int row = m_blk * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+
+      if (EPI == kEpiGlu) {
+        // accumulator columns [0,128) = value channels, [128,256) = their gate channels
+        const int nb = n_blk * BN;
+        __nv_bfloat16* orow = p.out + (int64_t)row * p.ld_out + (int64_t)n_blk * (BN / 2);
+#pragma unroll 1
+        for (int j = 0; j < BN / 2; j += 16) {
+          uint32_t va[16], vg[16];
+          tmem_ld16(t_row + (uint32_t)j, va);
+          tmem_ld16(t_row + (uint32_t)(BN / 2 + j), vg);
+          tmem_wait_ld();
+          float o[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            float a = __uint_as_float(va[c]);
+            float g = __uint_as_float(vg[c]);
+            if (W_I8) {
+              a *= __ldg(p.col_scale + nb + j + c);
+              g *= __ldg(p.col_scale + nb + BN / 2 + j + c);
+            }
+            a += __ldg(p.bias + nb + j + c);
+            g += __ldg(p.bias + nb + BN / 2 + j + c);
+            o[c] = a * sigmoid_fast(g);
+          }
+          if (row_ok) store_bf16x16(orow + j, o);
+        }
+      } else {
+        const int nb = n_blk * BN;
+        __nv_bfloat16* orow = p.out + (int64_t)row * p.ld_out + nb;
+        const __nv_bfloat16* rrow = p.residual + (p.residual ? (int64_t)row * p.ld_res + nb : 0);
+#pragma unroll 1
+        for (int j = 0; j < BN; j += 16) {
+          uint32_t v[16];
+          tmem_ld16(t_row + (uint32_t)j, v);
+          uint4 r0 = make_uint4(0, 0, 0, 0), r1 = make_uint4(0, 0, 0, 0);
+          if (row_ok && p.residual != nullptr) {
+            r0 = __ldg(reinterpret_cast<const uint4*>(rrow + j));
+            r1 = __ldg(reinterpret_cast<const uint4*>(rrow + j) + 1);
+          }
+          tmem_wait_ld();
+          const uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+          float o[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            float a = __uint_as_float(v[c]);
+            if (W_I8) a *= __ldg(p.col_scale + nb + j + c);
+            a += __ldg(p.bias + nb + j + c);
+            const float res = (c & 1) ? bf16hi_to_f32(rr[c >> 1]) : bf16lo_to_f32(rr[c >> 1]);
+            o[c] = a + res;
+          }
+          if (row_ok) store_bf16x16(orow + j, o);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.tempty[acc]);
+    }
+  } else if (W_I8) {
+    // ---------------------------------------------------------------- int8 -> bf16 W converter (warps 6..9)
+    const int ct = threadIdx.x - 192;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        bool got = mbar_wait_bounded(&s.full[stage], phase, abort_flag, kStatusTimeoutMma);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = s.b8[stage];
+        uint8_t* dst = s.b[stage];
+#pragma unroll 4
+        for (int it = 0; it < (BN * 8) / 128; ++it) {
+          const int task = it * 128 + ct;
+          const int n = task >> 3;      // W row inside the tile
+          const int c = task & 7;       // 8-element chunk along K
+          const uint2 w8 = *reinterpret_cast<const uint2*>(src + n * BK + c * 8);
+          uint4 o;
+          i8x4_to_bf16x4(w8.x, o.x, o.y);
+          i8x4_to_bf16x4(w8.y, o.z, o.w);
+          // 128-byte swizzle: 16-byte chunk c of row n lands at chunk (c ^ (n % 8))
+          *reinterpret_cast<uint4*>(dst + n * 128 + ((c ^ (n & 7)) << 4)) = o;
+        }
+        fence_proxy_async_smem();   // generic-proxy writes -> visible to the tensor core (async proxy)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.full_b[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int EPI, bool W_I8>
+int launch_impl(const GemmArgs& a, cudaStream_t stream) {
+  CUtensorMap tmA, tmW;
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
+    const uint64_t strides[1] = {(uint64_t)a.K * 2};
+    const uint32_t box[2] = {BK, BM};
+    int rc = encode_tmap(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
+    const uint64_t strides[1] = {(uint64_t)a.K * (W_I8 ? 1 : 2)};
+    const uint32_t box[2] = {BK, BN};
+    int rc = encode_tmap(&tmW, W_I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w,
+                         dims, strides, box, W_I8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  KParams p;
+  p.bias = a.bias;
+  p.col_scale = a.col_scale;
+  p.residual = a.residual;
+  p.out = a.out;
+  p.ld_out = a.ld_out;
+  p.ld_res = a.ld_res;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  const int smem = (int)sizeof(Smem<W_I8>) + 1024;
+  auto kern = gemm_kernel<EPI, W_I8>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  const int sms = device_sm_count();
+  const int grid = tiles < sms ? tiles : sms;
+  if (grid <= 0) return 0;
+  kern<<<grid, Cfg<W_I8>::THREADS, smem, stream>>>(tmA, tmW, p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace gemm_impl
+using namespace gemm_impl;
+
+int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
+  if (epilogue == kEpiGlu)
+    return a.w_int8 ? launch_impl<kEpiGlu, true>(a, stream) : launch_impl<kEpiGlu, false>(a, stream);
+  return a.w_int8 ? launch_impl<kEpiResidual, true>(a, stream) : launch_impl<kEpiResidual, false>(a, stream);
+}
+
+}  // namespace gsn

@@ -1,0 +1,6 @@
+// Single translation unit of libgsn_conv.so: the device status word (gsn_ptx.cuh) must have exactly one
+// definition visible to every kernel without relocatable device code.
+#include "layernorm.cu"
+#include "dwconv.cu"
+#include "gemm_sm100.cu"
+#include "capi.cu"

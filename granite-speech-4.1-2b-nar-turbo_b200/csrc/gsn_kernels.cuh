@@ -1,0 +1,64 @@
+// Host-side launchers of the conv-module kernels (implemented in gemm_sm100.cu, dwconv.cu, layernorm.cu).
+// All return a cudaError_t-style status from the launch; argument validation happens in capi.cu.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gsn {
+
+// ---- tensor maps (capi.cu) --------------------------------------------------------------------------------
+// Encodes a tiled TMA descriptor.  dims/strides follow cuTensorMapEncodeTiled: dims[0] is the innermost
+// (contiguous) extent, strides[i] is the byte stride of dims[i + 1].
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
+int device_sm_count();
+
+// ---- GEMMs (gemm_sm100.cu) --------------------------------------------------------------------------------
+// out = epilogue(A[M,K] (bf16, row-major) x W[N,K]^T)
+//   GLU:      W rows are interleaved per 256-row block as [128 value rows | 128 gate rows]; out is [M, N/2]:
+//             out[m, 128*j + c] = (acc[m, 256*j + c] * s + b) * sigmoid(acc[m, 256*j + 128 + c] * s + b)
+//   RESIDUAL: out[m, n] = acc[m, n] * s + b[n] (+ residual[m, n] when residual is not null)
+// `col_scale` (per W row) is null for bf16 weights; with int8 weights W is int8 and dequantised in shared memory.
+struct GemmArgs {
+  const __nv_bfloat16* a;
+  const void* w;                 // bf16 [N, K] or int8 [N, K]
+  const float* bias;             // [N], same row order as W
+  const float* col_scale;        // [N] or null
+  const __nv_bfloat16* residual; // RESIDUAL only: [M, N], row stride ld_res, or null
+  __nv_bfloat16* out;
+  int64_t ld_out, ld_res;
+  int M, N, K;
+  int w_int8;
+};
+
+enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1 };
+
+int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
+
+// ---- depthwise conv k=15 + bias + SiLU (dwconv.cu) -------------------------------------------------------
+// x: (B, C, T) logical, element strides sxB, sxC, sxT; y likewise.  GLU: x holds 2C channels (value | gate).
+struct DwArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w;        // (C, K) contiguous, K = 15
+  const __nv_bfloat16* bias;     // (C,)
+  __nv_bfloat16* y;
+  const int* lengths;            // (B,) or null
+  int64_t sxB, sxC, sxT, syB, syC, syT;
+  int B, C, T;
+  int glu;
+};
+
+int launch_dwconv(const DwArgs& args, cudaStream_t stream);
+
+// ---- LayerNorm over the last dim (layernorm.cu) -------------------------------------------------------------
+int launch_layernorm(const __nv_bfloat16* x, int64_t ld_x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
+                     __nv_bfloat16* y, int64_t ld_y, int M, int D, float eps, cudaStream_t stream);
+
+// ---- self-test of the bounded wait (capi.cu) ----------------------------------------------------------------
+int launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);
+
+}  // namespace gsn

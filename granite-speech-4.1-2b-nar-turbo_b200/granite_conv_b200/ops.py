@@ -1,0 +1,231 @@
+"""``torch.library`` custom ops over libgsn_conv.so.
+
+Same names and signatures as the reference's ops (``script/models/granite_speech_nar/conv_kernel.py:41-56``):
+
+* ``granite::dwconv_silu(Tensor x, Tensor weight, Tensor bias) -> Tensor``
+* ``granite::dwconv_silu_glu(Tensor x2, Tensor weight, Tensor bias) -> Tensor``
+
+plus the ops of the whole module (new):
+
+* ``granite::dwconv_silu_masked(x, weight, bias, lengths) -> Tensor``  (lengths int32 [B])
+* ``granite::conv_module(x, ln_w, ln_b, w1_glu, b1_glu, dw_w, dw_b, w2, b2, lengths?, ln_eps, add_residual)``
+* ``granite::conv_module_i8w(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths?, ln_eps,
+  add_residual)``
+
+All are ``mutates_args=()``, CUDA-only, launch on ``torch.cuda.current_stream()`` (as ``jit.py:180-181``) and
+have ``register_fake`` implementations whose strides equal the real outputs', so ``torch.compile(fullgraph=True)``
+sees one opaque node per call.  Inputs in (B, C, T) may be channels-first contiguous (the reference layout) or a
+channels-last view (``x.transpose(1, 2)`` of a contiguous [B, T, C]); the output keeps the input's layout.
+There is no fallback: a CPU tensor or a failed launch raises.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+KERNEL_SIZE = 15
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(name: str, *ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name}: every tensor must be on a CUDA device (got {t.device}); "
+                               "the conv-module kernels have no CPU path")
+
+
+def _is_channels_last_dense(x: torch.Tensor) -> bool:
+    B, C, T = x.shape
+    return x.stride(1) == 1 and x.stride(2) == C and (B == 1 or x.stride(0) == C * T)
+
+
+def _dw_out(x: torch.Tensor, c_out: int) -> torch.Tensor:
+    """Output of the depthwise ops: channels-last if the input is a dense channels-last view, else contiguous."""
+    B, _, T = x.shape
+    if _is_channels_last_dense(x) and x.shape[1] >= 1:
+        return torch.empty_strided((B, c_out, T), (T * c_out, 1, c_out), dtype=x.dtype, device=x.device)
+    return torch.empty((B, c_out, T), dtype=x.dtype, device=x.device)
+
+
+def _prep_dw_input(x: torch.Tensor) -> torch.Tensor:
+    if _is_channels_last_dense(x) or x.is_contiguous():
+        return x
+    return x.contiguous()
+
+
+def _dw_call(name: str, entry: str, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, c_out: int,
+             lengths: Optional[torch.Tensor]) -> torch.Tensor:
+    _require_cuda(name, x, weight, bias, lengths)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or bias.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: bf16 tensors required (x {x.dtype}, weight {weight.dtype}, bias {bias.dtype})")
+    if weight.shape[-1] != KERNEL_SIZE or weight.numel() != c_out * KERNEL_SIZE:
+        raise RuntimeError(f"{name}: weight must be (C, 1, 15), got {tuple(weight.shape)}")
+    x = _prep_dw_input(x)
+    w = weight.contiguous()
+    b = bias.contiguous()
+    if lengths is not None:
+        lengths = lengths.to(torch.int32).contiguous()
+    y = _dw_out(x, c_out)
+    B, _, T = x.shape
+    _lib.call(entry, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), B, c_out, T, KERNEL_SIZE,
+              x.stride(0), x.stride(1), x.stride(2), y.stride(0), y.stride(1), y.stride(2), _ptr(lengths),
+              _stream(x))
+    return y
+
+
+# ---------------------------------------------------------------------------------------------------------------
+@torch.library.custom_op("granite::dwconv_silu", mutates_args=(), device_types="cuda")
+def dwconv_silu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """silu(depthwise_conv_k15(x) + bias), x (B, C, T) bf16, weight (C, 1, 15), bias (C,)."""
+    return _dw_call("granite::dwconv_silu", "gsn_dwconv_silu_bf16", x, weight, bias, x.shape[1], None)
+
+
+@dwconv_silu.register_fake
+def _(x, weight, bias):
+    return _dw_out(x, x.shape[1])
+
+
+@torch.library.custom_op("granite::dwconv_silu_glu", mutates_args=(), device_types="cuda")
+def dwconv_silu_glu(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """silu(depthwise_conv_k15(glu(x2, dim=1)) + bias), x2 (B, 2C, T) -> (B, C, T)."""
+    return _dw_call("granite::dwconv_silu_glu", "gsn_dwconv_silu_glu_bf16", x2, weight, bias, x2.shape[1] // 2,
+                    None)
+
+
+@dwconv_silu_glu.register_fake
+def _(x2, weight, bias):
+    return _dw_out(x2, x2.shape[1] // 2)
+
+
+@torch.library.custom_op("granite::dwconv_silu_masked", mutates_args=(), device_types="cuda")
+def dwconv_silu_masked(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                       lengths: torch.Tensor) -> torch.Tensor:
+    """dwconv_silu with per-utterance lengths: frames t >= lengths[b] read as zero and are written as zero."""
+    return _dw_call("granite::dwconv_silu_masked", "gsn_dwconv_silu_bf16", x, weight, bias, x.shape[1], lengths)
+
+
+@dwconv_silu_masked.register_fake
+def _(x, weight, bias, lengths):
+    return _dw_out(x, x.shape[1])
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def _module_common(name: str, x: torch.Tensor, ln_w: torch.Tensor, dw_w: torch.Tensor,
+                   lengths: Optional[torch.Tensor]):
+    if x.dim() != 3 or x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: x must be bf16 [B, T, D], got {x.dtype} {tuple(x.shape)}")
+    B, T, D = x.shape
+    if ln_w.shape[0] != D:
+        raise RuntimeError(f"{name}: LayerNorm width {ln_w.shape[0]} != D {D}")
+    inner = dw_w.shape[0]
+    xc = x.contiguous()
+    lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    out = torch.empty_like(xc)
+    nbytes = int(_lib.lib().gsn_conv_module_workspace_bytes(B, T, D, inner)) if B * T > 0 else 0
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    return xc, lens, out, ws, nbytes, B, T, D, inner
+
+
+@torch.library.custom_op("granite::conv_module", mutates_args=(), device_types="cuda")
+def conv_module(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w1_glu: torch.Tensor,
+                b1_glu: torch.Tensor, dw_w: torch.Tensor, dw_b: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor,
+                lengths: Optional[torch.Tensor], ln_eps: float, add_residual: bool) -> torch.Tensor:
+    """ConformerConvModule.forward (+ the block's residual add when add_residual) on bf16 x [B, T, D]."""
+    name = "granite::conv_module"
+    _require_cuda(name, x, ln_w, ln_b, w1_glu, b1_glu, dw_w, dw_b, w2, b2, lengths)
+    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(name, x, ln_w, dw_w, lengths)
+    _lib.call("gsn_conv_module_bf16", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w1_glu.data_ptr(),
+              b1_glu.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), w2.data_ptr(), b2.data_ptr(), _ptr(lens),
+              1 if add_residual else 0, out.data_ptr(), B, T, D, inner, float(ln_eps), ws.data_ptr(), nbytes,
+              _stream(xc))
+    return out
+
+
+@conv_module.register_fake
+def _(x, ln_w, ln_b, w1_glu, b1_glu, dw_w, dw_b, w2, b2, lengths, ln_eps, add_residual):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+@torch.library.custom_op("granite::conv_module_i8w", mutates_args=(), device_types="cuda")
+def conv_module_i8w(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w1q_glu: torch.Tensor,
+                    s1_glu: torch.Tensor, b1_glu: torch.Tensor, dw_w: torch.Tensor, dw_b: torch.Tensor,
+                    w2q: torch.Tensor, s2: torch.Tensor, b2: torch.Tensor, lengths: Optional[torch.Tensor],
+                    ln_eps: float, add_residual: bool) -> torch.Tensor:
+    """conv_module with int8 per-output-channel weights on both pointwise GEMMs (bf16 activations, fp32
+    accumulate, the scale applied in the epilogue)."""
+    name = "granite::conv_module_i8w"
+    _require_cuda(name, x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths)
+    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(name, x, ln_w, dw_w, lengths)
+    _lib.call("gsn_conv_module_i8w", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w1q_glu.data_ptr(),
+              s1_glu.data_ptr(), b1_glu.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), w2q.data_ptr(), s2.data_ptr(),
+              b2.data_ptr(), _ptr(lens), 1 if add_residual else 0, out.data_ptr(), B, T, D, inner, float(ln_eps),
+              ws.data_ptr(), nbytes, _stream(xc))
+    return out
+
+
+@conv_module_i8w.register_fake
+def _(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, ln_eps, add_residual):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, add_residual: bool = True,
+                    int8: bool = False) -> torch.Tensor:
+    """Call the fused module op with a :class:`~granite_conv_b200.weights.PreparedConvModule`."""
+    if int8:
+        if not p.has_int8:
+            raise RuntimeError("run_conv_module(int8=True): weights were prepared without int8")
+        return torch.ops.granite.conv_module_i8w(x, p.ln_w, p.ln_b, p.w1q_glu, p.s1_glu, p.b1_glu, p.dw_w, p.dw_b,
+                                                 p.w2q, p.s2, p.b2, lengths, p.ln_eps, add_residual)
+    return torch.ops.granite.conv_module(x, p.ln_w, p.ln_b, p.w1_glu, p.b1_glu, p.dw_w, p.dw_b, p.w2, p.b2, lengths,
+                                         p.ln_eps, add_residual)
+
+
+# ---- single-kernel wrappers (tests, benchmarks) ---------------------------------------------------------------
+def layernorm(x2d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    _require_cuda("layernorm", x2d, w, b)
+    M, D = x2d.shape
+    y = torch.empty_like(x2d)
+    _lib.call("gsn_layernorm_bf16", x2d.data_ptr(), x2d.stride(0), w.data_ptr(), b.data_ptr(), y.data_ptr(),
+              y.stride(0), M, D, float(eps), _stream(x2d))
+    return y
+
+
+def gemm1_glu(a: torch.Tensor, w_glu: torch.Tensor, b_glu: torch.Tensor, scale_glu: Optional[torch.Tensor] = None):
+    _require_cuda("gemm1_glu", a, w_glu, b_glu, scale_glu)
+    M, K = a.shape
+    N = w_glu.shape[0]
+    h = torch.empty((M, N // 2), dtype=torch.bfloat16, device=a.device)
+    if scale_glu is None:
+        _lib.call("gsn_gemm1_glu_bf16", a.data_ptr(), w_glu.data_ptr(), b_glu.data_ptr(), h.data_ptr(), M, K, N,
+                  _stream(a))
+    else:
+        _lib.call("gsn_gemm1_glu_i8w", a.data_ptr(), w_glu.data_ptr(), scale_glu.data_ptr(), b_glu.data_ptr(),
+                  h.data_ptr(), M, K, N, _stream(a))
+    return h
+
+
+def gemm2_residual(d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, residual: Optional[torch.Tensor],
+                   scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _require_cuda("gemm2_residual", d, w, b, residual, scale)
+    M, K = d.shape
+    N = w.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=d.device)
+    ld_res = residual.stride(0) if residual is not None else 0
+    if scale is None:
+        _lib.call("gsn_gemm2_residual_bf16", d.data_ptr(), w.data_ptr(), b.data_ptr(), _ptr(residual), ld_res,
+                  out.data_ptr(), out.stride(0), M, K, N, _stream(d))
+    else:
+        _lib.call("gsn_gemm2_residual_i8w", d.data_ptr(), w.data_ptr(), scale.data_ptr(), b.data_ptr(),
+                  _ptr(residual), ld_res, out.data_ptr(), out.stride(0), M, K, N, _stream(d))
+    return out

@@ -1,0 +1,97 @@
+"""Seeded synthetic inputs for the Conformer conv module workloads.
+
+There is no dataset or checkpoint on the build machines, so every workload is generated from a fixed seed with
+numpy's PCG64 generator.  The shapes and distributions restate the workload definitions of the conv-module
+benchmark:
+
+* depthwise alone: bf16 ``[B=48, T=1024, C=2048]`` channels-last, folded weights ~N(0, 0.05), bias ~N(0, 0.02),
+  x ~N(0, 1), every frame valid;
+* one module: D=1024, inner 2048 (``EncoderConfig.hidden_dim`` x ``conv_expansion_factor``,
+  ``models/granite_speech_nar/config.py:20,30``), depthwise k=15 (``config.py:29``); pointwise weights and biases
+  ~N(0, 0.02), depthwise weight ~N(0, 0.02), BatchNorm running mean ~N(0, 0.1), var ~U(0.5, 1.5),
+  gamma ~U(0.8, 1.2), beta ~N(0, 0.05), eps 1e-5; LayerNorm affine gamma ~N(1, 0.02), beta ~N(0, 0.02);
+* utterance lengths: lognormal with median 600 frames and sigma 0.5, clipped to [64, 1536], the padded length
+  rounded up to the 128-frame grid (``script/bench_asr.py:352-356``).
+
+Seeds: workload ``n`` uses ``1000 + n``; layer ``l`` of a stack uses ``base + l``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+D_MODEL = 1024          # EncoderConfig.hidden_dim
+D_INNER = 2048          # hidden_dim * conv_expansion_factor
+KERNEL = 15             # EncoderConfig.conv_kernel_size
+FRAME_GRID = 128        # bench_asr.py FRAME_GRID used by the record run
+EXEC_BATCH = 48         # bench_asr.py EXEC_BATCH used by the record run
+LEN_MEDIAN = 600.0
+LEN_SIGMA = 0.5
+LEN_MIN, LEN_MAX = 64, 1536
+
+
+@dataclass
+class ConvModuleParams:
+    """Raw (unfolded) parameters of one ConformerConvModule, named after the reference state_dict keys
+    (``models/granite_speech_nar/conformer.py:164-170``).  All arrays are float32."""
+
+    norm_weight: np.ndarray        # (D,)
+    norm_bias: np.ndarray          # (D,)
+    up_weight: np.ndarray          # (2I, D)   up_conv.weight[:, :, 0]
+    up_bias: np.ndarray            # (2I,)
+    dw_weight: np.ndarray          # (I, K)    depth_conv.conv.weight[:, 0, :]
+    bn_mean: np.ndarray            # (I,)
+    bn_var: np.ndarray             # (I,)
+    bn_weight: np.ndarray          # (I,)
+    bn_bias: np.ndarray            # (I,)
+    down_weight: np.ndarray        # (D, I)    down_conv.weight[:, :, 0]
+    down_bias: np.ndarray          # (D,)
+    bn_eps: float = 1e-5
+    ln_eps: float = 1e-5
+
+
+def make_params(seed: int, d_model: int = D_MODEL, d_inner: int = D_INNER, kernel: int = KERNEL,
+                w_std: float = 0.02) -> ConvModuleParams:
+    """Random-init parameters of one conv module.  ``w_std`` scales the pointwise and depthwise weights; the
+    benchmark value is 0.02, parity tests also use larger values so that the module output is not dwarfed by
+    the residual."""
+    g = np.random.default_rng(seed)
+    f32 = np.float32
+    return ConvModuleParams(
+        norm_weight=(1.0 + g.normal(0.0, 0.02, d_model)).astype(f32),
+        norm_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+        up_weight=g.normal(0.0, w_std, (2 * d_inner, d_model)).astype(f32),
+        up_bias=g.normal(0.0, 0.02, 2 * d_inner).astype(f32),
+        dw_weight=g.normal(0.0, w_std, (d_inner, kernel)).astype(f32),
+        bn_mean=g.normal(0.0, 0.1, d_inner).astype(f32),
+        bn_var=g.uniform(0.5, 1.5, d_inner).astype(f32),
+        bn_weight=g.uniform(0.8, 1.2, d_inner).astype(f32),
+        bn_bias=g.normal(0.0, 0.05, d_inner).astype(f32),
+        down_weight=g.normal(0.0, w_std, (d_model, d_inner)).astype(f32),
+        down_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+    )
+
+
+def make_activations(seed: int, shape: tuple[int, ...]) -> np.ndarray:
+    """x ~ N(0, 1), float32."""
+    return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)
+
+
+def make_dw_weights(seed: int, channels: int = D_INNER, kernel: int = KERNEL) -> tuple[np.ndarray, np.ndarray]:
+    """Folded depthwise weight (C, K) ~N(0, 0.05) and bias (C,) ~N(0, 0.02) of the depthwise-alone workload."""
+    g = np.random.default_rng(seed)
+    w = g.normal(0.0, 0.05, (channels, kernel)).astype(np.float32)
+    b = g.normal(0.0, 0.02, channels).astype(np.float32)
+    return w, b
+
+
+def sample_lengths(seed: int, n: int) -> np.ndarray:
+    """Utterance lengths in encoder frames: round(exp(N(ln 600, 0.5))) clipped to [64, 1536]."""
+    g = np.random.default_rng(seed)
+    lens = np.rint(np.exp(g.normal(np.log(LEN_MEDIAN), LEN_SIGMA, n)))
+    return np.clip(lens, LEN_MIN, LEN_MAX).astype(np.int32)
+
+
+def round_up(v: int, grid: int) -> int:
+    return ((int(v) + grid - 1) // grid) * grid

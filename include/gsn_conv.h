@@ -1,0 +1,132 @@
+/* C ABI of the B200 (sm_100a) Conformer conv-module kernels: libgsn_conv.so.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, sizes and element strides, launches on the
+ * given CUDA stream (a cudaStream_t; NULL = legacy default stream) and returns a status code: GSN_OK (0) or one
+ * of the GSN_ERR_* values, with a message in gsn_last_error_string() (per calling thread).  Nothing here
+ * allocates device memory; the caller owns every buffer.  Calls are asynchronous with respect to the host, as
+ * kernel launches are.
+ *
+ * bf16 tensors are passed as `const void*` to IEEE bfloat16 data; fp32 vectors as `const float*`; lengths as
+ * int32.  The reference interface each entry point replaces is cited beside it (paths inside the reference
+ * project ccyrene/granite-speech-4.1-2b-nar-turbo).
+ */
+#ifndef GSN_CONV_H_
+#define GSN_CONV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gsn_stream_t; /* same type as cudaStream_t / CUstream */
+
+enum {
+  GSN_OK = 0,
+  GSN_ERR_INVALID_ARG = 1,   /* null pointer, negative size, wrong kernel size */
+  GSN_ERR_UNSUPPORTED = 2,   /* shape / stride / alignment outside what the kernels handle */
+  GSN_ERR_CUDA = 3,          /* a CUDA runtime error at launch */
+  GSN_ERR_DRIVER = 4,        /* cuTensorMapEncodeTiled unavailable or it rejected a descriptor */
+  GSN_ERR_WORKSPACE = 5,     /* workspace smaller than gsn_conv_module_workspace_bytes() */
+  GSN_ERR_DEVICE_STATUS = 6  /* a kernel recorded a timeout in the device status word */
+};
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int gsn_version(void);
+
+/* Message of the last failed call on this thread ("" after a successful call). */
+const char* gsn_last_error_string(void);
+
+/* ---- depthwise conv k=15 + bias + SiLU -------------------------------------------------------------------
+ * Replaces granite::dwconv_silu (script/models/granite_speech_nar/conv_kernel.py:41-43), i.e. dwconv1d_silu
+ * (script/cuda_kernels/conv1d.py:102-114) and its kernel dwconv1d_silu_bf16 (conv1d.py:21-42):
+ *   y[b,c,t] = silu(bias[c] + sum_{j<K} weight[c,j] * x[b,c,t-K/2+j]), zero padding outside [0,T).
+ * x, y: logical (B, C, T) bf16 with element strides (sxB, sxC, sxT) / (syB, syC, syT); channels-last
+ * (sxC == 1) and channels-first (sxT == 1) both work, other strides take a slower generic path.  weight:
+ * (C, 1, K) bf16 contiguous, K must be 15; bias: (C,) bf16.  lengths: NULL or int32[B]; frames t >= lengths[b]
+ * read as zero and are written as zero (the reference op has no lengths). */
+int gsn_dwconv_silu_bf16(const void* x, const void* weight, const void* bias, void* y, int B, int C, int T, int K,
+                         int64_t sxB, int64_t sxC, int64_t sxT, int64_t syB, int64_t syC, int64_t syT,
+                         const int32_t* lengths, gsn_stream_t stream);
+
+/* Replaces granite::dwconv_silu_glu (conv_kernel.py:49-56) = dwconv1d_silu_glu (conv1d.py:85-99): x2 holds 2C
+ * channels, value = [0, C), gate = [C, 2C); the GLU product is rounded to bf16 before the convolution
+ * (conv1d.py:70-73).  C is the OUTPUT channel count; strides are those of x2 (B, 2C, T) and y (B, C, T). */
+int gsn_dwconv_silu_glu_bf16(const void* x2, const void* weight, const void* bias, void* y, int B, int C, int T,
+                             int K, int64_t sxB, int64_t sxC, int64_t sxT, int64_t syB, int64_t syC, int64_t syT,
+                             const int32_t* lengths, gsn_stream_t stream);
+
+/* ---- LayerNorm over the channel dim of channels-last rows ------------------------------------------------
+ * Replaces ConformerConvModule.norm (script/models/granite_speech_nar/conformer.py:164, :176).  x, y: [M, D]
+ * bf16 with row strides ld_x, ld_y (elements, multiples of 8); gamma, beta: [D] bf16; D in {256,512,1024,2048}. */
+int gsn_layernorm_bf16(const void* x, int64_t ld_x, const void* gamma, const void* beta, void* y, int64_t ld_y,
+                       int M, int D, float eps, gsn_stream_t stream);
+
+/* ---- pointwise_conv1 + GLU ------------------------------------------------------------------------------
+ * Replaces up_conv + GLU (conformer.py:165-166, :177, :181): h[m, c] = v * sigmoid(g) with
+ * v = (a[m,:] . W1[c,:]) + b1[c], g = (a[m,:] . W1[C+c,:]) + b1[C+c], C = N/2.
+ * a: [M, K] bf16 contiguous; h: [M, N/2] bf16 contiguous.  w1_glu / b1_glu hold W1 and b1 with their rows
+ * interleaved per 256-row block as [128 value rows | the matching 128 gate rows] (gsn_interleave_glu_rows).
+ * K % 64 == 0, N % 256 == 0, pointers 16-byte aligned.  b1_glu is fp32. */
+int gsn_gemm1_glu_bf16(const void* a, const void* w1_glu, const float* b1_glu, void* h, int M, int K, int N,
+                       gsn_stream_t stream);
+
+/* int8-weight form: w1q_glu int8 [N, K] (interleaved), s1_glu fp32 [N] per-row scale (W1 ~= w1q * s1). */
+int gsn_gemm1_glu_i8w(const void* a, const void* w1q_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
+                      int K, int N, gsn_stream_t stream);
+
+/* ---- pointwise_conv2 + residual -------------------------------------------------------------------------
+ * Replaces down_conv (conformer.py:170, :187) plus the block's residual add (conformer.py:207):
+ * out[m, n] = (d[m,:] . W2[n,:]) + b2[n] + residual[m, n].  d: [M, K] bf16; residual, out: [M, N] bf16 with
+ * row strides ld_res, ld_out (multiples of 8); residual may be NULL (no add).  K % 64 == 0, N % 256 == 0.
+ * b2 is fp32. */
+int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, const void* residual, int64_t ld_res,
+                            void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream);
+
+int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, const float* b2, const void* residual,
+                           int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream);
+
+/* ---- whole conv module + residual -------------------------------------------------------------------------
+ * Replaces ConformerConvModule.forward (conformer.py:175-189) followed by the residual add of
+ * ConformerBlock.forward (conformer.py:207), with BatchNorm folded (fold_bn.py:33-68):
+ *   out = x + down_conv(silu(dwconv(glu(up_conv(layernorm(x))))))
+ * (add_residual = 0 returns the module output alone, for callers that add the residual themselves as
+ * ConformerBlock.forward does.)
+ * x, out: [B, T, D] bf16 contiguous (channels-last frames), D = 1024 and inner 2048 in the Granite encoder but
+ * any D in {256,512,1024,2048} with 2*inner % 256 == 0 works.  lengths: NULL or int32[B]: GLU frames
+ * t >= lengths[b] are zeroed before the depthwise conv and its output there is zero, so valid frames equal the
+ * module run on the trimmed utterance and padded frames of `out` equal x + b2.
+ * workspace: device buffer of at least gsn_conv_module_workspace_bytes(B, T, D, inner) bytes, 256-byte aligned. */
+size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner);
+
+int gsn_conv_module_bf16(const void* x, const void* ln_w, const void* ln_b, const void* w1_glu,
+                         const float* b1_glu, const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                         const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
+                         float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
+int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const void* w1q_glu,
+                        const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,
+                        const void* w2q, const float* s2, const float* b2, const int32_t* lengths,
+                        int add_residual, void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
+                        size_t workspace_bytes, gsn_stream_t stream);
+
+/* ---- weight preparation --------------------------------------------------------------------------------
+ * Device-to-device copy of `rows` x `row_bytes` with the GLU row interleave used by gsn_gemm1_*: output block j
+ * (256 rows) = input rows [128 j, 128 j + 128) followed by rows [rows/2 + 128 j, rows/2 + 128 j + 128).
+ * rows % 256 == 0.  Works for weights (row_bytes = K * elem), biases and scales (row_bytes = elem). */
+int gsn_interleave_glu_rows(const void* src, void* dst, int rows, int64_t row_bytes, gsn_stream_t stream);
+
+/* ---- failure detection ---------------------------------------------------------------------------------
+ * Every spin-wait in these kernels is bounded (2 s); one that runs out records a code in a per-device status
+ * word and the kernel unwinds.  gsn_device_status synchronises `stream`, returns the word in *status and
+ * clears it when `clear` is non-zero.  gsn_selftest_bounded_wait launches one CTA that waits on an mbarrier
+ * nothing will complete, with a limit of limit_ns (<= 2e9); the status word then reads 0x1FF. */
+int gsn_device_status(int* status, int clear, gsn_stream_t stream);
+int gsn_selftest_bounded_wait(uint64_t limit_ns, gsn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSN_CONV_H_ */

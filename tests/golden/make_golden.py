@@ -1,0 +1,139 @@
+"""Generate the golden fixtures in this folder by running the reference's own eager PyTorch code on the CPU.
+
+Run from the repository root in a container where the reference is mounted read-only at /root/reference:
+
+    python tests/golden/make_golden.py [/root/reference]
+
+What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/script``):
+
+* ``ConformerConvModule`` (``script/models/granite_speech_nar/conformer.py:158-189``) after ``fold_conv_bn_``
+  (``script/models/granite_speech_nar/fold_bn.py:33``), plus the residual add of ``conformer.py:207``, in fp32
+  (the CPU workload: B=1, T=256, seed 1001) and in bf16 (B=2, T=37, the load-time test-fire shape of
+  ``conv_kernel.py:91-95``), with and without trimming each utterance to its length;
+* the post-fold eager chain that ``granite::dwconv_silu`` replaces, ``F.silu(conv0(x))``
+  (``conv_kernel.py:95-96``), and the fp64 golden of ``script/cuda_kernels/conv1d.py:135-138``;
+* the GLU variant's eager chain ``F.silu(conv0(F.glu(x2, dim=1)))`` (``conv_kernel.py:91-92``).
+
+Inputs and parameters come from ``granite_conv_b200.synth`` (numpy PCG64 seeds), so the tests regenerate them
+bit-for-bit and only the reference outputs are stored.  bf16 tensors are stored as uint16 bit patterns.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "granite-speech-4.1-2b-nar-turbo_b200"))
+from granite_conv_b200 import synth  # noqa: E402
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def _reference_module(ref_script: str):
+    sys.path.insert(0, ref_script)
+    from models.granite_speech_nar.conformer import ConformerConvModule  # noqa: E402
+    from models.granite_speech_nar.config import EncoderConfig  # noqa: E402
+    from models.granite_speech_nar.fold_bn import fold_conv_bn_  # noqa: E402
+    return ConformerConvModule, EncoderConfig, fold_conv_bn_
+
+
+def build_module(ConformerConvModule, EncoderConfig, fold_conv_bn_, p: synth.ConvModuleParams, dtype):
+    m = ConformerConvModule(EncoderConfig())
+    with torch.no_grad():
+        m.norm.weight.copy_(torch.from_numpy(p.norm_weight))
+        m.norm.bias.copy_(torch.from_numpy(p.norm_bias))
+        m.up_conv.weight.copy_(torch.from_numpy(p.up_weight)[:, :, None])
+        m.up_conv.bias.copy_(torch.from_numpy(p.up_bias))
+        m.depth_conv.conv.weight.copy_(torch.from_numpy(p.dw_weight)[:, None, :])
+        m.batch_norm.running_mean.copy_(torch.from_numpy(p.bn_mean))
+        m.batch_norm.running_var.copy_(torch.from_numpy(p.bn_var))
+        m.batch_norm.weight.copy_(torch.from_numpy(p.bn_weight))
+        m.batch_norm.bias.copy_(torch.from_numpy(p.bn_bias))
+        m.down_conv.weight.copy_(torch.from_numpy(p.down_weight)[:, :, None])
+        m.down_conv.bias.copy_(torch.from_numpy(p.down_bias))
+    m.eval()
+    m = m.to(dtype)        # the fold casts back to the weight dtype, as in a bf16 model load
+    assert fold_conv_bn_(m) == 1
+    return m
+
+
+@torch.no_grad()
+def main(ref_root: str) -> None:
+    torch.manual_seed(0)
+    torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
+    CM, EC, fold = _reference_module(os.path.join(ref_root, "script"))
+    out = {}
+
+    # ---- fp32 CPU workload: B=1, T=256, seed 1001, no mask --------------------------------------------------
+    p = synth.make_params(1001)
+    x = synth.make_activations(1001 + 500, (1, 256, synth.D_MODEL))
+    m = build_module(CM, EC, fold, p, torch.float32)
+    xt = torch.from_numpy(x)
+    y = (m(xt) + xt).numpy().astype(np.float64)
+    flat = y.reshape(-1)
+    idx = np.arange(0, flat.size, 61)
+    np.savez_compressed(os.path.join(HERE, "module_fp32_b1t256.npz"),
+                        row_sum=y.sum(axis=-1).reshape(-1), row_sumsq=(y * y).sum(axis=-1).reshape(-1),
+                        sample_idx=idx.astype(np.int64), sample=flat[idx].astype(np.float32),
+                        dw_weight_folded=m.depth_conv.conv.weight.detach().numpy()[:, 0, :].astype(np.float32),
+                        dw_bias_folded=m.depth_conv.conv.bias.detach().numpy().astype(np.float32))
+    out["module_fp32_b1t256"] = y.shape
+
+    # ---- bf16 module, test-fire shape B=2, T=37; two weight scales; full and trimmed per utterance ---------
+    for tag, seed, w_std in (("w002", 1003, 0.02), ("w006", 2003, 0.06)):
+        p = synth.make_params(seed, w_std=w_std)
+        x = synth.make_activations(seed + 500, (2, 37, synth.D_MODEL))
+        m = build_module(CM, EC, fold, p, torch.bfloat16)
+        xb = torch.from_numpy(x).to(torch.bfloat16)
+        y_full = m(xb) + xb
+        lengths = np.array([37, 23], dtype=np.int32)
+        y_trim = [(m(xb[b:b + 1, :L]) + xb[b:b + 1, :L])[0] for b, L in enumerate(lengths)]
+        np.savez_compressed(os.path.join(HERE, f"module_bf16_b2t37_{tag}.npz"),
+                            full=_bits(y_full), lengths=lengths,
+                            trimmed=np.concatenate([_bits(t) for t in y_trim], axis=0),
+                            dw_weight_folded=_bits(m.depth_conv.conv.weight[:, 0, :]),
+                            dw_bias_folded=_bits(m.depth_conv.conv.bias))
+        out[f"module_bf16_{tag}"] = tuple(y_full.shape)
+
+    # ---- granite::dwconv_silu and its GLU variant (channels-first, as the reference op takes them) ----------
+    C, K = synth.D_INNER, synth.KERNEL
+    w, b = synth.make_dw_weights(1002)
+    conv0 = torch.nn.Conv1d(C, C, K, groups=C, bias=True, padding=K // 2)
+    with torch.no_grad():
+        conv0.weight.copy_(torch.from_numpy(w)[:, None, :])
+        conv0.bias.copy_(torch.from_numpy(b))
+    conv0 = conv0.to(torch.bfloat16)
+    xs = synth.make_activations(1002 + 500, (1, C, 37))
+    xb = torch.from_numpy(xs).to(torch.bfloat16)
+    eager = F.silu(conv0(xb))
+    golden64 = F.silu(F.conv1d(F.pad(xb.double(), (K // 2, K // 2)), conv0.weight.double(),
+                               conv0.bias.double(), groups=C)).to(torch.bfloat16)
+    x2 = synth.make_activations(1002 + 600, (1, 2 * C, 37))
+    x2b = torch.from_numpy(x2).to(torch.bfloat16)
+    eager_glu = F.silu(conv0(F.glu(x2b, dim=1)))
+    np.savez_compressed(os.path.join(HERE, "dwconv_silu_b1c2048t37.npz"),
+                        eager=_bits(eager), golden_fp64=_bits(golden64), eager_glu=_bits(eager_glu))
+    out["dwconv_silu"] = tuple(eager.shape)
+
+    # ---- fp64 golden on the conv1d.py self-test length T=261: statistics only ------------------------------
+    xs = synth.make_activations(1002 + 700, (1, C, 261))
+    xb = torch.from_numpy(xs).to(torch.bfloat16)
+    g = F.silu(F.conv1d(F.pad(xb.double(), (K // 2, K // 2)), conv0.weight.double(), conv0.bias.double(),
+                        groups=C)).to(torch.bfloat16).double().numpy()
+    np.savez_compressed(os.path.join(HERE, "dwconv_silu_stats_c2048t261.npz"),
+                        chan_sum=g.sum(axis=-1).reshape(-1), chan_sumsq=(g * g).sum(axis=-1).reshape(-1))
+    out["dwconv_silu_stats"] = g.shape
+
+    for k, v in out.items():
+        print(f"{k}: {v}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
