@@ -35,9 +35,11 @@ def test_module_vs_reference_golden(tag, seed, w_std):
     y = ops.run_conv_module(_t(x), p)
     ref_full = O.from_bf16_bits(g["full"])
     assert_bf16_close(y, ref_full, f"module {tag} vs reference")
-    # module part alone (residual removed) must agree too when it is not dwarfed by the residual
+    # the module part alone (residual removed) must agree in rel-L2 too when it is not dwarfed by the residual;
+    # element-wise it carries the final bf16 rounding of x + delta, so only the L2 gate applies to it
     if w_std >= 0.06:
-        assert_bf16_close(y.float().cpu().numpy() - x, ref_full - x, f"module delta {tag}", rel_l2=2e-2)
+        dy, dr = y.float().cpu().numpy() - x, ref_full - x
+        assert np.linalg.norm(dy - dr) / np.linalg.norm(dr) <= 2e-2
     lens = g["lengths"]
     ym = ops.run_conv_module(_t(x), p, lengths=torch.from_numpy(lens).to(DEV)).float().cpu().numpy()
     valid = np.concatenate([ym[b, :L] for b, L in enumerate(lens)])

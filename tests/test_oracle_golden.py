@@ -1,0 +1,105 @@
+"""Pins the CPU oracle to the reference: every fixture in tests/golden was produced by the reference's own eager
+PyTorch code (tests/golden/make_golden.py); the oracle must reproduce it from the same seeded inputs."""
+import os
+
+import numpy as np
+import pytest
+
+from granite_conv_b200 import synth
+from oracle import conv_module as O
+from parity import TOL_FP32, assert_bf16_close
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _load(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def test_bf16_round_matches_torch():
+    import torch
+    x = np.random.default_rng(0).normal(size=10000).astype(np.float32) * 10
+    x[:4] = [0.0, -0.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8]          # ties to even
+    ours = O.bf16_round(x)
+    ref = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(ours, ref)
+    np.testing.assert_array_equal(O.from_bf16_bits(O.bf16_bits(x)), ref)
+
+
+def test_fp32_module_cpu_workload():
+    """The CPU workload (B=1, T=256, fp32, no mask): oracle vs reference within 1e-5."""
+    g = _load("module_fp32_b1t256.npz")
+    p = synth.make_params(1001)
+    x = synth.make_activations(1501, (1, 256, synth.D_MODEL))
+    prep = O.prepare_fp32(p)
+    np.testing.assert_array_equal(prep["dw_w"], g["dw_weight_folded"])
+    np.testing.assert_array_equal(prep["dw_b"], g["dw_bias_folded"])
+    y = O.conv_module(x, prep, mode="fp32")
+    flat = y.reshape(-1)
+    assert np.max(np.abs(flat[g["sample_idx"]] - g["sample"])) <= TOL_FP32
+    np.testing.assert_allclose(y.sum(axis=-1).reshape(-1), g["row_sum"], atol=TOL_FP32 * 1024)
+    np.testing.assert_allclose((y.astype(np.float64) ** 2).sum(axis=-1).reshape(-1), g["row_sumsq"], rtol=1e-6)
+
+
+@pytest.mark.parametrize("tag,seed,w_std", [("w002", 1003, 0.02), ("w006", 2003, 0.06)])
+def test_bf16_module(tag, seed, w_std):
+    g = _load(f"module_bf16_b2t37_{tag}.npz")
+    p = synth.make_params(seed, w_std=w_std)
+    prep = O.prepare_bf16(p)
+    np.testing.assert_array_equal(O.bf16_bits(prep["dw_w"]), g["dw_weight_folded"])   # fold is bit-exact
+    np.testing.assert_array_equal(O.bf16_bits(prep["dw_b"]), g["dw_bias_folded"])
+    x = O.bf16_round(synth.make_activations(seed + 500, (2, 37, synth.D_MODEL)))
+    ref = O.from_bf16_bits(g["full"])
+    # reference rounding points: agrees up to a few one-ulp rounding flips
+    s = assert_bf16_close(O.conv_module(x, prep, mode="reference"), ref, f"{tag} reference-rounding oracle")
+    assert s["rel_l2"] < 1e-3
+    # fused rounding points (what the kernels compute): within the parity gate of the reference
+    assert_bf16_close(O.conv_module(x, prep, mode="fused"), ref, f"{tag} fused oracle")
+    lens = g["lengths"]
+    y = O.conv_module(x, prep, lengths=lens, mode="fused")
+    valid = np.concatenate([y[b, :L] for b, L in enumerate(lens)])
+    assert_bf16_close(valid, O.from_bf16_bits(g["trimmed"]), f"{tag} masked oracle vs trimmed reference")
+
+
+def test_dwconv_ops():
+    g = _load("dwconv_silu_b1c2048t37.npz")
+    w, b = synth.make_dw_weights(1002)
+    wb, bb = O.bf16_round(w), O.bf16_round(b)
+    x = O.bf16_round(synth.make_activations(1502, (1, 2048, 37)))
+    y = O.dwconv_silu(x.transpose(0, 2, 1), wb, bb).transpose(0, 2, 1)
+    np.testing.assert_array_equal(O.bf16_bits(y), g["golden_fp64"])          # exact against the fp64 golden
+    assert_bf16_close(y, O.from_bf16_bits(g["eager"]), "dw vs eager bf16")
+    x2 = O.bf16_round(synth.make_activations(1602, (1, 4096, 37)))
+    y2 = O.dwconv_silu_glu(x2.transpose(0, 2, 1), wb, bb).transpose(0, 2, 1)
+    assert_bf16_close(y2, O.from_bf16_bits(g["eager_glu"]), "dw glu vs eager bf16")
+
+
+def test_dwconv_stats_t261():
+    g = _load("dwconv_silu_stats_c2048t261.npz")
+    w, b = synth.make_dw_weights(1002)
+    x = O.bf16_round(synth.make_activations(1702, (1, 2048, 261)))
+    y = O.dwconv_silu(x.transpose(0, 2, 1), O.bf16_round(w), O.bf16_round(b)).transpose(0, 2, 1).astype(np.float64)
+    np.testing.assert_allclose(y.sum(axis=-1).reshape(-1), g["chan_sum"], atol=1e-9)
+    np.testing.assert_allclose((y * y).sum(axis=-1).reshape(-1), g["chan_sumsq"], rtol=1e-12)
+
+
+def test_lengths_semantics():
+    """Masked module rows equal the module on the trimmed utterance; padded rows are x + b2."""
+    p = synth.make_params(3, d_model=256, d_inner=256, w_std=0.05)
+    prep = O.prepare_bf16(p)
+    x = O.bf16_round(synth.make_activations(4, (2, 20, 256)))
+    lens = np.array([20, 9])
+    y = O.conv_module(x, prep, lengths=lens, mode="fused")
+    y9 = O.conv_module(x[1:2, :9], prep, mode="fused")
+    np.testing.assert_array_equal(y[1, :9], y9[0])
+    np.testing.assert_array_equal(y[1, 9:], O.bf16_round(x[1, 9:] + prep["b2"]))
+
+
+def test_quantize_per_channel():
+    w = np.random.default_rng(5).normal(0, 0.02, (64, 128)).astype(np.float32)
+    w[3] = 0.0
+    q, s = O.quantize_per_channel(w)
+    assert q.dtype == np.int8 and np.abs(q).max() <= 127
+    assert np.all(np.abs(q).max(axis=1)[np.arange(64) != 3] == 127)
+    assert s[3] == 1.0 and not q[3].any()
+    assert np.max(np.abs(q * s[:, None] - w)) <= 0.5 * s.max() + 1e-9
