@@ -264,37 +264,43 @@ def run_ours(args):
     act = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]   # ping-pong buffers
     act2 = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
 
-    g1_events = []
+    layer_events = []      # per recorded layer: (events[5], chunk) around layernorm, gemm1, dwconv, gemm2
 
     def layer_kernels(x, out, c, p, lens, record):
         """The four kernels of one conv module (the same launches gsn_conv_module_* makes), with CUDA events
-        around the up_conv GEMM when `record`."""
+        between them when `record`."""
         M = c.padded_frames
         hp = h_buf.data_ptr()
         tp = h_buf.data_ptr() + t_off
-        _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
-                                        p.ln_eps, sp), "layernorm")
+        lp, T = lens.data_ptr(), c.T
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
         if record:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+            ev[0].record(stream)
+        _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
+                                        p.ln_eps, lp, T, sp), "layernorm")
+        if record:
+            ev[1].record(stream)
         if int8:
             _lib.check(L.gsn_gemm1_glu_i8w(tp, p.w1q_glu.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), hp,
-                                           M, D, 2 * I, sp), "gemm1")
+                                           M, D, 2 * I, lp, T, sp), "gemm1")
         else:
-            _lib.check(L.gsn_gemm1_glu_bf16(tp, p.w1_glu.data_ptr(), p.b1_glu.data_ptr(), hp, M, D, 2 * I, sp),
-                       "gemm1")
+            _lib.check(L.gsn_gemm1_glu_bf16(tp, p.w1_glu.data_ptr(), p.b1_glu.data_ptr(), hp, M, D, 2 * I, lp, T,
+                                            sp), "gemm1")
         if record:
-            e1.record(stream)
-            g1_events.append((e0, e1, M))
+            ev[2].record(stream)
         _lib.check(L.gsn_dwconv_silu_bf16(hp, p.dw_w.data_ptr(), p.dw_b.data_ptr(), tp, c.B, I, c.T, 15,
-                                          c.T * I, 1, I, c.T * I, 1, I, lens.data_ptr(), sp), "dwconv")
+                                          c.T * I, 1, I, c.T * I, 1, I, lp, sp), "dwconv")
+        if record:
+            ev[3].record(stream)
         if int8:
             _lib.check(L.gsn_gemm2_residual_i8w(tp, p.w2q.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(), x.data_ptr(),
-                                                D, out.data_ptr(), D, M, I, D, sp), "gemm2")
+                                                D, out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
         else:
             _lib.check(L.gsn_gemm2_residual_bf16(tp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
-                                                 out.data_ptr(), D, M, I, D, sp), "gemm2")
+                                                 out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
+        if record:
+            ev[4].record(stream)
+            layer_events.append((ev, c))
 
     dw_events = []
 
@@ -367,14 +373,15 @@ def run_ours(args):
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
     else:
-        dur = sum(a.elapsed_time(b) for a, b, _ in g1_events) / len(g1_events)
-        frames = sum(m for _, _, m in g1_events) / len(g1_events)
-        achieved = frames * GEMM1_FLOP_PER_FRAME / (dur / 1e3) / 1e12
-        pk = peaks["bf16_tflops_sustained"]
-        roof = {"kernel": "gemm_kernel<GLU> (up_conv 1024->4096 + GLU)", "bound": "tensor", "achieved": achieved,
-                "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk, "traffic": None, "per_launch_ms": dur,
+        kernels = _kernel_breakdown(layer_events, peaks)
+        g1 = kernels["gemm1_glu"]
+        roof = {"kernel": "gemm_kernel<GLU> (up_conv 1024->4096 + GLU)", "bound": "tensor",
+                "achieved": g1["achieved"], "peak": g1["peak"], "unit": "TFLOP/s", "frac": g1["frac"],
+                "traffic": None, "per_launch_ms": g1["ms_per_launch"],
                 "algorithmic_flop_per_frame": GEMM1_FLOP_PER_FRAME,
-                "peak_source": f"bf16_tflops_sustained of {peaks['source']}"}
+                "frames_counted": "rows of the 128-row tiles holding valid frames (tiles of pure padding are "
+                                  "skipped by the kernel)",
+                "peak_source": f"bf16_tflops_sustained of {peaks['source']}", "kernels": kernels}
 
     # ---- end to end through the public op with pinned host buffers
     e2e = None
@@ -399,6 +406,40 @@ def run_ours(args):
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def _tile_rows(c, tile=128):
+    """Rows of the 128-row tiles that hold at least one valid frame (T is on the 128 grid)."""
+    return int(sum(((int(L) + tile - 1) // tile) * tile for L in c.lengths))
+
+
+def _kernel_breakdown(layer_events, peaks):
+    """Average launch time, share of the recorded kernel time and achieved rate of each of the four kernels.
+    Work per launch: LayerNorm reads and writes the valid frames (2 x 2 KB); the GEMMs compute the rows of the
+    128-row tiles that hold valid frames; the depthwise kernel reads the valid frames and writes every frame
+    (4 KB each way per frame)."""
+    names = ("layernorm", "gemm1_glu", "dwconv_silu", "gemm2_residual")
+    tot = {n: 0.0 for n in names}
+    work = {n: 0.0 for n in names}
+    for ev, c in layer_events:
+        m = c.padded_frames
+        for k, n in enumerate(names):
+            tot[n] += ev[k].elapsed_time(ev[k + 1])
+        valid = c.valid_frames
+        rows = _tile_rows(c)
+        work["layernorm"] += valid * 2 * D * 2
+        work["gemm1_glu"] += rows * GEMM1_FLOP_PER_FRAME
+        work["dwconv_silu"] += valid * I * 2 + m * I * 2
+        work["gemm2_residual"] += rows * GEMM2_FLOP_PER_FRAME
+    all_ms = sum(tot.values())
+    out = {}
+    for n in names:
+        tensor = n.startswith("gemm")
+        ach = work[n] / (tot[n] / 1e3) / (1e12 if tensor else 1e9)
+        pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
+        out[n] = {"ms_per_launch": tot[n] / len(layer_events), "share": tot[n] / all_ms, "achieved": ach,
+                  "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
+    return out
 
 
 def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):

@@ -183,7 +183,7 @@ int gsn_dwconv_silu_glu_bf16(const void* x2, const void* weight, const void* bia
 }
 
 int gsn_layernorm_bf16(const void* x, int64_t ld_x, const void* gamma, const void* beta, void* y, int64_t ld_y,
-                       int M, int D, float eps, gsn_stream_t stream) {
+                       int M, int D, float eps, const int32_t* lengths, int T, gsn_stream_t stream) {
   if (M < 0) return fail(GSN_ERR_INVALID_ARG, "layernorm: M=%d", M);
   if (!ln_dim_ok(D)) return fail(GSN_ERR_UNSUPPORTED, "layernorm: D=%d not in {256,512,1024,2048}", D);
   if (M == 0) return ok();
@@ -191,50 +191,69 @@ int gsn_layernorm_bf16(const void* x, int64_t ld_x, const void* gamma, const voi
   if (ld_x % 8 || ld_y % 8 || ld_x < D || ld_y < D || !aligned(x, 16) || !aligned(y, 16) || !aligned(gamma, 16) ||
       !aligned(beta, 16))
     return fail(GSN_ERR_UNSUPPORTED, "layernorm: rows must be 16-byte aligned (ld %% 8 == 0)");
+  if (lengths && (T <= 0 || M % T != 0))
+    return fail(GSN_ERR_UNSUPPORTED, "layernorm: with lengths, T=%d must divide M=%d", T, M);
   return finish(launch_layernorm((const __nv_bfloat16*)x, ld_x, (const __nv_bfloat16*)gamma,
-                                 (const __nv_bfloat16*)beta, (__nv_bfloat16*)y, ld_y, M, D, eps, (cudaStream_t)stream),
+                                 (const __nv_bfloat16*)beta, (__nv_bfloat16*)y, ld_y, M, D, eps, lengths, T,
+                                 (cudaStream_t)stream),
                 "gsn_layernorm_bf16");
 }
 
+// lengths != NULL: rows are M / T utterances of T frames (T % 128 == 0) and tiles of pure padding are skipped
+static int check_lengths(const char* name, const int32_t* lengths, int T, int M) {
+  if (!lengths) return 0;
+  if (T <= 0 || T % 128 != 0 || M % T != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: with lengths, T=%d must be a positive multiple of 128 dividing M=%d", name,
+                T, M);
+  return 0;
+}
+
 static int gemm1(const void* a, const void* w, const float* scale, const float* b, void* h, int M, int K, int N,
-                 int i8, gsn_stream_t stream, const char* name) {
+                 const int32_t* lengths, int T, int i8, gsn_stream_t stream, const char* name) {
   if (int rc = check_gemm(name, a, w, b, h, M, K, N)) return rc < 0 ? ok() : rc;
   if (i8 && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
+  if (int rc = check_lengths(name, lengths, T, M)) return rc;
   GemmArgs g{(const __nv_bfloat16*)a, w, b, i8 ? scale : nullptr, nullptr, (__nv_bfloat16*)h, (int64_t)(N / 2), 0,
-             M, N, K, i8};
+             M, N, K, i8, lengths, T};
   return finish(launch_gemm(g, kEpiGlu, (cudaStream_t)stream), name);
 }
 
 static int gemm2(const void* d, const void* w, const float* scale, const float* b, const void* res, int64_t ld_res,
-                 void* out, int64_t ld_out, int M, int K, int N, int i8, gsn_stream_t stream, const char* name) {
+                 void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths, int T, int i8,
+                 gsn_stream_t stream, const char* name) {
   if (int rc = check_gemm(name, d, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
   if (res && !aligned(res, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: residual must be 16-byte aligned", name);
   if (i8 && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
   if (ld_out % 8 || ld_out < N || (res && (ld_res % 8 || ld_res < N)))
     return fail(GSN_ERR_UNSUPPORTED, "%s: row strides must be >= N and multiples of 8", name);
+  if (int rc = check_lengths(name, lengths, T, M)) return rc;
   GemmArgs g{(const __nv_bfloat16*)d, w, b, i8 ? scale : nullptr, (const __nv_bfloat16*)res, (__nv_bfloat16*)out,
-             ld_out, ld_res, M, N, K, i8};
+             ld_out, ld_res, M, N, K, i8, lengths, T};
   return finish(launch_gemm(g, kEpiResidual, (cudaStream_t)stream), name);
 }
 
 int gsn_gemm1_glu_bf16(const void* a, const void* w1_glu, const float* b1_glu, void* h, int M, int K, int N,
-                       gsn_stream_t stream) {
-  return gemm1(a, w1_glu, nullptr, b1_glu, h, M, K, N, 0, stream, "gsn_gemm1_glu_bf16");
+                       const int32_t* lengths, int T, gsn_stream_t stream) {
+  return gemm1(a, w1_glu, nullptr, b1_glu, h, M, K, N, lengths, T, 0, stream, "gsn_gemm1_glu_bf16");
 }
 
 int gsn_gemm1_glu_i8w(const void* a, const void* w1q_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
-                      int K, int N, gsn_stream_t stream) {
-  return gemm1(a, w1q_glu, s1_glu, b1_glu, h, M, K, N, 1, stream, "gsn_gemm1_glu_i8w");
+                      int K, int N, const int32_t* lengths, int T, gsn_stream_t stream) {
+  return gemm1(a, w1q_glu, s1_glu, b1_glu, h, M, K, N, lengths, T, 1, stream, "gsn_gemm1_glu_i8w");
 }
 
 int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, const void* residual, int64_t ld_res,
-                            void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream) {
-  return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, 0, stream, "gsn_gemm2_residual_bf16");
+                            void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths, int T,
+                            gsn_stream_t stream) {
+  return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 0, stream,
+               "gsn_gemm2_residual_bf16");
 }
 
 int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, const float* b2, const void* residual,
-                           int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream) {
-  return gemm2(d, w2q, s2, b2, residual, ld_res, out, ld_out, M, K, N, 1, stream, "gsn_gemm2_residual_i8w");
+                           int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
+                           int T, gsn_stream_t stream) {
+  return gemm2(d, w2q, s2, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 1, stream,
+               "gsn_gemm2_residual_i8w");
 }
 
 size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
@@ -270,10 +289,12 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   __nv_bfloat16* t = (__nv_bfloat16*)((char*)ws + align256((size_t)M * inner * 2));
   const cudaStream_t st = (cudaStream_t)stream;
 
+  // with lengths and T on the 128-frame grid, 128-row tiles of pure padding skip the LayerNorm and GEMM work
+  const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
   int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
-                            M, D, eps, st);
+                            M, D, eps, skip, T, st);
   if (rc) return finish(rc, name);
-  GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, i8};
+  GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, i8, skip, T};
   rc = launch_gemm(g1, kEpiGlu, st);
   if (rc) return finish(rc, name);
   DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
@@ -281,7 +302,7 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   rc = launch_dwconv(dw, st);
   if (rc) return finish(rc, name);
   GemmArgs g2{t, w2, b2, i8 ? s2 : nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr, (__nv_bfloat16*)out,
-              D, D, M, D, inner, i8};
+              D, D, M, D, inner, i8, skip, T};
   rc = launch_gemm(g2, kEpiResidual, st);
   return finish(rc, name);
 }

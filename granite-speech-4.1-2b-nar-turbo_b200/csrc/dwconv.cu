@@ -7,18 +7,34 @@
 // Accumulation is fp32 and the output is rounded to bf16 once, as in the reference kernel.
 //
 // Two layouts:
-//  * channels-last (element stride of C is 1; the conv-module layout [B, T, C]): a CTA owns 128 channels of one
-//    utterance and walks 4 time tiles of 64 frames.  Each tile plus its 7-frame halo on both sides (78 rows x 256
-//    bytes) is staged in shared memory by a 3-D TMA load; out-of-range frames (t < 0, t >= T) arrive zero-filled.
-//    Two stages: the TMA for tile i+2 is issued as soon as tile i has been consumed.  A warp owns 16 output
-//    frames, a lane 4 channels (8-byte shared-memory rows, conflict-free), with the 60 weights in registers and
-//    packed fp32x2 FMAs.
+//  * channels-last (element stride of C is 1; the conv-module layout [B, T, C]): a persistent kernel.  A tile is
+//    CC channels x TT frames of one utterance; it is staged with its 7-frame halo on both sides ((TT + 14) rows of
+//    CC * 2 bytes) by a 3-D TMA load, out-of-range frames (t < 0, t >= T) arriving zero-filled.  Each CTA walks
+//    its tiles through a 3-stage shared-memory ring, so the loads of the next tiles are in flight while the
+//    current one is computed, across work-item boundaries.  A warp owns FPW output frames, a lane CPT channels
+//    (conflict-free shared-memory rows), with the 15 x CPT weights in registers and packed fp32x2 FMAs.  Tiles
+//    entirely inside the utterance take an unmasked path; tiles entirely past its end skip the load.
 //  * channels-first (element stride of T is 1; the layout the reference op receives from up_conv): a CTA owns 32
 //    channels x 128 frames, stages the rows (plus halo) in shared memory as fp32 with plain coalesced loads
 //    (row strides need not be 16-byte multiples there, e.g. T = 37), and transposes the result through shared
-//    memory for coalesced stores.
+//    memory for coalesced stores.  Any other stride pattern also takes this path.
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
+
+// Tile shape of the channels-last kernel (compile-time: channels per lane, frames per warp, warps per CTA, and
+// time tiles per work item).
+#ifndef GSN_DW_CPT
+#define GSN_DW_CPT 4
+#endif
+#ifndef GSN_DW_FPW
+#define GSN_DW_FPW 16
+#endif
+#ifndef GSN_DW_WARPS
+#define GSN_DW_WARPS 4
+#endif
+#ifndef GSN_DW_SEG
+#define GSN_DW_SEG 4
+#endif
 
 namespace gsn {
 
@@ -29,19 +45,24 @@ constexpr int HALO = 7;
 
 // ----------------------------------------------------------------------------------------------------------------
 // channels-last
-constexpr int CL_CC = 128;                // channels per CTA
-constexpr int CL_TT = 64;                 // output frames per tile
-constexpr int CL_ROWS = CL_TT + 2 * HALO; // 78 staged rows
-constexpr int CL_THREADS = 128;           // 4 warps x 16 frames
-constexpr int CL_FPW = CL_TT / 4;         // frames per warp
-constexpr int CL_TILES = 4;               // tiles per CTA
-constexpr int CL_ROW_BYTES = CL_CC * 2;
-constexpr int CL_TILE_BYTES = CL_ROWS * CL_ROW_BYTES;  // 19968
+template <int CPT, int FPW, int WARPS, bool GLU>
+struct ClCfg {
+  static constexpr int NP = CPT / 2;               // fp32 pairs per lane
+  static constexpr int CC = 32 * CPT;              // channels per tile
+  static constexpr int TT = FPW * WARPS;           // output frames per tile
+  static constexpr int ROWS = TT + 2 * HALO;       // staged rows
+  static constexpr int ROW_BYTES = CC * 2;
+  static constexpr int TILE_BYTES = ROWS * ROW_BYTES;
+  static constexpr int STAGES = 3;
+  static constexpr int THREADS = 32 * WARPS;
+  static constexpr int SEG = GSN_DW_SEG;           // consecutive time tiles per work item
+};
 
-template <bool GLU>
+template <int CPT, int FPW, int WARPS, bool GLU>
 struct __align__(128) ClSmem {
-  uint8_t x[2][GLU ? 2 : 1][CL_TILE_BYTES];
-  uint64_t full[2];
+  using C = ClCfg<CPT, FPW, WARPS, GLU>;
+  uint8_t x[C::STAGES][GLU ? 2 : 1][C::TILE_BYTES];
+  uint64_t full[C::STAGES];
   int abort_flag;
 };
 
@@ -51,7 +72,8 @@ struct ClParams {
   __nv_bfloat16* y;
   const int* lengths;
   int64_t syB, syT;
-  int T, C;
+  int B, T, C;
+  int n_ct, n_seg, n_items;     // channel tiles, time segments per (b, channel tile), work items
 };
 
 __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t v) { return make_float2(bf16lo_to_f32(v), bf16hi_to_f32(v)); }
@@ -64,127 +86,248 @@ __device__ __forceinline__ float2 glu_pair(uint32_t a, uint32_t g) {
   return bf16x2_to_f2(r);
 }
 
-template <bool GLU>
-__global__ void __launch_bounds__(CL_THREADS, 3)
+template <int NP>
+__device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t (&w)[NP]) {
+  if constexpr (NP == 4) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (NP == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+
+template <int NP>
+__device__ __forceinline__ void stg_words(__nv_bfloat16* p, const uint32_t (&w)[NP]) {
+  if constexpr (NP == 4) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else if constexpr (NP == 2) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  }
+}
+
+// Position of the k-th tile walked by this CTA: work items are (utterance, channel tile, time segment) in that
+// order, dealt round-robin to the persistent CTAs; a segment is SEG consecutive time tiles.
+template <class Cfg>
+struct TileWalk {
+  int item, sub;
+  __device__ void start() {
+    item = blockIdx.x;
+    sub = 0;
+  }
+  __device__ bool valid(const ClParams& p) const { return item < p.n_items; }
+  __device__ void coords(const ClParams& p, int& b, int& c0, int& t0) const {
+    const int seg = item % p.n_seg;
+    const int rest = item / p.n_seg;
+    const int ct = rest % p.n_ct;
+    b = rest / p.n_ct;
+    c0 = ct * Cfg::CC;
+    t0 = (seg * Cfg::SEG + sub) * Cfg::TT;
+  }
+  __device__ void next(const ClParams& p) {
+    int b, c0, t0;
+    coords(p, b, c0, t0);
+    ++sub;
+    if (sub >= Cfg::SEG || t0 + Cfg::TT >= p.T) {
+      sub = 0;
+      item += gridDim.x;
+    }
+  }
+};
+
+template <int CPT, int FPW, int WARPS, bool GLU>
+__global__ void __launch_bounds__(32 * WARPS)
     dwconv_cl_kernel(const __grid_constant__ CUtensorMap tmX, ClParams p) {
+  using Cfg = ClCfg<CPT, FPW, WARPS, GLU>;
+  constexpr int NP = Cfg::NP;
+  constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  ClSmem<GLU>& s = *reinterpret_cast<ClSmem<GLU>*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  auto& s = *reinterpret_cast<ClSmem<CPT, FPW, WARPS, GLU>*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                                             ~uintptr_t(127));
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int c0 = blockIdx.x * CL_CC;
-  const int b = blockIdx.z;
-  const int t_begin = blockIdx.y * (CL_TT * CL_TILES);
   const int T = p.T;
-  int n_tiles = (T - t_begin + CL_TT - 1) / CL_TT;
-  if (n_tiles > CL_TILES) n_tiles = CL_TILES;
-  const int len = p.lengths ? min(max(__ldg(p.lengths + b), 0), T) : T;
-  constexpr uint32_t kTxBytes = (GLU ? 2 : 1) * CL_TILE_BYTES;
+  constexpr uint32_t kTxBytes = (GLU ? 2 : 1) * Cfg::TILE_BYTES;
 
   if (tid == 0) {
-    mbar_init(&s.full[0], 1);
-    mbar_init(&s.full[1], 1);
+    for (int i = 0; i < STAGES; ++i) mbar_init(&s.full[i], 1);
     s.abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmX);
   }
   __syncthreads();
 
-  auto issue = [&](int i) {
-    const int st = i & 1;
-    const int t_in = t_begin + i * CL_TT - HALO;
+  auto len_of = [&](int b) { return p.lengths ? min(max(__ldg(p.lengths + b), 0), T) : T; };
+  // producer side (thread 0): load tile `w` into stage st, or, if every output frame of it is padding, complete
+  // the stage's phase without a copy
+  auto issue = [&](const TileWalk<Cfg>& w, int st) {
+    int b, c0, t0;
+    w.coords(p, b, c0, t0);
+    if (t0 >= len_of(b)) {
+      mbar_arrive(&s.full[st]);
+      return;
+    }
     mbar_arrive_expect_tx(&s.full[st], kTxBytes);
-    tma_load_3d(s.x[st][0], &tmX, &s.full[st], c0, t_in, b);
-    if (GLU) tma_load_3d(s.x[st][GLU ? 1 : 0], &tmX, &s.full[st], c0 + p.C, t_in, b);
+    tma_load_3d(s.x[st][0], &tmX, &s.full[st], c0, t0 - HALO, b);
+    if (GLU) tma_load_3d(s.x[st][GLU ? 1 : 0], &tmX, &s.full[st], c0 + p.C, t0 - HALO, b);
   };
-  if (tid == 0) {
-    if (n_tiles > 0) issue(0);
-    if (n_tiles > 1) issue(1);
-  }
 
-  // weights of this lane's 4 channels, as fp32 pairs: wr[j][0] = (c, c+1), wr[j][1] = (c+2, c+3)
-  const int cl = c0 + lane * 4;
-  float2 wr[KW][2];
-  {
-    const __nv_bfloat16* wp = p.w + (int64_t)cl * KW;
-#pragma unroll
-    for (int j = 0; j < KW; ++j) {
-      wr[j][0] = make_float2(__bfloat162float(wp[j]), __bfloat162float(wp[KW + j]));
-      wr[j][1] = make_float2(__bfloat162float(wp[2 * KW + j]), __bfloat162float(wp[3 * KW + j]));
+  TileWalk<Cfg> prod;
+  prod.start();
+  int issued = 0;                                    // tiles handed to stages so far (thread 0)
+  if (tid == 0) {
+    for (int i = 0; i < STAGES && prod.valid(p); ++i) {
+      issue(prod, i);
+      prod.next(p);
+      ++issued;
     }
   }
-  const float2 bias01 = make_float2(__bfloat162float(p.bias[cl]), __bfloat162float(p.bias[cl + 1]));
-  const float2 bias23 = make_float2(__bfloat162float(p.bias[cl + 2]), __bfloat162float(p.bias[cl + 3]));
 
+  TileWalk<Cfg> cons;
+  cons.start();
+  int cur_c0 = -1;
+  float2 wr[KW][NP];
+  float2 bias[NP];
   bool alive = true;
-  for (int i = 0; i < n_tiles; ++i) {
-    const int st = i & 1;
-    if (alive) alive = mbar_wait_bounded(&s.full[st], (uint32_t)((i >> 1) & 1), &s.abort_flag, kStatusTimeoutDw);
-    const int t0 = t_begin + i * CL_TT;
-    if (alive) {
-      float2 acc[CL_FPW][2];
+  for (int k = 0; cons.valid(p); ++k, cons.next(p)) {
+    int b, c0, t0;
+    cons.coords(p, b, c0, t0);
+    const int len = len_of(b);
+    const int st = k % STAGES;
+    if (c0 != cur_c0) {  // weights of this lane's channels, as fp32 pairs
+      cur_c0 = c0;
+      const __nv_bfloat16* wp = p.w + (int64_t)(c0 + lane * CPT) * KW;
 #pragma unroll
-      for (int f = 0; f < CL_FPW; ++f) {
-        acc[f][0] = bias01;
-        acc[f][1] = bias23;
+      for (int j = 0; j < KW; ++j)
+#pragma unroll
+        for (int q = 0; q < NP; ++q)
+          wr[j][q] = make_float2(__bfloat162float(wp[(2 * q) * KW + j]), __bfloat162float(wp[(2 * q + 1) * KW + j]));
+#pragma unroll
+      for (int q = 0; q < NP; ++q)
+        bias[q] = make_float2(__bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
+                              __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
+    }
+    if (alive)
+      alive = mbar_wait_bounded(&s.full[st], (uint32_t)((k / STAGES) & 1), &s.abort_flag, kStatusTimeoutDw);
+    const int row0 = warp * FPW;                 // first output frame (and staged row) of this warp
+    __nv_bfloat16* yb = p.y + (int64_t)b * p.syB + c0 + lane * CPT;
+    if (alive && t0 >= len) {
+      // every output frame of the tile is padding
+#pragma unroll
+      for (int f = 0; f < FPW; ++f) {
+        const int t = t0 + row0 + f;
+        uint32_t z[NP];
+#pragma unroll
+        for (int q = 0; q < NP; ++q) z[q] = 0u;
+        if (t < T) stg_words<NP>(yb + (int64_t)t * p.syT, z);
       }
-      const int row0 = warp * CL_FPW;                // first staged row read by this warp
-      const int t_row0 = t0 - HALO + row0;           // its frame index
-      const uint8_t* xa = s.x[st][0] + row0 * CL_ROW_BYTES + lane * 8;
-      const uint8_t* xg = s.x[st][GLU ? 1 : 0] + row0 * CL_ROW_BYTES + lane * 8;
+    } else if (alive) {
+      const bool fast = t0 + Cfg::TT + HALO <= len;   // every staged row and output frame is inside the utterance
+      float2 acc[FPW][NP];
 #pragma unroll
-      for (int r = 0; r < CL_FPW + 2 * HALO; ++r) {
-        float2 x01, x23;
-        const uint2 va = *reinterpret_cast<const uint2*>(xa + r * CL_ROW_BYTES);
+      for (int f = 0; f < FPW; ++f)
+#pragma unroll
+        for (int q = 0; q < NP; ++q) acc[f][q] = bias[q];
+      const int t_row0 = t0 - HALO + row0;
+      const uint8_t* xa = s.x[st][0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
+      const uint8_t* xg = s.x[st][GLU ? 1 : 0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
+#pragma unroll
+      for (int r = 0; r < FPW + 2 * HALO; ++r) {
+        uint32_t va[NP];
+        lds_words<NP>(xa + r * Cfg::ROW_BYTES, va);
+        float2 xv[NP];
         if (GLU) {
-          const uint2 vg = *reinterpret_cast<const uint2*>(xg + r * CL_ROW_BYTES);
-          x01 = glu_pair(va.x, vg.x);
-          x23 = glu_pair(va.y, vg.y);
+          uint32_t vg[NP];
+          lds_words<NP>(xg + r * Cfg::ROW_BYTES, vg);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) xv[q] = glu_pair(va[q], vg[q]);
         } else {
-          x01 = bf16x2_to_f2(va.x);
-          x23 = bf16x2_to_f2(va.y);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) xv[q] = bf16x2_to_f2(va[q]);
         }
-        if (t_row0 + r >= len) {  // frames past the utterance read as zero (t >= T is zero-filled by TMA)
-          x01 = make_float2(0.f, 0.f);
-          x23 = make_float2(0.f, 0.f);
+        if (!fast && t_row0 + r >= len) {  // frames past the utterance read as zero (t >= T is zero-filled)
+#pragma unroll
+          for (int q = 0; q < NP; ++q) xv[q] = make_float2(0.f, 0.f);
         }
 #pragma unroll
-        for (int f = 0; f < CL_FPW; ++f) {
+        for (int f = 0; f < FPW; ++f) {
           const int j = r - f;
           if (j >= 0 && j < KW) {
-            acc[f][0] = ffma2(wr[j][0], x01, acc[f][0]);
-            acc[f][1] = ffma2(wr[j][1], x23, acc[f][1]);
+#pragma unroll
+            for (int q = 0; q < NP; ++q) acc[f][q] = ffma2(wr[j][q], xv[q], acc[f][q]);
           }
         }
       }
-      __nv_bfloat16* yb = p.y + (int64_t)b * p.syB + cl;
 #pragma unroll
-      for (int f = 0; f < CL_FPW; ++f) {
+      for (int f = 0; f < FPW; ++f) {
         const int t = t0 + row0 + f;
-        if (t < T) {
-          uint2 o;
-          if (t < len) {
-            o.x = pack_bf16x2(silu_fast(acc[f][0].x), silu_fast(acc[f][0].y));
-            o.y = pack_bf16x2(silu_fast(acc[f][1].x), silu_fast(acc[f][1].y));
-          } else {
-            o.x = 0u;
-            o.y = 0u;
-          }
-          *reinterpret_cast<uint2*>(yb + (int64_t)t * p.syT) = o;
-        }
+        uint32_t o[NP];
+        const bool valid = fast || t < len;
+#pragma unroll
+        for (int q = 0; q < NP; ++q)
+          o[q] = valid ? pack_bf16x2(silu_fast(acc[f][q].x), silu_fast(acc[f][q].y)) : 0u;
+        if (fast || t < T) stg_words<NP>(yb + (int64_t)t * p.syT, o);
       }
     }
     __syncthreads();  // stage st fully consumed by every warp
-    if (tid == 0 && alive && !s.abort_flag && i + 2 < n_tiles) {
+    if (tid == 0 && alive && !s.abort_flag && prod.valid(p)) {
       fence_proxy_async_smem();
-      issue(i + 2);
+      issue(prod, st);
+      prod.next(p);
+      ++issued;
     }
   }
   if (tid == 0 && s.abort_flag) {
-    // unwinding after a timeout: let outstanding copies land before the shared memory is released
-    for (int i = n_tiles - 2; i < n_tiles; ++i)
-      if (i >= 0) mbar_wait_bounded(&s.full[i & 1], (uint32_t)((i >> 1) & 1), nullptr, kStatusTimeoutDw, 100000000ull);
+    // unwinding after a timeout: let the copies still in flight (the last STAGES issued) land before the shared
+    // memory is released
+    for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k)
+      mbar_wait_bounded(&s.full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr, kStatusTimeoutDw, 100000000ull);
   }
+}
+
+template <int CPT, int FPW, int WARPS, bool GLU>
+int launch_cl(const DwArgs& a, cudaStream_t stream) {
+  using Cfg = ClCfg<CPT, FPW, WARPS, GLU>;
+  CUtensorMap tm;
+  const uint64_t cx = (uint64_t)a.C * (GLU ? 2 : 1);
+  const uint64_t dims[3] = {cx, (uint64_t)a.T, (uint64_t)a.B};
+  const uint64_t strides[2] = {(uint64_t)a.sxT * 2, (uint64_t)a.sxB * 2};
+  const uint32_t box[3] = {(uint32_t)Cfg::CC, (uint32_t)Cfg::ROWS, 1};
+  int rc = encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  ClParams p;
+  p.w = a.w;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.lengths = a.lengths;
+  p.syB = a.syB;
+  p.syT = a.syT;
+  p.B = a.B;
+  p.T = a.T;
+  p.C = a.C;
+  p.n_ct = a.C / Cfg::CC;
+  const int n_tt = (a.T + Cfg::TT - 1) / Cfg::TT;
+  p.n_seg = (n_tt + Cfg::SEG - 1) / Cfg::SEG;
+  const int64_t items = (int64_t)a.B * p.n_ct * p.n_seg;
+  if (items > 0x7fffffff) return (int)cudaErrorInvalidValue;
+  p.n_items = (int)items;
+  auto kern = dwconv_cl_kernel<CPT, FPW, WARPS, GLU>;
+  const int smem = (int)sizeof(ClSmem<CPT, FPW, WARPS, GLU>) + 128;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::THREADS, smem);
+  if (e != cudaSuccess) return (int)e;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t slots = (int64_t)device_sm_count() * per_sm;
+  const int grid = (int)(items < slots ? items : slots);
+  kern<<<grid, Cfg::THREADS, smem, stream>>>(tm, p);
+  return (int)cudaGetLastError();
 }
 
 // ----------------------------------------------------------------------------------------------------------------
@@ -282,33 +425,14 @@ using namespace dw_impl;
 
 int launch_dwconv(const DwArgs& a, cudaStream_t stream) {
   if (a.B == 0 || a.T == 0 || a.C == 0) return 0;
-  const bool cl = (a.sxC == 1 && a.syC == 1 && (a.C % CL_CC) == 0 && (a.sxT % 8) == 0 && (a.sxB % 8) == 0 &&
-                   (a.syT % 4) == 0 && (a.syB % 4) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
-                   (reinterpret_cast<uintptr_t>(a.y) & 7) == 0);
+  constexpr int CC = ClCfg<GSN_DW_CPT, GSN_DW_FPW, GSN_DW_WARPS, false>::CC;
+  const bool cl = (a.sxC == 1 && a.syC == 1 && (a.C % CC) == 0 && (a.sxT % 8) == 0 && (a.sxB % 8) == 0 &&
+                   (a.syT % GSN_DW_CPT) == 0 && (a.syB % GSN_DW_CPT) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.y) & (2 * GSN_DW_CPT - 1)) == 0);
   if (cl) {
-    // x viewed as [B][T][Cx] with Cx = C (or 2C for GLU) channels contiguous
-    CUtensorMap tm;
-    const uint64_t cx = (uint64_t)a.C * (a.glu ? 2 : 1);
-    const uint64_t dims[3] = {cx, (uint64_t)a.T, (uint64_t)a.B};
-    const uint64_t strides[2] = {(uint64_t)a.sxT * 2, (uint64_t)a.sxB * 2};
-    const uint32_t box[3] = {CL_CC, CL_ROWS, 1};
-    int rc = encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.x, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-    ClParams p{a.w, a.bias, a.y, a.lengths, a.syB, a.syT, a.T, a.C};
-    dim3 grid(a.C / CL_CC, (a.T + CL_TT * CL_TILES - 1) / (CL_TT * CL_TILES), a.B);
-    if (a.glu) {
-      const int smem = (int)sizeof(ClSmem<true>) + 128;
-      cudaError_t e = cudaFuncSetAttribute(dwconv_cl_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return (int)e;
-      dwconv_cl_kernel<true><<<grid, CL_THREADS, smem, stream>>>(tm, p);
-    } else {
-      const int smem = (int)sizeof(ClSmem<false>) + 128;
-      cudaError_t e = cudaFuncSetAttribute(dwconv_cl_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return (int)e;
-      dwconv_cl_kernel<false><<<grid, CL_THREADS, smem, stream>>>(tm, p);
-    }
-    return (int)cudaGetLastError();
+    return a.glu ? launch_cl<GSN_DW_CPT, GSN_DW_FPW, GSN_DW_WARPS, true>(a, stream)
+                 : launch_cl<GSN_DW_CPT, GSN_DW_FPW, GSN_DW_WARPS, false>(a, stream);
   }
   CfParams p{a.x, a.w, a.bias, a.y, a.lengths, a.sxB, a.sxC, a.sxT, a.syB, a.syC, a.syT, a.C, a.T};
   dim3 grid((a.T + CF_TT - 1) / CF_TT, (a.C + CF_CC - 1) / CF_CC, a.B);

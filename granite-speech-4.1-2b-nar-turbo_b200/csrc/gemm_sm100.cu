@@ -14,7 +14,13 @@
 //   warps 6-9   (int8 weights only) dequantise the staged int8 W tile into the swizzled bf16 layout
 // The accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of tile i overlaps the
 // main loop of tile i+1.  Tiles are visited N-fastest so the 16 (or 4) CTAs sharing an A row-block run at
-// the same time and read it from L2.
+// the same time and read it from L2.  The epilogue keeps the tile's bias / scale columns in a per-warp shared
+// slice (broadcast reads) and, for the residual GEMM, fetches its row of the residual before it waits for the
+// accumulator, so the HBM latency of that read overlaps the main loop.
+//
+// With per-utterance lengths (rows b*T .. b*T+T-1 belong to utterance b, T % 128 == 0), a 128-row tile made only
+// of padding frames is skipped by every role: the GLU GEMM leaves those rows unwritten (nothing downstream reads
+// them) and the residual GEMM writes them as residual + bias, which is what a zero row of A produces.
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
@@ -50,6 +56,7 @@ struct __align__(1024) Smem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
+  float ep_vec[4][2][BN];                 // per epilogue warp: the tile's bias and scale columns
 };
 
 struct KParams {
@@ -57,9 +64,21 @@ struct KParams {
   const float* col_scale;
   const __nv_bfloat16* residual;
   __nv_bfloat16* out;
+  const int* lengths;                     // per-utterance valid frames, or null (every row computed)
   int64_t ld_out, ld_res;
   int M, N, K;
+  int T;                                  // frames per utterance when lengths != null (T % 128 == 0)
 };
+
+// A 128-row tile lies inside one utterance (T % 128 == 0); it is inactive when every row is padding.
+__device__ __forceinline__ bool tile_active(const KParams& p, int m_blk) {
+  if (p.lengths == nullptr) return true;
+  const int row = m_blk * BM;
+  const int b = row / p.T;
+  return row - b * p.T < __ldg(p.lengths + b);
+}
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
 __device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
   uint4 lo, hi;
@@ -142,6 +161,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const int m_blk = tile / num_n;
       const int n_blk = tile - m_blk * num_n;
+      if (!tile_active(p, m_blk)) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         bool got = mbar_wait_bounded(&s.empty[stage], phase ^ 1u, abort_flag, kStatusTimeoutProducer);
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -183,9 +203,11 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     uint32_t phase = 0;
     bool ok = true;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      if (!tile_active(p, tile / num_n)) continue;
       const int acc = local & 1;
       const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+      ++local;
       bool got = mbar_wait_bounded(&s.tempty[acc], use_par ^ 1u, abort_flag, kStatusTimeoutMma);
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
@@ -227,24 +249,42 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     mbar_wait_bounded(&s.mma_done, 0, nullptr, kStatusTimeoutMma, 100000000ull);
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
-    const int q = warp & 3;  // a warp may only read its own 32-lane quarter of TMEM
+    const int q = warp & 3;           // a warp may only read its own 32-lane quarter of TMEM
+    float* vb = s.ep_vec[warp - 2][0];
+    float* vs = s.ep_vec[warp - 2][1];
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m_blk = tile / num_n;
       const int n_blk = tile - m_blk * num_n;
-      const int acc = local & 1;
-      const uint32_t use_par = (uint32_t)((local >> 1) & 1);
-      bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
-      got = __shfl_sync(0xffffffffu, got, 0);
-      if (!got) break;
-      tc_fence_after();
+      const bool active = tile_active(p, m_blk);
+      if (EPI == kEpiGlu && !active) continue;   // GLU rows of padding frames are never read downstream
+      const int nb = n_blk * BN;
+      // this tile's 256 bias (and scale) values into the warp's own shared slice
+      __syncwarp();
+      {
+        const float4* src = reinterpret_cast<const float4*>(p.bias + nb);
+        reinterpret_cast<float4*>(vb)[lane] = __ldg(src + lane);
+        reinterpret_cast<float4*>(vb)[lane + 32] = __ldg(src + lane + 32);
+        if (W_I8) {
+          const float4* ss = reinterpret_cast<const float4*>(p.col_scale + nb);
+          reinterpret_cast<float4*>(vs)[lane] = __ldg(ss + lane);
+          reinterpret_cast<float4*>(vs)[lane + 32] = __ldg(ss + lane + 32);
+        }
+      }
+      __syncwarp();
       const int row = m_blk * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 
       if (EPI == kEpiGlu) {
+        const int acc = local & 1;
+        const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+        ++local;
+        bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) break;
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
         // accumulator columns [0,128) = value channels, [128,256) = their gate channels
-        const int nb = n_blk * BN;
         __nv_bfloat16* orow = p.out + (int64_t)row * p.ld_out + (int64_t)n_blk * (BN / 2);
 #pragma unroll 1
         for (int j = 0; j < BN / 2; j += 16) {
@@ -254,49 +294,82 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
           tmem_wait_ld();
           float o[16];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            float a = __uint_as_float(va[c]);
-            float g = __uint_as_float(vg[c]);
+          for (int c4 = 0; c4 < 16; c4 += 4) {
+            const float4 ba = lds4(vb + j + c4), bg = lds4(vb + BN / 2 + j + c4);
+            float4 sa = make_float4(1.f, 1.f, 1.f, 1.f), sg = sa;
             if (W_I8) {
-              a *= __ldg(p.col_scale + nb + j + c);
-              g *= __ldg(p.col_scale + nb + BN / 2 + j + c);
+              sa = lds4(vs + j + c4);
+              sg = lds4(vs + BN / 2 + j + c4);
             }
-            a += __ldg(p.bias + nb + j + c);
-            g += __ldg(p.bias + nb + BN / 2 + j + c);
-            o[c] = a * sigmoid_fast(g);
+            const float bav[4] = {ba.x, ba.y, ba.z, ba.w}, bgv[4] = {bg.x, bg.y, bg.z, bg.w};
+            const float sav[4] = {sa.x, sa.y, sa.z, sa.w}, sgv[4] = {sg.x, sg.y, sg.z, sg.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float a = fmaf(__uint_as_float(va[c4 + c]), sav[c], bav[c]);
+              const float g = fmaf(__uint_as_float(vg[c4 + c]), sgv[c], bgv[c]);
+              o[c4 + c] = a * sigmoid_fast(g);
+            }
           }
           if (row_ok) store_bf16x16(orow + j, o);
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tempty[acc]);
       } else {
-        const int nb = n_blk * BN;
+        // residual row of this tile fetched before the accumulator is ready (hides the HBM latency)
+        uint4 res[BN / 8];
+        const bool has_res = p.residual != nullptr && row_ok;
+        const uint4* rsrc =
+            reinterpret_cast<const uint4*>(p.residual + (has_res ? (int64_t)row * p.ld_res + nb : 0));
+#pragma unroll
+        for (int i = 0; i < BN / 8; ++i) res[i] = has_res ? __ldg(rsrc + i) : make_uint4(0u, 0u, 0u, 0u);
+        int acc = 0;
+        uint32_t t_row = 0;
+        if (active) {
+          acc = local & 1;
+          const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+          ++local;
+          bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) break;
+          tc_fence_after();
+          t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+        }
         __nv_bfloat16* orow = p.out + (int64_t)row * p.ld_out + nb;
-        const __nv_bfloat16* rrow = p.residual + (p.residual ? (int64_t)row * p.ld_res + nb : 0);
-#pragma unroll 1
+#pragma unroll
         for (int j = 0; j < BN; j += 16) {
           uint32_t v[16];
-          tmem_ld16(t_row + (uint32_t)j, v);
-          uint4 r0 = make_uint4(0, 0, 0, 0), r1 = make_uint4(0, 0, 0, 0);
-          if (row_ok && p.residual != nullptr) {
-            r0 = __ldg(reinterpret_cast<const uint4*>(rrow + j));
-            r1 = __ldg(reinterpret_cast<const uint4*>(rrow + j) + 1);
+          if (active) {
+            tmem_ld16(t_row + (uint32_t)j, v);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) v[c] = 0u;   // padding rows: out = residual + bias
           }
-          tmem_wait_ld();
-          const uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+          const uint32_t rr[8] = {res[j / 8].x,     res[j / 8].y,     res[j / 8].z,     res[j / 8].w,
+                                  res[j / 8 + 1].x, res[j / 8 + 1].y, res[j / 8 + 1].z, res[j / 8 + 1].w};
           float o[16];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            float a = __uint_as_float(v[c]);
-            if (W_I8) a *= __ldg(p.col_scale + nb + j + c);
-            a += __ldg(p.bias + nb + j + c);
-            const float res = (c & 1) ? bf16hi_to_f32(rr[c >> 1]) : bf16lo_to_f32(rr[c >> 1]);
-            o[c] = a + res;
+          for (int c4 = 0; c4 < 16; c4 += 4) {
+            const float4 bb = lds4(vb + j + c4);
+            float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
+            if (W_I8) sc = lds4(vs + j + c4);
+            const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, sv[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int k = c4 + c;
+              const float r = (k & 1) ? bf16hi_to_f32(rr[k >> 1]) : bf16lo_to_f32(rr[k >> 1]);
+              o[k] = fmaf(__uint_as_float(v[k]), sv[c], bv[c]) + r;
+            }
           }
           if (row_ok) store_bf16x16(orow + j, o);
         }
+        if (active) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tempty[acc]);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.tempty[acc]);
     }
   } else if (W_I8) {
     // ---------------------------------------------------------------- int8 -> bf16 W converter (warps 6..9)
@@ -305,6 +378,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      if (!tile_active(p, tile / num_n)) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         bool got = mbar_wait_bounded(&s.full[stage], phase, abort_flag, kStatusTimeoutMma);
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -369,11 +443,13 @@ int launch_impl(const GemmArgs& a, cudaStream_t stream) {
   p.col_scale = a.col_scale;
   p.residual = a.residual;
   p.out = a.out;
+  p.lengths = a.lengths;
   p.ld_out = a.ld_out;
   p.ld_res = a.ld_res;
   p.M = a.M;
   p.N = a.N;
   p.K = a.K;
+  p.T = a.T;
   const int smem = (int)sizeof(Smem<W_I8>) + 1024;
   auto kern = gemm_kernel<EPI, W_I8>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

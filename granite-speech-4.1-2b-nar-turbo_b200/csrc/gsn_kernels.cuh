@@ -33,6 +33,8 @@ struct GemmArgs {
   int64_t ld_out, ld_res;
   int M, N, K;
   int w_int8;
+  const int* lengths;            // null, or per-utterance valid frames: 128-row tiles of pure padding are
+  int T;                         //   skipped (GLU) or written as residual + bias (RESIDUAL); needs T % 128 == 0
 };
 
 enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1 };
@@ -55,8 +57,10 @@ struct DwArgs {
 int launch_dwconv(const DwArgs& args, cudaStream_t stream);
 
 // ---- LayerNorm over the last dim (layernorm.cu) -------------------------------------------------------------
+// lengths (optional): rows r with r % T >= lengths[r / T] are padding and are skipped.
 int launch_layernorm(const __nv_bfloat16* x, int64_t ld_x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
-                     __nv_bfloat16* y, int64_t ld_y, int M, int D, float eps, cudaStream_t stream);
+                     __nv_bfloat16* y, int64_t ld_y, int M, int D, float eps, const int* lengths, int T,
+                     cudaStream_t stream);
 
 // ---- self-test of the bounded wait (capi.cu) ----------------------------------------------------------------
 int launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);

@@ -17,11 +17,15 @@ template <int V>  // V = D / 256 16-byte vectors per lane
 __global__ void __launch_bounds__(LN_WARPS * 32)
     layernorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, const __nv_bfloat16* __restrict__ gamma,
                      const __nv_bfloat16* __restrict__ beta, __nv_bfloat16* __restrict__ y, int64_t ld_y, int M,
-                     float eps) {
+                     float eps, const int* __restrict__ lengths, int T) {
   constexpr int D = V * 256;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * LN_WARPS + (threadIdx.x >> 5);
   if (row >= M) return;
+  if (lengths != nullptr) {               // padding frames: their LayerNorm output is never consumed
+    const int b = row / T;
+    if (row - b * T >= __ldg(lengths + b)) return;
+  }
   const __nv_bfloat16* xr = x + (int64_t)row * ld_x;
   float v[V][8];
 #pragma unroll
@@ -76,14 +80,15 @@ __global__ void __launch_bounds__(LN_WARPS * 32)
 using namespace ln_impl;
 
 int launch_layernorm(const __nv_bfloat16* x, int64_t ld_x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
-                     __nv_bfloat16* y, int64_t ld_y, int M, int D, float eps, cudaStream_t stream) {
+                     __nv_bfloat16* y, int64_t ld_y, int M, int D, float eps, const int* lengths, int T,
+                     cudaStream_t stream) {
   if (M == 0) return 0;
   const int grid = (M + LN_WARPS - 1) / LN_WARPS;
   switch (D) {
-    case 256: layernorm_kernel<1><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps); break;
-    case 512: layernorm_kernel<2><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps); break;
-    case 1024: layernorm_kernel<4><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps); break;
-    case 2048: layernorm_kernel<8><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps); break;
+    case 256: layernorm_kernel<1><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps, lengths, T); break;
+    case 512: layernorm_kernel<2><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps, lengths, T); break;
+    case 1024: layernorm_kernel<4><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps, lengths, T); break;
+    case 2048: layernorm_kernel<8><<<grid, LN_WARPS * 32, 0, stream>>>(x, ld_x, gamma, beta, y, ld_y, M, eps, lengths, T); break;
     default: return (int)cudaErrorInvalidValue;
   }
   return (int)cudaGetLastError();

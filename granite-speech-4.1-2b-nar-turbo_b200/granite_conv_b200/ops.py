@@ -192,40 +192,46 @@ def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, 
 
 
 # ---- single-kernel wrappers (tests, benchmarks) ---------------------------------------------------------------
-def layernorm(x2d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
-    _require_cuda("layernorm", x2d, w, b)
+def layernorm(x2d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5,
+              lengths: Optional[torch.Tensor] = None, T: int = 0) -> torch.Tensor:
+    """LayerNorm of bf16 rows [M, D]; with lengths (int32 [M / T]) padding rows are left unwritten."""
+    _require_cuda("layernorm", x2d, w, b, lengths)
     M, D = x2d.shape
     y = torch.empty_like(x2d)
     _lib.call("gsn_layernorm_bf16", x2d.data_ptr(), x2d.stride(0), w.data_ptr(), b.data_ptr(), y.data_ptr(),
-              y.stride(0), M, D, float(eps), _stream(x2d))
+              y.stride(0), M, D, float(eps), _ptr(lengths), T, _stream(x2d))
     return y
 
 
-def gemm1_glu(a: torch.Tensor, w_glu: torch.Tensor, b_glu: torch.Tensor, scale_glu: Optional[torch.Tensor] = None):
-    _require_cuda("gemm1_glu", a, w_glu, b_glu, scale_glu)
+def gemm1_glu(a: torch.Tensor, w_glu: torch.Tensor, b_glu: torch.Tensor, scale_glu: Optional[torch.Tensor] = None,
+              lengths: Optional[torch.Tensor] = None, T: int = 0) -> torch.Tensor:
+    """h = GLU(a @ W1^T + b1) from GLU-interleaved weights; with lengths, tiles of pure padding are skipped."""
+    _require_cuda("gemm1_glu", a, w_glu, b_glu, scale_glu, lengths)
     M, K = a.shape
     N = w_glu.shape[0]
     h = torch.empty((M, N // 2), dtype=torch.bfloat16, device=a.device)
     if scale_glu is None:
         _lib.call("gsn_gemm1_glu_bf16", a.data_ptr(), w_glu.data_ptr(), b_glu.data_ptr(), h.data_ptr(), M, K, N,
-                  _stream(a))
+                  _ptr(lengths), T, _stream(a))
     else:
         _lib.call("gsn_gemm1_glu_i8w", a.data_ptr(), w_glu.data_ptr(), scale_glu.data_ptr(), b_glu.data_ptr(),
-                  h.data_ptr(), M, K, N, _stream(a))
+                  h.data_ptr(), M, K, N, _ptr(lengths), T, _stream(a))
     return h
 
 
 def gemm2_residual(d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, residual: Optional[torch.Tensor],
-                   scale: Optional[torch.Tensor] = None) -> torch.Tensor:
-    _require_cuda("gemm2_residual", d, w, b, residual, scale)
+                   scale: Optional[torch.Tensor] = None, lengths: Optional[torch.Tensor] = None,
+                   T: int = 0) -> torch.Tensor:
+    """out = d @ W2^T + b2 (+ residual); with lengths, tiles of pure padding are written as residual + b2."""
+    _require_cuda("gemm2_residual", d, w, b, residual, scale, lengths)
     M, K = d.shape
     N = w.shape[0]
     out = torch.empty((M, N), dtype=torch.bfloat16, device=d.device)
     ld_res = residual.stride(0) if residual is not None else 0
     if scale is None:
         _lib.call("gsn_gemm2_residual_bf16", d.data_ptr(), w.data_ptr(), b.data_ptr(), _ptr(residual), ld_res,
-                  out.data_ptr(), out.stride(0), M, K, N, _stream(d))
+                  out.data_ptr(), out.stride(0), M, K, N, _ptr(lengths), T, _stream(d))
     else:
         _lib.call("gsn_gemm2_residual_i8w", d.data_ptr(), w.data_ptr(), scale.data_ptr(), b.data_ptr(),
-                  _ptr(residual), ld_res, out.data_ptr(), out.stride(0), M, K, N, _stream(d))
+                  _ptr(residual), ld_res, out.data_ptr(), out.stride(0), M, K, N, _ptr(lengths), T, _stream(d))
     return out

@@ -59,33 +59,39 @@ int gsn_dwconv_silu_glu_bf16(const void* x2, const void* weight, const void* bia
 
 /* ---- LayerNorm over the channel dim of channels-last rows ------------------------------------------------
  * Replaces ConformerConvModule.norm (script/models/granite_speech_nar/conformer.py:164, :176).  x, y: [M, D]
- * bf16 with row strides ld_x, ld_y (elements, multiples of 8); gamma, beta: [D] bf16; D in {256,512,1024,2048}. */
+ * bf16 with row strides ld_x, ld_y (elements, multiples of 8); gamma, beta: [D] bf16; D in {256,512,1024,2048}.
+ * lengths: NULL, or int32[M / T]: rows r with r % T >= lengths[r / T] are padding and are left unwritten. */
 int gsn_layernorm_bf16(const void* x, int64_t ld_x, const void* gamma, const void* beta, void* y, int64_t ld_y,
-                       int M, int D, float eps, gsn_stream_t stream);
+                       int M, int D, float eps, const int32_t* lengths, int T, gsn_stream_t stream);
 
 /* ---- pointwise_conv1 + GLU ------------------------------------------------------------------------------
  * Replaces up_conv + GLU (conformer.py:165-166, :177, :181): h[m, c] = v * sigmoid(g) with
  * v = (a[m,:] . W1[c,:]) + b1[c], g = (a[m,:] . W1[C+c,:]) + b1[C+c], C = N/2.
  * a: [M, K] bf16 contiguous; h: [M, N/2] bf16 contiguous.  w1_glu / b1_glu hold W1 and b1 with their rows
  * interleaved per 256-row block as [128 value rows | the matching 128 gate rows] (gsn_interleave_glu_rows).
- * K % 64 == 0, N % 256 == 0, pointers 16-byte aligned.  b1_glu is fp32. */
+ * K % 64 == 0, N % 256 == 0, pointers 16-byte aligned.  b1_glu is fp32.
+ * lengths: NULL, or int32[M / T] with T % 128 == 0: the rows are M / T utterances of T frames and 128-row tiles
+ * made only of padding frames (t >= lengths[b]) are skipped, their rows of h left unwritten. */
 int gsn_gemm1_glu_bf16(const void* a, const void* w1_glu, const float* b1_glu, void* h, int M, int K, int N,
-                       gsn_stream_t stream);
+                       const int32_t* lengths, int T, gsn_stream_t stream);
 
 /* int8-weight form: w1q_glu int8 [N, K] (interleaved), s1_glu fp32 [N] per-row scale (W1 ~= w1q * s1). */
 int gsn_gemm1_glu_i8w(const void* a, const void* w1q_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
-                      int K, int N, gsn_stream_t stream);
+                      int K, int N, const int32_t* lengths, int T, gsn_stream_t stream);
 
 /* ---- pointwise_conv2 + residual -------------------------------------------------------------------------
  * Replaces down_conv (conformer.py:170, :187) plus the block's residual add (conformer.py:207):
  * out[m, n] = (d[m,:] . W2[n,:]) + b2[n] + residual[m, n].  d: [M, K] bf16; residual, out: [M, N] bf16 with
  * row strides ld_res, ld_out (multiples of 8); residual may be NULL (no add).  K % 64 == 0, N % 256 == 0.
- * b2 is fp32. */
+ * b2 is fp32.  lengths / T as for gsn_gemm1_glu_bf16: 128-row tiles of pure padding skip the MMA and are written
+ * as residual + b2 (what a zero row of d gives). */
 int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, const void* residual, int64_t ld_res,
-                            void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream);
+                            void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths, int T,
+                            gsn_stream_t stream);
 
 int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, const float* b2, const void* residual,
-                           int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, gsn_stream_t stream);
+                           int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
+                           int T, gsn_stream_t stream);
 
 /* ---- whole conv module + residual -------------------------------------------------------------------------
  * Replaces ConformerConvModule.forward (conformer.py:175-189) followed by the residual add of

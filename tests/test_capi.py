@@ -1,0 +1,75 @@
+"""The C ABI without a GPU: the library loads, exports every function include/gsn_conv.h declares (and the ctypes
+table binds exactly those), and argument validation rejects bad calls before any CUDA work."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from granite_conv_b200 import _lib, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "gsn_conv.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(gsn_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = _declared()
+    assert len(names) >= 15
+    L = _lib.lib()
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in gsn_conv.h but not exported"
+    assert sorted(_lib.SIGNATURES) == names
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.library_path()], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\sT\s(gsn_[a-z0-9_]+)", out))
+    assert set(names) <= exported
+
+
+def test_version_and_workspace():
+    L = _lib.lib()
+    assert L.gsn_version() == 10000
+    assert L.gsn_conv_module_workspace_bytes(48, 1536, 1024, 2048) == 48 * 1536 * (2048 * 2 + 2048 * 2)
+    assert L.gsn_conv_module_workspace_bytes(0, 10, 1024, 2048) == 0
+
+
+def test_validation_without_gpu():
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)
+    # kernel size other than 15
+    rc = L.gsn_dwconv_silu_bf16(p, p, p, p, 1, 8, 8, 14, 64, 8, 1, 64, 8, 1, None, None)
+    assert rc == 2 and "kernel size 14" in _lib.last_error()
+    # GEMM shape constraints
+    assert L.gsn_gemm1_glu_bf16(p, p, p, p, 128, 100, 4096, None, 0, None) == 2
+    assert "multiple of 64" in _lib.last_error()
+    assert L.gsn_gemm2_residual_bf16(p, p, p, None, 0, p, 1024, 128, 2048, 1000, None, 0, None) == 2
+    assert L.gsn_layernorm_bf16(p, 768, p, p, p, 768, 4, 768, 1e-5, None, 0, None) == 2
+    # lengths need T on the 128-frame grid dividing M
+    assert L.gsn_gemm1_glu_bf16(p, p, p, p, 200, 1024, 4096, p, 100, None) == 2
+    assert "multiple of 128" in _lib.last_error()
+    # empty problems succeed without touching the device
+    assert L.gsn_dwconv_silu_bf16(None, None, None, None, 0, 8, 8, 15, 0, 0, 0, 0, 0, 0, None, None) == 0
+    assert L.gsn_gemm1_glu_bf16(None, None, None, None, 0, 1024, 4096, None, 0, None) == 0
+    assert L.gsn_conv_module_bf16(*([None] * 10), 1, None, 0, 16, 1024, 2048, 1e-5, None, 0, None) == 0
+    # workspace too small
+    rc = L.gsn_conv_module_bf16(*([p] * 10), 1, p, 2, 16, 1024, 2048, 1e-5, p, 100, None)
+    assert rc == 5 and "workspace" in _lib.last_error()
+    assert L.gsn_interleave_glu_rows(p, p, 100, 8, None) == 2
+    assert L.gsn_selftest_bounded_wait(0, None) == 1
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    x = torch.zeros(1, 8, 10, dtype=torch.bfloat16)
+    w = torch.zeros(8, 1, 15, dtype=torch.bfloat16)
+    b = torch.zeros(8, dtype=torch.bfloat16)
+    with pytest.raises(Exception):
+        torch.ops.granite.dwconv_silu(x, w, b)
+
+
+def test_build_is_current():
+    assert not build.needs_build()

@@ -57,7 +57,7 @@ def test_gemm2_strided_rows():
     from granite_conv_b200 import _lib
     dt, wt, bt = _t(d), _t(w), _t(b, torch.float32)
     _lib.call("gsn_gemm2_residual_bf16", dt.data_ptr(), wt.data_ptr(), bt.data_ptr(), res.data_ptr(), res.stride(0),
-              out.data_ptr(), out.stride(0), M, K, N, torch.cuda.current_stream().cuda_stream)
+              out.data_ptr(), out.stride(0), M, K, N, None, 0, torch.cuda.current_stream().cuda_stream)
     ref = O.bf16_round((O.pointwise(d, w, b) + rw[:, N:]).astype(np.float32))
     assert_bf16_close(out, ref, "gemm2 strided")
 
@@ -100,6 +100,38 @@ def test_gemm_shape_errors():
                       torch.zeros((256, 64), dtype=torch.bfloat16, device=DEV),
                       torch.zeros((256,), dtype=torch.float32, device=DEV))
     assert h.shape == (0, 128)
+
+
+def test_gemms_skip_padding_tiles():
+    """With lengths (T on the 128 grid): rows of tiles that hold valid frames match the dense result, GEMM2 tiles of
+    pure padding are residual + bias, and LayerNorm leaves padding rows untouched."""
+    T, lens = 384, np.array([384, 1, 129, 0, 256], dtype=np.int32)
+    B = lens.size
+    M, K1, N1, K2, N2 = B * T, 1024, 4096, 2048, 1024
+    a = _rand(1, (M, K1))
+    w1 = _rand(2, (N1, K1), std=0.05)
+    b1 = _rand(3, (N1,), std=0.02)
+    lt = torch.from_numpy(lens).to(DEV)
+    h_dense = ops.gemm1_glu(_t(a), glu_interleave(_t(w1)), glu_interleave(_t(b1, torch.float32)))
+    h_skip = ops.gemm1_glu(_t(a), glu_interleave(_t(w1)), glu_interleave(_t(b1, torch.float32)), lengths=lt, T=T)
+    d = _rand(4, (M, K2), std=0.5)
+    w2 = _rand(5, (N2, K2), std=0.05)
+    b2 = _rand(6, (N2,), std=0.02)
+    r = _rand(7, (M, N2))
+    o_dense = ops.gemm2_residual(_t(d), _t(w2), _t(b2, torch.float32), _t(r))
+    o_skip = ops.gemm2_residual(_t(d), _t(w2), _t(b2, torch.float32), _t(r), lengths=lt, T=T)
+    x = _rand(8, (M, 1024))
+    g, bt = _rand(9, (1024,), std=0.02) + 1.0, _rand(10, (1024,), std=0.02)
+    y_dense = ops.layernorm(_t(x), _t(O.bf16_round(g)), _t(bt))
+    y_skip = ops.layernorm(_t(x), _t(O.bf16_round(g)), _t(bt), lengths=lt, T=T)
+    for b, L in enumerate(lens):
+        rows = slice(b * T, b * T + ((int(L) + 127) // 128) * 128)
+        assert torch.equal(h_skip[rows], h_dense[rows]), f"gemm1 utt {b}"
+        assert torch.equal(o_skip[rows], o_dense[rows]), f"gemm2 utt {b}"
+        assert torch.equal(y_skip[b * T:b * T + int(L)], y_dense[b * T:b * T + int(L)]), f"layernorm utt {b}"
+        pad = slice(rows.stop, (b + 1) * T)
+        ref = O.bf16_round((r[pad] + b2[None, :]).astype(np.float32))
+        np.testing.assert_array_equal(o_skip[pad].float().cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("M,D", [(1, 1024), (37, 1024), (1000, 1024), (64, 256), (64, 512), (33, 2048)])
