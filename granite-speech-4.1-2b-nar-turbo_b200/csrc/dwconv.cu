@@ -110,8 +110,9 @@ __device__ __forceinline__ void stg_words(__nv_bfloat16* p, const uint32_t (&w)[
   }
 }
 
-// Position of the k-th tile walked by this CTA: work items are (utterance, channel tile, time segment) in that
-// order, dealt round-robin to the persistent CTAs; a segment is SEG consecutive time tiles.
+// Position of the k-th tile walked by this CTA: work items are (utterance, time segment, channel tile) with the
+// channel tile fastest, dealt round-robin to the persistent CTAs, so the CTAs running at the same time read whole
+// frame rows (all channel tiles of the same frames) from DRAM together; a segment is SEG consecutive time tiles.
 template <class Cfg>
 struct TileWalk {
   int item, sub;
@@ -121,10 +122,10 @@ struct TileWalk {
   }
   __device__ bool valid(const ClParams& p) const { return item < p.n_items; }
   __device__ void coords(const ClParams& p, int& b, int& c0, int& t0) const {
-    const int seg = item % p.n_seg;
-    const int rest = item / p.n_seg;
-    const int ct = rest % p.n_ct;
-    b = rest / p.n_ct;
+    const int ct = item % p.n_ct;
+    const int rest = item / p.n_ct;
+    const int seg = rest % p.n_seg;
+    b = rest / p.n_seg;
     c0 = ct * Cfg::CC;
     t0 = (seg * Cfg::SEG + sub) * Cfg::TT;
   }

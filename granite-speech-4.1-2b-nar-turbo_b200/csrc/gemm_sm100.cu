@@ -48,6 +48,7 @@ struct __align__(1024) Smem {
   uint8_t a[Cfg<W_I8>::STAGES][A_BYTES];
   uint8_t b[Cfg<W_I8>::STAGES][B_BYTES];
   uint8_t b8[W_I8 ? Cfg<W_I8>::STAGES : 1][W_I8 ? B8_BYTES : 16];
+  alignas(16) float ep_vec[4][2][BN];     // per epilogue warp: the tile's bias and scale columns (float4 reads)
   uint64_t full[Cfg<W_I8>::STAGES];
   uint64_t full_b[Cfg<W_I8>::STAGES];     // int8: converted W tile ready
   uint64_t empty[Cfg<W_I8>::STAGES];
@@ -56,8 +57,12 @@ struct __align__(1024) Smem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
-  float ep_vec[4][2][BN];                 // per epilogue warp: the tile's bias and scale columns
 };
+
+// float4 shared loads of the epilogue slices and TMA destinations need these alignments
+static_assert(offsetof(Smem<false>, ep_vec) % 16 == 0 && offsetof(Smem<true>, ep_vec) % 16 == 0, "ep_vec alignment");
+static_assert(offsetof(Smem<false>, b) % 1024 == 0 && offsetof(Smem<true>, b8) % 1024 == 0, "tile alignment");
+static_assert(sizeof(Smem<false>) + 1024 <= 232448 && sizeof(Smem<true>) + 1024 <= 232448, "shared memory size");
 
 struct KParams {
   const float* bias;
