@@ -6,21 +6,26 @@
 // Layout: A = activations [M, K] bf16 row-major (M = B*T frames, channels-last), W = weights [N, K] (the Conv1d
 // weight [N, K, 1] as stored), both K-major, so D = A * W^T accumulates in TMEM in fp32.
 //
-// Kernel shape: persistent, one CTA per SM (the shared-memory ring is sized so only one CTA fits, which also
-// guarantees the 512 TMEM columns are free), warp-specialised:
-//   warp 0      TMA producer: A tile 128x64 and W tile 256x64 per stage, 128-byte swizzle, 4-stage ring
-//   warp 1      TMEM allocator + single-thread UMMA issuer (M=128, N=256, K=16 per instruction)
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator, bias (+scale) (+GLU | +residual), bf16 stores
-//   warps 6-9   (int8 weights only) dequantise the staged int8 W tile into the swizzled bf16 layout
-// The accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of tile i overlaps the
-// main loop of tile i+1.  Tiles are visited N-fastest so the 16 (or 4) CTAs sharing an A row-block run at
-// the same time and read it from L2.  The epilogue keeps the tile's bias / scale columns in a per-warp shared
-// slice (broadcast reads) and, for the residual GEMM, fetches its row of the residual before it waits for the
-// accumulator, so the HBM latency of that read overlaps the main loop.
+// Two mainloops share one epilogue:
+//  * single CTA per SM (every dtype): warp 0 TMA producer (A 128x64 + W 256x64 per stage, 128-byte swizzle,
+//    4-stage ring), warp 1 TMEM allocator + single-thread UMMA issuer (M=128, N=256, K=16), warps 2-5 epilogue,
+//    warps 6-9 (int8 weights only) dequantise the staged int8 W tile into the swizzled bf16 layout;
+//  * CTA pairs (bf16 weights, compiled in with GSN_GEMM_PAIR=1): cta_group::2 MMA on 256 x 256 tiles, each CTA
+//    loading its own halves of A and W (32 KB per K-block), 6-stage ring.
+// Persistent grids; one CTA per SM (the shared-memory footprint guarantees it, and with it the 512 TMEM
+// columns); the accumulator is double-buffered in TMEM (2 x 256 columns) so the epilogue of tile i overlaps the
+// main loop of tile i+1.  Tiles are visited N-fastest so the CTAs sharing an A row-block run at the same time
+// and read it from L2.
 //
-// With per-utterance lengths (rows b*T .. b*T+T-1 belong to utterance b, T % 128 == 0), a 128-row tile made only
-// of padding frames is skipped by every role: the GLU GEMM leaves those rows unwritten (nothing downstream reads
-// them) and the residual GEMM writes them as residual + bias, which is what a zero row of A produces.
+// Epilogue: a warp owns 32 accumulator rows (its TMEM lane quarter).  It keeps the tile's bias / scale columns
+// in a shared slice (broadcast reads) and moves results through two 32 x 32 bf16 staging boxes in shared memory
+// with the 64-byte swizzle: the residual sub-tile arrives there by TMA (prefetched one sub-tile ahead), each
+// lane reads and overwrites its own row (conflict-free under the swizzle) and the box leaves by TMA store, so
+// global memory only sees full, coalesced tiles.
+//
+// With per-utterance lengths (rows b*T .. b*T+T-1 belong to utterance b, T % 128 == 0), 128-row blocks made only
+// of padding frames are skipped: the GLU GEMM leaves those rows unwritten (nothing downstream reads them) and the
+// residual GEMM writes them as residual + bias, which is what a zero row of A produces.
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
@@ -34,38 +39,9 @@ constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;      // 16 KB
 constexpr int B_BYTES = BN * BK * 2;      // 32 KB (bf16, swizzled)
 constexpr int B8_BYTES = BN * BK;         // 16 KB (int8 staging)
+constexpr int BOX = 32;                   // epilogue box: 32 rows x 32 columns bf16
+constexpr int BOX_BYTES = BOX * BOX * 2;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
-
-template <bool W_I8>
-struct Cfg {
-  static constexpr int STAGES = W_I8 ? 3 : 4;
-  static constexpr int THREADS = W_I8 ? 320 : 192;
-};
-
-template <bool W_I8>
-struct __align__(1024) Smem {
-  uint8_t a[Cfg<W_I8>::STAGES][A_BYTES];
-  uint8_t b[Cfg<W_I8>::STAGES][B_BYTES];
-  uint8_t b8[W_I8 ? Cfg<W_I8>::STAGES : 1][W_I8 ? B8_BYTES : 16];
-  alignas(1024) uint8_t stage[4][2][32 * 32 * 2];   // per epilogue warp: two 32 x 32 bf16 boxes, 64-byte swizzle
-  alignas(16) float ep_vec[4][2][BN];     // per epilogue warp: the tile's bias and scale columns (float4 reads)
-  uint64_t full[Cfg<W_I8>::STAGES];
-  uint64_t full_b[Cfg<W_I8>::STAGES];     // int8: converted W tile ready
-  uint64_t empty[Cfg<W_I8>::STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
-  uint64_t res_full[4][2];                // residual box landed in stage[warp][buffer]
-  uint64_t mma_done;
-  uint32_t tmem_base;
-  int abort_flag;
-};
-
-// float4 shared loads of the epilogue slices and TMA destinations need these alignments
-static_assert(offsetof(Smem<false>, ep_vec) % 16 == 0 && offsetof(Smem<true>, ep_vec) % 16 == 0, "ep_vec alignment");
-static_assert(offsetof(Smem<false>, stage) % 1024 == 0 && offsetof(Smem<true>, stage) % 1024 == 0, "stage alignment");
-static_assert(offsetof(Smem<false>, b) % 1024 == 0 && offsetof(Smem<true>, b8) % 1024 == 0, "tile alignment");
-static_assert(sizeof(Smem<false>) + 1024 <= 232448 && sizeof(Smem<true>) + 1024 <= 232448, "shared memory size");
 
 struct KParams {
   const float* bias;
@@ -78,30 +54,16 @@ struct KParams {
   int T;                                  // frames per utterance when lengths != null (T % 128 == 0)
 };
 
-// A 128-row tile lies inside one utterance (T % 128 == 0); it is inactive when every row is padding.
-__device__ __forceinline__ bool tile_active(const KParams& p, int m_blk) {
+// 128-row block `blk` of the M range holds at least one valid frame (a block lies inside one utterance)
+__device__ __forceinline__ bool rows_active(const KParams& p, int blk) {
+  const int row = blk * 128;
+  if (row >= p.M) return false;
   if (p.lengths == nullptr) return true;
-  const int row = m_blk * BM;
   const int b = row / p.T;
   return row - b * p.T < __ldg(p.lengths + b);
 }
 
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-
-__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
-  uint4 lo, hi;
-  lo.x = pack_bf16x2(v[0], v[1]);
-  lo.y = pack_bf16x2(v[2], v[3]);
-  lo.z = pack_bf16x2(v[4], v[5]);
-  lo.w = pack_bf16x2(v[6], v[7]);
-  hi.x = pack_bf16x2(v[8], v[9]);
-  hi.y = pack_bf16x2(v[10], v[11]);
-  hi.z = pack_bf16x2(v[12], v[13]);
-  hi.w = pack_bf16x2(v[14], v[15]);
-  uint4* d = reinterpret_cast<uint4*>(dst);
-  d[0] = lo;
-  d[1] = hi;
-}
 
 // Four signed int8 (one 32-bit word) -> two bf16x2 words, exactly.  Each byte is biased to unsigned
 // (v + 128), placed in the low mantissa bits of the fp32 2^23, and the bias 2^23 + 128 is subtracted; every
@@ -116,11 +78,224 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_
   hi = pack_bf16x2(f2, f3);
 }
 
+// Shared-memory area of the four epilogue warps.
+struct __align__(1024) EpiSmem {
+  uint8_t stage[4][2][BOX_BYTES];         // two staging boxes per warp, 64-byte swizzle
+  float vec[4][2][BN];                    // per warp: the tile's bias and scale columns
+  uint64_t res_full[4][2];                // residual box landed in stage[warp][buffer]
+};
+
+// ------------------------------------------------------------------------------------------------------------
+// Epilogue of one warp (state lives in registers; one object per epilogue warp).
+template <int EPI, bool W_I8>
+struct Epilogue {
+  static constexpr int NU = (EPI == kEpiGlu ? BN / 2 : BN) / BOX;   // 32-column output sub-tiles per tile
+  float* vb;
+  float* vs;
+  uint8_t* stage0;                        // stage box b at stage0 + b * BOX_BYTES
+  uint64_t* res0;                         // its barrier at res0 + b
+  const CUtensorMap* tmO;
+  const CUtensorMap* tmR;
+  bool has_res;
+  int lane, swz;
+  uint32_t su;                            // sub-tiles handled so far: buffer su & 1, its use count su >> 1
+
+  __device__ void init(EpiSmem& e, int ew, const CUtensorMap* o, const CUtensorMap* r, const KParams& p) {
+    vb = e.vec[ew][0];
+    vs = e.vec[ew][1];
+    stage0 = e.stage[ew][0];
+    res0 = &e.res_full[ew][0];
+    tmO = o;
+    tmR = r;
+    has_res = EPI == kEpiResidual && p.residual != nullptr;
+    lane = threadIdx.x & 31;
+    swz = (lane >> 1) & 3;
+    su = 0;
+  }
+
+  // The tile's 256 bias (and scale) values into the warp's slice.  For the GLU they are halved:
+  // a * sigmoid(g) = a' + a' * tanh(g') with a' = a / 2 and g' = g / 2 (exact scalings).
+  __device__ void load_vectors(const KParams& p, int nb) {
+    const float h = EPI == kEpiGlu ? 0.5f : 1.0f;
+    __syncwarp();
+    const float4* src = reinterpret_cast<const float4*>(p.bias + nb);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float4 b = __ldg(src + lane + 32 * i);
+      b.x *= h; b.y *= h; b.z *= h; b.w *= h;
+      reinterpret_cast<float4*>(vb)[lane + 32 * i] = b;
+      if (W_I8) {
+        float4 sc = __ldg(reinterpret_cast<const float4*>(p.col_scale + nb) + lane + 32 * i);
+        sc.x *= h; sc.y *= h; sc.z *= h; sc.w *= h;
+        reinterpret_cast<float4*>(vs)[lane + 32 * i] = sc;
+      }
+    }
+    __syncwarp();
+  }
+
+  __device__ void load_residual(uint32_t buf, int col, int row0) {
+    mbar_arrive_expect_tx(res0 + buf, BOX_BYTES);
+    tma_load_2d(stage0 + buf * BOX_BYTES, tmR, res0 + buf, col, row0);
+  }
+
+  // residual of the tile's first sub-tile, issued before the accumulator is waited for
+  __device__ void prefetch_first(int ocol0, int row0) {
+    if (has_res && lane == 0) {
+      bulk_wait_group_read<0>();          // the buffer's previous store has read it
+      load_residual(su & 1, ocol0, row0);
+    }
+  }
+
+  // Drain one tile: `t_row` is the TMEM address of this warp's accumulator rows (unused when !active, i.e. a
+  // residual tile of pure padding).  Returns false if a wait ran out.
+  __device__ bool run(int row0, int ocol0, bool active, uint32_t t_row, volatile int* abort_flag) {
+    for (int u = 0; u < NU; ++u, ++su) {
+      const uint32_t buf = su & 1;
+      uint8_t* sb = stage0 + buf * BOX_BYTES;
+      if (has_res) {
+        if (lane == 0 && u + 1 < NU) {    // prefetch the next residual sub-tile into the other buffer
+          bulk_wait_group_read<0>();
+          load_residual(buf ^ 1, ocol0 + (u + 1) * BOX, row0);
+        }
+      } else {
+        if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
+        __syncwarp();
+      }
+      float o[BOX];
+      if (EPI == kEpiGlu) {
+        // accumulator columns [0,128) = value channels, [128,256) = their gate channels
+        uint32_t va[2][16], vg[2][16];
+        tmem_ld16(t_row + (uint32_t)(u * BOX), va[0]);
+        tmem_ld16(t_row + (uint32_t)(u * BOX + 16), va[1]);
+        tmem_ld16(t_row + (uint32_t)(BN / 2 + u * BOX), vg[0]);
+        tmem_ld16(t_row + (uint32_t)(BN / 2 + u * BOX + 16), vg[1]);
+        tmem_wait_ld_dep(va[0], va[1]);
+        tmem_wait_ld_dep(vg[0], vg[1]);
+#pragma unroll
+        for (int c4 = 0; c4 < BOX; c4 += 4) {
+          const int j = u * BOX + c4;
+          const float4 ba = lds4(vb + j), bg = lds4(vb + BN / 2 + j);
+          float4 sa = make_float4(0.5f, 0.5f, 0.5f, 0.5f), sg = sa;
+          if (W_I8) {
+            sa = lds4(vs + j);
+            sg = lds4(vs + BN / 2 + j);
+          }
+          const float bav[4] = {ba.x, ba.y, ba.z, ba.w}, bgv[4] = {bg.x, bg.y, bg.z, bg.w};
+          const float sav[4] = {sa.x, sa.y, sa.z, sa.w}, sgv[4] = {sg.x, sg.y, sg.z, sg.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int k = c4 + c;
+            const float a = fmaf(__uint_as_float(va[k >> 4][k & 15]), sav[c], bav[c]);   // value / 2
+            const float g = fmaf(__uint_as_float(vg[k >> 4][k & 15]), sgv[c], bgv[c]);   // gate / 2
+            o[k] = fmaf(a, tanh_approx(g), a);
+          }
+        }
+      } else {
+        uint32_t v[2][16];
+        if (active) {
+          tmem_ld16(t_row + (uint32_t)(u * BOX), v[0]);
+          tmem_ld16(t_row + (uint32_t)(u * BOX + 16), v[1]);
+          tmem_wait_ld_dep(v[0], v[1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) v[0][c] = v[1][c] = 0u;   // padding rows: out = residual + bias
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < BOX; c4 += 4) {
+          const int j = u * BOX + c4;
+          const float4 bb = lds4(vb + j);
+          float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
+          if (W_I8) sc = lds4(vs + j);
+          const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, sv[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int k = c4 + c;
+            o[k] = fmaf(__uint_as_float(v[k >> 4][k & 15]), sv[c], bv[c]);
+          }
+        }
+        if (has_res) {
+          bool got = mbar_wait_bounded(res0 + buf, (su >> 1) & 1, abort_flag, kStatusTimeoutEpilogue);
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) return false;
+        }
+      }
+      // lane = row of the 32 x 32 box; 16-byte chunk c of the row sits at chunk c ^ ((row >> 1) & 3)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4* pc = reinterpret_cast<uint4*>(sb + lane * 64 + ((c ^ swz) << 4));
+        float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (has_res) {
+          const uint4 rv = *pc;
+          const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            r[2 * i] = bf16lo_to_f32(rw[i]);
+            r[2 * i + 1] = bf16hi_to_f32(rw[i]);
+          }
+        }
+        uint4 w;
+        w.x = pack_bf16x2(o[c * 8 + 0] + r[0], o[c * 8 + 1] + r[1]);
+        w.y = pack_bf16x2(o[c * 8 + 2] + r[2], o[c * 8 + 3] + r[3]);
+        w.z = pack_bf16x2(o[c * 8 + 4] + r[4], o[c * 8 + 5] + r[5]);
+        w.w = pack_bf16x2(o[c * 8 + 6] + r[6], o[c * 8 + 7] + r[7]);
+        *pc = w;
+      }
+      fence_proxy_async_smem();          // the generic-proxy writes are visible to the TMA store
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmO, sb, ocol0 + u * BOX, row0);
+        bulk_commit_group();
+      }
+    }
+    return true;
+  }
+
+  __device__ void finish() {
+    if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed before the CTA ends
+    __syncwarp();
+  }
+};
+
+__device__ __forceinline__ void init_epi_barriers(EpiSmem& e) {
+  for (int w = 0; w < 4; ++w) {
+    mbar_init(&e.res_full[w][0], 1);
+    mbar_init(&e.res_full[w][1], 1);
+  }
+}
+
+// ================================================================================================================
+// single CTA per SM
+template <bool W_I8>
+struct Cfg {
+  static constexpr int STAGES = W_I8 ? 3 : 4;
+  static constexpr int THREADS = W_I8 ? 320 : 192;
+};
+
+template <bool W_I8>
+struct __align__(1024) Smem {
+  uint8_t a[Cfg<W_I8>::STAGES][A_BYTES];
+  uint8_t b[Cfg<W_I8>::STAGES][B_BYTES];
+  uint8_t b8[W_I8 ? Cfg<W_I8>::STAGES : 1][W_I8 ? B8_BYTES : 16];
+  EpiSmem epi;
+  uint64_t full[Cfg<W_I8>::STAGES];
+  uint64_t full_b[Cfg<W_I8>::STAGES];     // int8: converted W tile ready
+  uint64_t empty[Cfg<W_I8>::STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(offsetof(Smem<false>, b) % 1024 == 0 && offsetof(Smem<true>, b8) % 1024 == 0, "tile alignment");
+static_assert(offsetof(Smem<false>, epi) % 1024 == 0 && offsetof(Smem<true>, epi) % 1024 == 0, "box alignment");
+static_assert(sizeof(Smem<false>) + 1024 <= 232448 && sizeof(Smem<true>) + 1024 <= 232448, "shared memory size");
+
 template <int EPI, bool W_I8>
 __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, KParams p) {
   constexpr int STAGES = Cfg<W_I8>::STAGES;
+  constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
   extern __shared__ uint8_t smem_raw[];
   Smem<W_I8>& s =
       *reinterpret_cast<Smem<W_I8>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -142,10 +317,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], 4);
     }
-    for (int w = 0; w < 4; ++w) {
-      mbar_init(&s.res_full[w][0], 1);
-      mbar_init(&s.res_full[w][1], 1);
-    }
+    init_epi_barriers(s.epi);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -175,7 +347,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const int m_blk = tile / num_n;
       const int n_blk = tile - m_blk * num_n;
-      if (!tile_active(p, m_blk)) continue;
+      if (!rows_active(p, m_blk)) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         bool got = mbar_wait_bounded(&s.empty[stage], phase ^ 1u, abort_flag, kStatusTimeoutProducer);
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -218,7 +390,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     bool ok = true;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      if (!tile_active(p, tile / num_n)) continue;
+      if (!rows_active(p, tile / num_n)) continue;
       const int acc = local & 1;
       const uint32_t use_par = (uint32_t)((local >> 1) & 1);
       ++local;
@@ -263,45 +435,20 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     mbar_wait_bounded(&s.mma_done, 0, nullptr, kStatusTimeoutMma, 100000000ull);
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
-    // A warp owns 32 rows (its TMEM lane quarter) and moves its results through two 32 x 32 bf16 staging buffers
-    // in shared memory with the 64-byte swizzle: the residual sub-tile arrives there by TMA (prefetched one
-    // sub-tile ahead), each lane reads and overwrites its own row (conflict-free under the swizzle) and the buffer
-    // leaves by TMA store, so global memory only sees full, coalesced tiles.
     const int q = warp & 3;           // a warp may only read its own 32-lane quarter of TMEM
-    const int ew = warp - 2;
-    float* vb = s.ep_vec[ew][0];
-    float* vs = s.ep_vec[ew][1];
-    constexpr int NU = (EPI == kEpiGlu ? BN / 2 : BN) / 32;   // 32-column output sub-tiles per tile
-    const bool has_res = EPI == kEpiResidual && p.residual != nullptr;
-    const int swz = (lane >> 1) & 3;  // 64-byte swizzle of this lane's 64-byte row
-    uint32_t su = 0;                  // sub-tiles handled so far: buffer su & 1, its use count su >> 1
+    Epilogue<EPI, W_I8> epi;
+    epi.init(s.epi, warp - 2, &tmO, &tmR, p);
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m_blk = tile / num_n;
       const int n_blk = tile - m_blk * num_n;
-      const bool active = tile_active(p, m_blk);
+      const bool active = rows_active(p, m_blk);
       if (EPI == kEpiGlu && !active) continue;   // GLU rows of padding frames are never read downstream
       const int nb = n_blk * BN;
-      // this tile's 256 bias (and scale) values into the warp's own shared slice
-      __syncwarp();
-      {
-        const float4* src = reinterpret_cast<const float4*>(p.bias + nb);
-        reinterpret_cast<float4*>(vb)[lane] = __ldg(src + lane);
-        reinterpret_cast<float4*>(vb)[lane + 32] = __ldg(src + lane + 32);
-        if (W_I8) {
-          const float4* ss = reinterpret_cast<const float4*>(p.col_scale + nb);
-          reinterpret_cast<float4*>(vs)[lane] = __ldg(ss + lane);
-          reinterpret_cast<float4*>(vs)[lane + 32] = __ldg(ss + lane + 32);
-        }
-      }
-      __syncwarp();
+      epi.load_vectors(p, nb);
       const int row0 = m_blk * BM + q * 32;
       const int ocol0 = EPI == kEpiGlu ? n_blk * (BN / 2) : nb;
-      if (has_res && lane == 0) {       // residual of the first sub-tile (its buffer's last store has been read)
-        bulk_wait_group_read<0>();
-        mbar_arrive_expect_tx(&s.res_full[ew][su & 1], 32 * 32 * 2);
-        tma_load_2d(s.stage[ew][su & 1], &tmR, &s.res_full[ew][su & 1], ocol0, row0);
-      }
+      epi.prefetch_first(ocol0, row0);
       int acc = 0;
       uint32_t t_row = 0;
       if (active) {
@@ -314,109 +461,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
         tc_fence_after();
         t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       }
-      bool ok = true;
-      for (int u = 0; u < NU; ++u, ++su) {
-        const uint32_t buf = su & 1;
-        uint8_t* sb = s.stage[ew][buf];
-        if (has_res) {
-          if (lane == 0 && u + 1 < NU) {  // prefetch the next residual sub-tile into the other buffer
-            bulk_wait_group_read<0>();
-            mbar_arrive_expect_tx(&s.res_full[ew][buf ^ 1], 32 * 32 * 2);
-            tma_load_2d(s.stage[ew][buf ^ 1], &tmR, &s.res_full[ew][buf ^ 1], ocol0 + (u + 1) * 32, row0);
-          }
-        } else {
-          if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
-          __syncwarp();
-        }
-        float o[32];
-        if (EPI == kEpiGlu) {
-          // accumulator columns [0,128) = value channels, [128,256) = their gate channels
-          uint32_t va[2][16], vg[2][16];
-          tmem_ld16(t_row + (uint32_t)(u * 32), va[0]);
-          tmem_ld16(t_row + (uint32_t)(u * 32 + 16), va[1]);
-          tmem_ld16(t_row + (uint32_t)(BN / 2 + u * 32), vg[0]);
-          tmem_ld16(t_row + (uint32_t)(BN / 2 + u * 32 + 16), vg[1]);
-          tmem_wait_ld_dep(va[0], va[1]);
-          tmem_wait_ld_dep(vg[0], vg[1]);
-#pragma unroll
-          for (int c4 = 0; c4 < 32; c4 += 4) {
-            const int j = u * 32 + c4;
-            const float4 ba = lds4(vb + j), bg = lds4(vb + BN / 2 + j);
-            float4 sa = make_float4(1.f, 1.f, 1.f, 1.f), sg = sa;
-            if (W_I8) {
-              sa = lds4(vs + j);
-              sg = lds4(vs + BN / 2 + j);
-            }
-            const float bav[4] = {ba.x, ba.y, ba.z, ba.w}, bgv[4] = {bg.x, bg.y, bg.z, bg.w};
-            const float sav[4] = {sa.x, sa.y, sa.z, sa.w}, sgv[4] = {sg.x, sg.y, sg.z, sg.w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int k = c4 + c;
-              const float a = fmaf(__uint_as_float(va[k >> 4][k & 15]), sav[c], bav[c]);
-              const float g = fmaf(__uint_as_float(vg[k >> 4][k & 15]), sgv[c], bgv[c]);
-              o[k] = a * sigmoid_fast(g);
-            }
-          }
-        } else {
-          uint32_t v[2][16];
-          if (active) {
-            tmem_ld16(t_row + (uint32_t)(u * 32), v[0]);
-            tmem_ld16(t_row + (uint32_t)(u * 32 + 16), v[1]);
-            tmem_wait_ld_dep(v[0], v[1]);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 16; ++c) v[0][c] = v[1][c] = 0u;   // padding rows: out = residual + bias
-          }
-#pragma unroll
-          for (int c4 = 0; c4 < 32; c4 += 4) {
-            const int j = u * 32 + c4;
-            const float4 bb = lds4(vb + j);
-            float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
-            if (W_I8) sc = lds4(vs + j);
-            const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, sv[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int k = c4 + c;
-              o[k] = fmaf(__uint_as_float(v[k >> 4][k & 15]), sv[c], bv[c]);
-            }
-          }
-          if (has_res) {
-            bool got = mbar_wait_bounded(&s.res_full[ew][buf], (su >> 1) & 1, abort_flag, kStatusTimeoutEpilogue);
-            got = __shfl_sync(0xffffffffu, got, 0);
-            if (!got) {
-              ok = false;
-              break;
-            }
-          }
-        }
-        // lane = row of the 32 x 32 box; 16-byte chunk c of the row sits at chunk c ^ ((row >> 1) & 3)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4* pc = reinterpret_cast<uint4*>(sb + lane * 64 + ((c ^ swz) << 4));
-          float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (has_res) {
-            const uint4 rv = *pc;
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              r[2 * i] = bf16lo_to_f32(rw[i]);
-              r[2 * i + 1] = bf16hi_to_f32(rw[i]);
-            }
-          }
-          uint4 w;
-          w.x = pack_bf16x2(o[c * 8 + 0] + r[0], o[c * 8 + 1] + r[1]);
-          w.y = pack_bf16x2(o[c * 8 + 2] + r[2], o[c * 8 + 3] + r[3]);
-          w.z = pack_bf16x2(o[c * 8 + 4] + r[4], o[c * 8 + 5] + r[5]);
-          w.w = pack_bf16x2(o[c * 8 + 6] + r[6], o[c * 8 + 7] + r[7]);
-          *pc = w;
-        }
-        fence_proxy_async_smem();      // the generic-proxy writes are visible to the TMA store
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmO, sb, ocol0 + u * 32, row0);
-          bulk_commit_group();
-        }
-      }
+      const bool ok = epi.run(row0, ocol0, active, t_row, abort_flag);
       if (active) {
         tc_fence_before();
         __syncwarp();
@@ -424,8 +469,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
       }
       if (!ok) break;
     }
-    if (lane == 0) bulk_wait_group<0>();   // every store of this warp has landed before the CTA ends
-    __syncwarp();
+    epi.finish();
   } else if (W_I8) {
     // ---------------------------------------------------------------- int8 -> bf16 W converter (warps 6..9)
     const int ct = threadIdx.x - 192;  // 0..127
@@ -433,7 +477,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      if (!tile_active(p, tile / num_n)) continue;
+      if (!rows_active(p, tile / num_n)) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         bool got = mbar_wait_bounded(&s.full[stage], phase, abort_flag, kStatusTimeoutMma);
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -474,77 +518,13 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   }
 }
 
-template <int EPI, bool W_I8>
-int launch_impl(const GemmArgs& a, cudaStream_t stream) {
-  CUtensorMap tmA, tmW;
-  {
-    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
-    const uint64_t strides[1] = {(uint64_t)a.K * 2};
-    const uint32_t box[2] = {BK, BM};
-    int rc = encode_tmap(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
-    const uint64_t strides[1] = {(uint64_t)a.K * (W_I8 ? 1 : 2)};
-    const uint32_t box[2] = {BK, BN};
-    int rc = encode_tmap(&tmW, W_I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w,
-                         dims, strides, box, W_I8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  // output (and residual) moved as 32 x 32 bf16 boxes with the 64-byte swizzle
-  CUtensorMap tmO, tmR;
-  {
-    const uint64_t dims[2] = {(uint64_t)(EPI == kEpiGlu ? a.N / 2 : a.N), (uint64_t)a.M};
-    const uint64_t strides[1] = {(uint64_t)a.ld_out * 2};
-    const uint32_t box[2] = {32, 32};
-    int rc = encode_tmap(&tmO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.out, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_64B);
-    if (rc) return rc;
-  }
-  if (EPI == kEpiResidual && a.residual != nullptr) {
-    const uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M};
-    const uint64_t strides[1] = {(uint64_t)a.ld_res * 2};
-    const uint32_t box[2] = {32, 32};
-    int rc = encode_tmap(&tmR, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.residual, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_64B);
-    if (rc) return rc;
-  } else {
-    tmR = tmO;   // never read
-  }
-  KParams p;
-  p.bias = a.bias;
-  p.col_scale = a.col_scale;
-  p.residual = a.residual;
-  p.out = a.out;
-  p.lengths = a.lengths;
-  p.ld_out = a.ld_out;
-  p.ld_res = a.ld_res;
-  p.M = a.M;
-  p.N = a.N;
-  p.K = a.K;
-  p.T = a.T;
-  const int smem = (int)sizeof(Smem<W_I8>) + 1024;
-  auto kern = gemm_kernel<EPI, W_I8>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return (int)e;
-  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
-  const int sms = device_sm_count();
-  const int grid = tiles < sms ? tiles : sms;
-  if (grid <= 0) return 0;
-  kern<<<grid, Cfg<W_I8>::THREADS, smem, stream>>>(tmA, tmW, tmO, tmR, p);
-  return (int)cudaGetLastError();
-}
-
 // ================================================================================================================
 // bf16 weights on CTA pairs: cta_group::2 MMA, 256 x 256 tiles per pair.
 //
 // The two CTAs of a cluster share one 256 x 256 output tile.  Each CTA loads its own half of A (128 rows) and its
-// own half of W (128 rows) per K-block (16 KB + 16 KB, i.e. a third less operand traffic per SM than a 128 x 256
-// tile on one SM), so a 6-stage ring fits.  The even CTA issues one M=256, N=256, K=16 MMA per slice that reads
-// both CTAs' shared memory and writes both CTAs' TMEM (rows 0-127 in the even CTA, 128-255 in the odd one); each
-// CTA's epilogue then drains its own 128 rows exactly as in the single-CTA kernel.  Synchronisation:
+// own half of W (128 rows) per K-block (16 KB + 16 KB), so a 6-stage ring fits.  The even CTA issues one M=256,
+// N=256, K=16 MMA per slice that reads both CTAs' shared memory and writes both CTAs' TMEM (rows 0-127 in the
+// even CTA, 128-255 in the odd one); each CTA's epilogue then drains its own 128 rows.  Synchronisation:
 //   full[s]   (even CTA)  both CTAs' TMA bytes of stage s; armed by the even CTA's producer
 //   empty[s]  (each CTA)  the pair's MMAs reading stage s completed (two commits from the even CTA)
 //   tfull[a]  (each CTA)  accumulator buffer a complete (two commits)
@@ -554,12 +534,11 @@ namespace pair_impl {
 
 constexpr int STAGES = 6;
 constexpr int HALF_BYTES = 128 * BK * 2;      // 16 KB: half of A or half of W per K-block
-constexpr uint32_t IDESC = make_idesc_bf16_f32(256, 256);
 
 struct __align__(1024) Smem {
   uint8_t a[STAGES][HALF_BYTES];
   uint8_t b[STAGES][HALF_BYTES];
-  alignas(16) float ep_vec[4][BN];        // per epilogue warp: the tile's bias columns
+  EpiSmem epi;
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tfull[2];
@@ -568,21 +547,14 @@ struct __align__(1024) Smem {
   uint32_t tmem_base;
   int abort_flag;
 };
-static_assert(offsetof(Smem, ep_vec) % 16 == 0 && offsetof(Smem, b) % 1024 == 0, "alignment");
+static_assert(offsetof(Smem, epi) % 1024 == 0 && offsetof(Smem, b) % 1024 == 0, "alignment");
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory size");
-
-// 128-row half h of the M range holds at least one valid frame
-__device__ __forceinline__ bool half_active(const KParams& p, int h) {
-  const int row = h * 128;
-  if (row >= p.M) return false;
-  if (p.lengths == nullptr) return true;
-  const int b = row / p.T;
-  return row - b * p.T < __ldg(p.lengths + b);
-}
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, KParams p) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, KParams p) {
+  constexpr uint32_t IDESC = make_idesc_bf16_f32(256, 256);
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -605,6 +577,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], 8);
     }
+    init_epi_barriers(s.epi);
     mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -612,6 +585,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc_pair(&s.tmem_base, TMEM_COLS);
@@ -622,7 +596,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
-  auto pair_active = [&](int mp) { return half_active(p, 2 * mp) || half_active(p, 2 * mp + 1); };
+  auto pair_active = [&](int mp) { return rows_active(p, 2 * mp) || rows_active(p, 2 * mp + 1); };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
@@ -722,7 +696,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5, both CTAs)
     const int q = warp & 3;
-    float* vb = s.ep_vec[warp - 2];
+    Epilogue<EPI, false> epi;
+    epi.init(s.epi, warp - 2, &tmO, &tmR, p);
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += n_pairs) {
       const int mp = tile / num_n;
@@ -730,117 +705,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const bool active = pair_active(mp);
       if (EPI == kEpiGlu && !active) continue;
       const int nb = n_blk * BN;
-      __syncwarp();
-      {
-        const float4* src = reinterpret_cast<const float4*>(p.bias + nb);
-        reinterpret_cast<float4*>(vb)[lane] = __ldg(src + lane);
-        reinterpret_cast<float4*>(vb)[lane + 32] = __ldg(src + lane + 32);
-      }
-      __syncwarp();
-      const int row = mp * 256 + (int)rank * 128 + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      const uint32_t tempty0 = mapa_shared(smem_u32(&s.tempty[local & 1]), 0);
-
-      if (EPI == kEpiGlu) {
-        const int acc = local & 1;
+      epi.load_vectors(p, nb);
+      const int row0 = mp * 256 + (int)rank * 128 + q * 32;
+      const int ocol0 = EPI == kEpiGlu ? n_blk * (BN / 2) : nb;
+      epi.prefetch_first(ocol0, row0);
+      int acc = 0;
+      uint32_t t_row = 0;
+      if (active) {
+        acc = local & 1;
         const uint32_t use_par = (uint32_t)((local >> 1) & 1);
         ++local;
         bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
         got = __shfl_sync(0xffffffffu, got, 0);
         if (!got) break;
         tc_fence_after();
-        const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-        __nv_bfloat16* orow = p.out + (int64_t)row * p.ld_out + (int64_t)n_blk * (BN / 2);
-        uint32_t va[2][16], vg[2][16];
-        tmem_ld16(t_row, va[0]);
-        tmem_ld16(t_row + (uint32_t)(BN / 2), vg[0]);
-        tmem_wait_ld_dep(va[0], vg[0]);
-#pragma unroll
-        for (int jj = 0; jj < BN / 32; ++jj) {   // 8 chunks of 16 value + 16 gate columns
-          const int cur = jj & 1;
-          const int j = jj * 16;
-          if (jj + 1 < BN / 32) {                 // next chunk's TMEM loads overlap this chunk's math
-            tmem_ld16(t_row + (uint32_t)(j + 16), va[cur ^ 1]);
-            tmem_ld16(t_row + (uint32_t)(BN / 2 + j + 16), vg[cur ^ 1]);
-          }
-          float o[16];
-#pragma unroll
-          for (int c4 = 0; c4 < 16; c4 += 4) {
-            const float4 ba = lds4(vb + j + c4), bg = lds4(vb + BN / 2 + j + c4);
-            const float bav[4] = {ba.x, ba.y, ba.z, ba.w}, bgv[4] = {bg.x, bg.y, bg.z, bg.w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const float a = __uint_as_float(va[cur][c4 + c]) + bav[c];
-              const float g = __uint_as_float(vg[cur][c4 + c]) + bgv[c];
-              o[c4 + c] = a * sigmoid_fast(g);
-            }
-          }
-          if (row_ok) store_bf16x16(orow + j, o);
-          if (jj + 1 < BN / 32) tmem_wait_ld_dep(va[cur ^ 1], vg[cur ^ 1]);
-        }
+        t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      }
+      const bool ok = epi.run(row0, ocol0, active, t_row, abort_flag);
+      if (active) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(tempty0);
-      } else {
-        uint4 res[BN / 8];
-        const bool has_res = p.residual != nullptr && row_ok;
-        const uint4* rsrc =
-            reinterpret_cast<const uint4*>(p.residual + (has_res ? (int64_t)row * p.ld_res + nb : 0));
-#pragma unroll
-        for (int i = 0; i < BN / 8; ++i) res[i] = has_res ? __ldg(rsrc + i) : make_uint4(0u, 0u, 0u, 0u);
-        uint32_t t_row = 0;
-        if (active) {
-          const int acc = local & 1;
-          const uint32_t use_par = (uint32_t)((local >> 1) & 1);
-          ++local;
-          bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
-          got = __shfl_sync(0xffffffffu, got, 0);
-          if (!got) break;
-          tc_fence_after();
-          t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-        }
-        __nv_bfloat16* orow = p.out + (int64_t)row * p.ld_out + nb;
-        uint32_t v[2][16];
-        if (active) {
-          tmem_ld16(t_row, v[0]);
-          tmem_ld16(t_row + 16u, v[1]);
-          tmem_wait_ld_dep(v[0], v[1]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 16; ++c) v[0][c] = v[1][c] = 0u;   // padding rows: out = residual + bias
-        }
-#pragma unroll
-        for (int jj = 0; jj < BN / 16; ++jj) {     // 16 chunks of 16 columns, loaded two at a time
-          const int cur = jj & 1;
-          const int j = jj * 16;
-          const uint32_t rr[8] = {res[j / 8].x,     res[j / 8].y,     res[j / 8].z,     res[j / 8].w,
-                                  res[j / 8 + 1].x, res[j / 8 + 1].y, res[j / 8 + 1].z, res[j / 8 + 1].w};
-          float o[16];
-#pragma unroll
-          for (int c4 = 0; c4 < 16; c4 += 4) {
-            const float4 bb = lds4(vb + j + c4);
-            const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int k = c4 + c;
-              const float r = (k & 1) ? bf16hi_to_f32(rr[k >> 1]) : bf16lo_to_f32(rr[k >> 1]);
-              o[k] = __uint_as_float(v[cur][k]) + bv[c] + r;
-            }
-          }
-          if (row_ok) store_bf16x16(orow + j, o);
-          if (active && cur == 1 && jj + 1 < BN / 16) {   // both buffers consumed: load the next two chunks
-            tmem_ld16(t_row + (uint32_t)(j + 16), v[0]);
-            tmem_ld16(t_row + (uint32_t)(j + 32), v[1]);
-            tmem_wait_ld_dep(v[0], v[1]);
-          }
-        }
-        if (active) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty0);
-        }
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.tempty[acc]), 0));
       }
+      if (!ok) break;
     }
+    epi.finish();
   }
 
   tc_fence_before();
@@ -849,6 +738,83 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
+}
+
+}  // namespace pair_impl
+
+// ------------------------------------------------------------------------------------------------------------
+// host side
+int encode_operands(const GemmArgs& a, int epilogue, int a_rows, int w_rows, CUtensorMap* tmA, CUtensorMap* tmW,
+                    CUtensorMap* tmO, CUtensorMap* tmR) {
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
+    const uint64_t strides[1] = {(uint64_t)a.K * 2};
+    const uint32_t box[2] = {BK, (uint32_t)a_rows};
+    int rc = encode_tmap(tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
+    const uint64_t strides[1] = {(uint64_t)a.K * (a.w_int8 ? 1 : 2)};
+    const uint32_t box[2] = {BK, (uint32_t)w_rows};
+    int rc = encode_tmap(tmW, a.w_int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w,
+                         dims, strides, box, a.w_int8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    // output (and residual) move as 32 x 32 bf16 boxes with the 64-byte swizzle
+    const uint64_t dims[2] = {(uint64_t)(epilogue == kEpiGlu ? a.N / 2 : a.N), (uint64_t)a.M};
+    const uint64_t strides[1] = {(uint64_t)a.ld_out * 2};
+    const uint32_t box[2] = {BOX, BOX};
+    int rc = encode_tmap(tmO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.out, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  }
+  if (epilogue == kEpiResidual && a.residual != nullptr) {
+    const uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M};
+    const uint64_t strides[1] = {(uint64_t)a.ld_res * 2};
+    const uint32_t box[2] = {BOX, BOX};
+    int rc = encode_tmap(tmR, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.residual, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  } else {
+    *tmR = *tmO;   // never read
+  }
+  return 0;
+}
+
+KParams make_params(const GemmArgs& a) {
+  KParams p;
+  p.bias = a.bias;
+  p.col_scale = a.col_scale;
+  p.residual = a.residual;
+  p.out = a.out;
+  p.lengths = a.lengths;
+  p.ld_out = a.ld_out;
+  p.ld_res = a.ld_res;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.T = a.T;
+  return p;
+}
+
+template <int EPI, bool W_I8>
+int launch_single(const GemmArgs& a, cudaStream_t stream) {
+  CUtensorMap tmA, tmW, tmO, tmR;
+  if (int rc = encode_operands(a, EPI, BM, BN, &tmA, &tmW, &tmO, &tmR)) return rc;
+  const KParams p = make_params(a);
+  const int smem = (int)sizeof(Smem<W_I8>) + 1024;
+  auto kern = gemm_kernel<EPI, W_I8>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  const int sms = device_sm_count();
+  const int grid = tiles < sms ? tiles : sms;
+  if (grid <= 0) return 0;
+  kern<<<grid, Cfg<W_I8>::THREADS, smem, stream>>>(tmA, tmW, tmO, tmR, p);
+  return (int)cudaGetLastError();
 }
 
 // Number of CTA pairs that can be resident at once (0 if the pair kernel cannot be scheduled).
@@ -870,7 +836,7 @@ int resident_pairs(int smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<EPI>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, pair_impl::gemm_pair_kernel<EPI>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -878,62 +844,32 @@ int resident_pairs(int smem) {
   return n;
 }
 
+// Returns with *launched = false (and status 0) when no CTA pair can be scheduled.
 template <int EPI>
 int launch_pair(const GemmArgs& a, cudaStream_t stream, bool* launched) {
   *launched = false;
-  const int smem = (int)sizeof(Smem) + 1024;
-  auto kern = gemm_pair_kernel<EPI>;
+  const int smem = (int)sizeof(pair_impl::Smem) + 1024;
+  auto kern = pair_impl::gemm_pair_kernel<EPI>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int pairs = resident_pairs<EPI>(smem);
-  if (pairs <= 0) return 0;                    // caller runs the single-CTA kernel instead
-  CUtensorMap tmA, tmW;
-  {
-    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
-    const uint64_t strides[1] = {(uint64_t)a.K * 2};
-    const uint32_t box[2] = {BK, 128};
-    int rc = encode_tmap(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
-    const uint64_t strides[1] = {(uint64_t)a.K * 2};
-    const uint32_t box[2] = {BK, 128};
-    int rc = encode_tmap(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w, dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  KParams p;
-  p.bias = a.bias;
-  p.col_scale = nullptr;
-  p.residual = a.residual;
-  p.out = a.out;
-  p.lengths = a.lengths;
-  p.ld_out = a.ld_out;
-  p.ld_res = a.ld_res;
-  p.M = a.M;
-  p.N = a.N;
-  p.K = a.K;
-  p.T = a.T;
+  if (pairs <= 0) return 0;
+  CUtensorMap tmA, tmW, tmO, tmR;
+  if (int rc = encode_operands(a, EPI, 128, 128, &tmA, &tmW, &tmO, &tmR)) return rc;
+  const KParams p = make_params(a);
   const int tiles = ((a.M + 255) / 256) * (a.N / BN);
   const int n = tiles < pairs ? tiles : pairs;
-  if (n <= 0) {
-    *launched = true;
-    return 0;
-  }
-  kern<<<2 * n, 192, smem, stream>>>(tmA, tmW, p);
   *launched = true;
+  if (n <= 0) return 0;
+  kern<<<2 * n, 192, smem, stream>>>(tmA, tmW, tmO, tmR, p);
   return (int)cudaGetLastError();
 }
-
-}  // namespace pair_impl
 
 }  // namespace gemm_impl
 using namespace gemm_impl;
 
-// The CTA-pair mainloop matches the single-CTA kernel on the dense conv-module shapes and loses on padded chunks
-// (its 256-row tiles skip padding more coarsely), so it is compiled in only when GSN_GEMM_PAIR is set to 1.
+// The CTA-pair mainloop is compiled in only when GSN_GEMM_PAIR is set to 1 (see the measurements of both
+// mainloops on the conv-module shapes).
 #ifndef GSN_GEMM_PAIR
 #define GSN_GEMM_PAIR 0
 #endif
@@ -941,13 +877,13 @@ using namespace gemm_impl;
 int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
   if (GSN_GEMM_PAIR && !a.w_int8) {
     bool launched = false;
-    const int rc = epilogue == kEpiGlu ? pair_impl::launch_pair<kEpiGlu>(a, stream, &launched)
-                                       : pair_impl::launch_pair<kEpiResidual>(a, stream, &launched);
+    const int rc = epilogue == kEpiGlu ? launch_pair<kEpiGlu>(a, stream, &launched)
+                                       : launch_pair<kEpiResidual>(a, stream, &launched);
     if (rc || launched) return rc;
   }
   if (epilogue == kEpiGlu)
-    return a.w_int8 ? launch_impl<kEpiGlu, true>(a, stream) : launch_impl<kEpiGlu, false>(a, stream);
-  return a.w_int8 ? launch_impl<kEpiResidual, true>(a, stream) : launch_impl<kEpiResidual, false>(a, stream);
+    return a.w_int8 ? launch_single<kEpiGlu, true>(a, stream) : launch_single<kEpiGlu, false>(a, stream);
+  return a.w_int8 ? launch_single<kEpiResidual, true>(a, stream) : launch_single<kEpiResidual, false>(a, stream);
 }
 
 }  // namespace gsn
