@@ -324,6 +324,65 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                      T, D, inner, ln_eps, workspace, workspace_bytes, 1, stream, "gsn_conv_module_i8w");
 }
 
+}  // extern "C"
+
+// ---- whole module with library-owned scratch -------------------------------------------------------------------
+// Some callers cannot allocate device memory at the point where they run the module: a plugin inside a host
+// application that owns the GPU memory budget and its allocator, or a latency-critical path where cudaMalloc /
+// cudaFree would synchronise the device.  For them the workspace of the module lives in this fixed array, part of
+// the library's device image: every GPU that loads the library holds it until the process exits, and nothing is
+// allocated per call.  Host code must not pass the array's name to a kernel (it is a host-side stand-in, not a
+// device address); the device address is fetched once per device with cudaGetSymbolAddress.
+namespace {
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[GSN_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (set-up on the first call per device).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail((int)e, "gsn_conv_module_bf16_noalloc (cudaGetDevice)");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GSN_ERR_UNSUPPORTED, "noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return cuda_fail((int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol),
+                       "gsn_conv_module_bf16_noalloc (cudaGetSymbolAddress of the static scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gsn_conv_module_bf16_noalloc(const void* x, const void* ln_w, const void* ln_b, const void* w1_glu,
+                                 const float* b1_glu, const void* dw_w, const void* dw_b, const void* w2,
+                                 const float* b2, const int32_t* lengths, int add_residual, void* out, int B, int T,
+                                 int D, int inner, float ln_eps, gsn_stream_t stream) {
+  const char* name = "gsn_conv_module_bf16_noalloc";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if ((int64_t)B * T == 0) return ok();
+  const size_t need = gsn_conv_module_workspace_bytes(B, T, D, inner);
+  if (need > (size_t)GSN_NOALLOC_SCRATCH_BYTES)
+    return fail(GSN_ERR_WORKSPACE,
+                "%s: B=%d T=%d D=%d inner=%d needs %zu bytes of scratch, above the library's static %d bytes "
+                "(at D=1024, inner=2048 at most %d frames per call); use gsn_conv_module_bf16 with a caller "
+                "workspace",
+                name, B, T, D, inner, need, GSN_NOALLOC_SCRATCH_BYTES, GSN_NOALLOC_SCRATCH_BYTES / 8192);
+  void* ws = nullptr;
+  if (int rc = noalloc_scratch(&ws)) return rc;
+  return conv_module(x, ln_w, ln_b, w1_glu, nullptr, b1_glu, dw_w, dw_b, w2, nullptr, b2, lengths, add_residual, out,
+                     B, T, D, inner, ln_eps, ws, (size_t)GSN_NOALLOC_SCRATCH_BYTES, 0, stream, name);
+}
+
 int gsn_interleave_glu_rows(const void* src, void* dst, int rows, int64_t row_bytes, gsn_stream_t stream) {
   if (!src || !dst) return fail(GSN_ERR_INVALID_ARG, "interleave: null pointer");
   if (rows <= 0 || rows % 256 != 0 || row_bytes <= 0)

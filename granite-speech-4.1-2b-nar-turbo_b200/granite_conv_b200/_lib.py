@@ -40,6 +40,8 @@ SIGNATURES = {
                                     _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
     "gsn_conv_module_i8w": (_i32, [_vp, _vp, _vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _fp, _vp, _i32, _vp,
                                    _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
+    "gsn_conv_module_bf16_noalloc": (_i32, [_vp, _vp, _vp, _vp, _fp, _vp, _vp, _vp, _fp, _vp, _i32, _vp, _i32,
+                                            _i32, _i32, _i32, _f32, _vp]),
     "gsn_interleave_glu_rows": (_i32, [_vp, _vp, _i32, _i64, _vp]),
     "gsn_device_status": (_i32, [ctypes.POINTER(_i32), _i32, _vp]),
     "gsn_selftest_bounded_wait": (_i32, [_u64, _vp]),

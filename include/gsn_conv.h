@@ -117,6 +117,25 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                         int add_residual, void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
                         size_t workspace_bytes, gsn_stream_t stream);
 
+/* ---- whole module without any allocation ------------------------------------------------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device memory where they run the module —
+ * a plugin inside a host application that owns the GPU memory budget and its allocator, or a latency-critical
+ * path where cudaMalloc / cudaFree would synchronise the device.  Same contract as gsn_conv_module_bf16 without
+ * the workspace arguments: the scratch is a fixed array of GSN_NOALLOC_SCRATCH_BYTES (32 MiB) inside the
+ * library's device image, held by every GPU that loads the library until the process exits, so a call needs
+ * gsn_conv_module_workspace_bytes(B, T, D, inner) <= 32 MiB (at D = 1024, inner = 2048: B * T <= 4096 frames)
+ * and larger problems are rejected with GSN_ERR_WORKSPACE.  Nothing is allocated, neither here nor per call.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make the first call on each device before any stream capture.  Every call shares the one array:
+ * calls that may overlap on the GPU (other streams, other host threads) race on it and must be serialised by the
+ * caller.  The array keeps the previous call's contents; the module writes every scratch byte it reads, so
+ * nothing needs clearing between calls. */
+#define GSN_NOALLOC_SCRATCH_BYTES 33554432
+int gsn_conv_module_bf16_noalloc(const void* x, const void* ln_w, const void* ln_b, const void* w1_glu,
+                                 const float* b1_glu, const void* dw_w, const void* dw_b, const void* w2,
+                                 const float* b2, const int32_t* lengths, int add_residual, void* out, int B, int T,
+                                 int D, int inner, float ln_eps, gsn_stream_t stream);
+
 /* ---- weight preparation --------------------------------------------------------------------------------
  * Device-to-device copy of `rows` x `row_bytes` with the GLU row interleave used by gsn_gemm1_*: output block j
  * (256 rows) = input rows [128 j, 128 j + 128) followed by rows [rows/2 + 128 j, rows/2 + 128 j + 128).
