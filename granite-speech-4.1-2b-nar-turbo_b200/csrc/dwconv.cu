@@ -7,13 +7,14 @@
 // Accumulation is fp32 and the output is rounded to bf16 once, as in the reference kernel.
 //
 // Two layouts:
-//  * channels-last (element stride of C is 1; the conv-module layout [B, T, C]): a persistent kernel.  A tile is
-//    CC channels x TT frames of one utterance; it is staged with its 7-frame halo on both sides ((TT + 14) rows of
-//    CC * 2 bytes) by a 3-D TMA load, out-of-range frames (t < 0, t >= T) arriving zero-filled.  Each CTA walks
-//    its tiles through a 3-stage shared-memory ring, so the loads of the next tiles are in flight while the
-//    current one is computed, across work-item boundaries.  A warp owns FPW output frames, a lane CPT channels
-//    (conflict-free shared-memory rows), with the 15 x CPT weights in registers and packed fp32x2 FMAs.  Tiles
-//    entirely inside the utterance take an unmasked path; tiles entirely past its end skip the load.
+//  * channels-last (element stride of C is 1; the conv-module layout [B, T, C]): a CTA owns CC channels of one
+//    utterance over TILES consecutive time tiles of TT frames (channel tile fastest in blockIdx.x, so the CTAs
+//    running together read whole frame rows).  Each tile plus its 7-frame halo on both sides ((TT + 14) rows of
+//    CC * 2 bytes) is staged in shared memory by a 3-D TMA load, out-of-range frames (t < 0, t >= T) arriving
+//    zero-filled, through a 3-stage ring: the load of tile i + 3 is issued as soon as tile i has been consumed.  A
+//    warp owns FPW output frames, a lane CPT channels (conflict-free shared-memory rows), with the 15 x CPT weights
+//    in registers and packed fp32x2 FMAs.  Tiles entirely inside the utterance take an unmasked path, tiles past
+//    its end skip their load, and a CTA whose frames are all padding only writes zeros.
 //  * channels-first (element stride of T is 1; the layout the reference op receives from up_conv): a CTA owns 32
 //    channels x 128 frames, stages the rows (plus halo) in shared memory as fp32 with plain coalesced loads
 //    (row strides need not be 16-byte multiples there, e.g. T = 37), and transposes the result through shared
@@ -21,19 +22,19 @@
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
-// Tile shape of the channels-last kernel (compile-time: channels per lane, frames per warp, warps per CTA, and
-// time tiles per work item).
+// Tile shape of the channels-last kernel (compile-time: channels per lane, frames per warp, warps per CTA, time
+// tiles per CTA).
 #ifndef GSN_DW_CPT
 #define GSN_DW_CPT 4
 #endif
 #ifndef GSN_DW_FPW
-#define GSN_DW_FPW 16
+#define GSN_DW_FPW 8
 #endif
 #ifndef GSN_DW_WARPS
 #define GSN_DW_WARPS 4
 #endif
 #ifndef GSN_DW_SEG
-#define GSN_DW_SEG 4
+#define GSN_DW_SEG 8
 #endif
 
 namespace gsn {
@@ -55,7 +56,7 @@ struct ClCfg {
   static constexpr int TILE_BYTES = ROWS * ROW_BYTES;
   static constexpr int STAGES = 3;
   static constexpr int THREADS = 32 * WARPS;
-  static constexpr int SEG = GSN_DW_SEG;           // consecutive time tiles per work item
+  static constexpr int TILES = GSN_DW_SEG;         // consecutive time tiles per CTA
 };
 
 template <int CPT, int FPW, int WARPS, bool GLU>
@@ -72,8 +73,7 @@ struct ClParams {
   __nv_bfloat16* y;
   const int* lengths;
   int64_t syB, syT;
-  int B, T, C;
-  int n_ct, n_seg, n_items;     // channel tiles, time segments per (b, channel tile), work items
+  int T, C;
 };
 
 __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t v) { return make_float2(bf16lo_to_f32(v), bf16hi_to_f32(v)); }
@@ -110,42 +110,13 @@ __device__ __forceinline__ void stg_words(__nv_bfloat16* p, const uint32_t (&w)[
   }
 }
 
-// Position of the k-th tile walked by this CTA: work items are (utterance, time segment, channel tile) with the
-// channel tile fastest, dealt round-robin to the persistent CTAs, so the CTAs running at the same time read whole
-// frame rows (all channel tiles of the same frames) from DRAM together; a segment is SEG consecutive time tiles.
-template <class Cfg>
-struct TileWalk {
-  int item, sub;
-  __device__ void start() {
-    item = blockIdx.x;
-    sub = 0;
-  }
-  __device__ bool valid(const ClParams& p) const { return item < p.n_items; }
-  __device__ void coords(const ClParams& p, int& b, int& c0, int& t0) const {
-    const int ct = item % p.n_ct;
-    const int rest = item / p.n_ct;
-    const int seg = rest % p.n_seg;
-    b = rest / p.n_seg;
-    c0 = ct * Cfg::CC;
-    t0 = (seg * Cfg::SEG + sub) * Cfg::TT;
-  }
-  __device__ void next(const ClParams& p) {
-    int b, c0, t0;
-    coords(p, b, c0, t0);
-    ++sub;
-    if (sub >= Cfg::SEG || t0 + Cfg::TT >= p.T) {
-      sub = 0;
-      item += gridDim.x;
-    }
-  }
-};
-
 template <int CPT, int FPW, int WARPS, bool GLU>
 __global__ void __launch_bounds__(32 * WARPS)
     dwconv_cl_kernel(const __grid_constant__ CUtensorMap tmX, ClParams p) {
   using Cfg = ClCfg<CPT, FPW, WARPS, GLU>;
   constexpr int NP = Cfg::NP;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int TT = Cfg::TT;
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<ClSmem<CPT, FPW, WARPS, GLU>*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                                              ~uintptr_t(127));
@@ -153,6 +124,22 @@ __global__ void __launch_bounds__(32 * WARPS)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int T = p.T;
+  const int c0 = blockIdx.x * Cfg::CC;
+  const int b = blockIdx.z;
+  const int t_begin = blockIdx.y * (TT * Cfg::TILES);
+  const int t_end = min(T, t_begin + TT * Cfg::TILES);
+  const int len = p.lengths ? min(max(__ldg(p.lengths + b), 0), T) : T;
+  __nv_bfloat16* yb = p.y + (int64_t)b * p.syB + c0 + lane * CPT;
+
+  if (t_begin >= len) {
+    // every frame of this CTA is padding: zeros, no loads
+    uint32_t z[NP];
+#pragma unroll
+    for (int q = 0; q < NP; ++q) z[q] = 0u;
+    for (int t = t_begin + warp; t < t_end; t += WARPS) stg_words<NP>(yb + (int64_t)t * p.syT, z);
+    return;
+  }
+  const int n_tiles = (t_end - t_begin + TT - 1) / TT;
   constexpr uint32_t kTxBytes = (GLU ? 2 : 1) * Cfg::TILE_BYTES;
 
   if (tid == 0) {
@@ -163,13 +150,12 @@ __global__ void __launch_bounds__(32 * WARPS)
   }
   __syncthreads();
 
-  auto len_of = [&](int b) { return p.lengths ? min(max(__ldg(p.lengths + b), 0), T) : T; };
-  // producer side (thread 0): load tile `w` into stage st, or, if every output frame of it is padding, complete
-  // the stage's phase without a copy
-  auto issue = [&](const TileWalk<Cfg>& w, int st) {
-    int b, c0, t0;
-    w.coords(p, b, c0, t0);
-    if (t0 >= len_of(b)) {
+  // producer side (thread 0): load tile i into stage i % STAGES, or, if every output frame of it is padding,
+  // complete the stage's phase without a copy
+  auto issue = [&](int i) {
+    const int st = i % STAGES;
+    const int t0 = t_begin + i * TT;
+    if (t0 >= len) {
       mbar_arrive(&s.full[st]);
       return;
     }
@@ -177,58 +163,46 @@ __global__ void __launch_bounds__(32 * WARPS)
     tma_load_3d(s.x[st][0], &tmX, &s.full[st], c0, t0 - HALO, b);
     if (GLU) tma_load_3d(s.x[st][GLU ? 1 : 0], &tmX, &s.full[st], c0 + p.C, t0 - HALO, b);
   };
-
-  TileWalk<Cfg> prod;
-  prod.start();
   int issued = 0;                                    // tiles handed to stages so far (thread 0)
   if (tid == 0) {
-    for (int i = 0; i < STAGES && prod.valid(p); ++i) {
-      issue(prod, i);
-      prod.next(p);
-      ++issued;
-    }
+    for (; issued < STAGES && issued < n_tiles; ++issued) issue(issued);
   }
 
-  TileWalk<Cfg> cons;
-  cons.start();
-  int cur_c0 = -1;
+  // weights of this lane's channels, as fp32 pairs: wr[j][q] = (channel 2q, channel 2q + 1)
   float2 wr[KW][NP];
   float2 bias[NP];
-  bool alive = true;
-  for (int k = 0; cons.valid(p); ++k, cons.next(p)) {
-    int b, c0, t0;
-    cons.coords(p, b, c0, t0);
-    const int len = len_of(b);
-    const int st = k % STAGES;
-    if (c0 != cur_c0) {  // weights of this lane's channels, as fp32 pairs
-      cur_c0 = c0;
-      const __nv_bfloat16* wp = p.w + (int64_t)(c0 + lane * CPT) * KW;
+  {
+    const __nv_bfloat16* wp = p.w + (int64_t)(c0 + lane * CPT) * KW;
 #pragma unroll
-      for (int j = 0; j < KW; ++j)
-#pragma unroll
-        for (int q = 0; q < NP; ++q)
-          wr[j][q] = make_float2(__bfloat162float(wp[(2 * q) * KW + j]), __bfloat162float(wp[(2 * q + 1) * KW + j]));
+    for (int j = 0; j < KW; ++j)
 #pragma unroll
       for (int q = 0; q < NP; ++q)
-        bias[q] = make_float2(__bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
-                              __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
-    }
+        wr[j][q] = make_float2(__bfloat162float(wp[(2 * q) * KW + j]), __bfloat162float(wp[(2 * q + 1) * KW + j]));
+#pragma unroll
+    for (int q = 0; q < NP; ++q)
+      bias[q] = make_float2(__bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
+                            __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
+  }
+
+  bool alive = true;
+  const int row0 = warp * FPW;                       // first output frame (and staged row) of this warp
+  for (int i = 0; i < n_tiles; ++i) {
+    const int st = i % STAGES;
+    const int t0 = t_begin + i * TT;
     if (alive)
-      alive = mbar_wait_bounded(&s.full[st], (uint32_t)((k / STAGES) & 1), &s.abort_flag, kStatusTimeoutDw);
-    const int row0 = warp * FPW;                 // first output frame (and staged row) of this warp
-    __nv_bfloat16* yb = p.y + (int64_t)b * p.syB + c0 + lane * CPT;
+      alive = mbar_wait_bounded(&s.full[st], (uint32_t)((i / STAGES) & 1), &s.abort_flag, kStatusTimeoutDw);
     if (alive && t0 >= len) {
       // every output frame of the tile is padding
+      uint32_t z[NP];
+#pragma unroll
+      for (int q = 0; q < NP; ++q) z[q] = 0u;
 #pragma unroll
       for (int f = 0; f < FPW; ++f) {
         const int t = t0 + row0 + f;
-        uint32_t z[NP];
-#pragma unroll
-        for (int q = 0; q < NP; ++q) z[q] = 0u;
         if (t < T) stg_words<NP>(yb + (int64_t)t * p.syT, z);
       }
     } else if (alive) {
-      const bool fast = t0 + Cfg::TT + HALO <= len;   // every staged row and output frame is inside the utterance
+      const bool fast = t0 + TT + HALO <= len;   // every staged row and output frame is inside the utterance
       float2 acc[FPW][NP];
 #pragma unroll
       for (int f = 0; f < FPW; ++f)
@@ -276,10 +250,9 @@ __global__ void __launch_bounds__(32 * WARPS)
       }
     }
     __syncthreads();  // stage st fully consumed by every warp
-    if (tid == 0 && alive && !s.abort_flag && prod.valid(p)) {
+    if (tid == 0 && alive && !s.abort_flag && issued < n_tiles) {
       fence_proxy_async_smem();
-      issue(prod, st);
-      prod.next(p);
+      issue(issued);
       ++issued;
     }
   }
@@ -308,25 +281,15 @@ int launch_cl(const DwArgs& a, cudaStream_t stream) {
   p.lengths = a.lengths;
   p.syB = a.syB;
   p.syT = a.syT;
-  p.B = a.B;
   p.T = a.T;
   p.C = a.C;
-  p.n_ct = a.C / Cfg::CC;
-  const int n_tt = (a.T + Cfg::TT - 1) / Cfg::TT;
-  p.n_seg = (n_tt + Cfg::SEG - 1) / Cfg::SEG;
-  const int64_t items = (int64_t)a.B * p.n_ct * p.n_seg;
-  if (items > 0x7fffffff) return (int)cudaErrorInvalidValue;
-  p.n_items = (int)items;
+  const int64_t t_chunks = ((int64_t)a.T + Cfg::TT * Cfg::TILES - 1) / (Cfg::TT * Cfg::TILES);
+  if (t_chunks > 65535 || a.B > 65535) return (int)cudaErrorInvalidValue;
   auto kern = dwconv_cl_kernel<CPT, FPW, WARPS, GLU>;
   const int smem = (int)sizeof(ClSmem<CPT, FPW, WARPS, GLU>) + 128;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::THREADS, smem);
-  if (e != cudaSuccess) return (int)e;
-  if (per_sm < 1) per_sm = 1;
-  const int64_t slots = (int64_t)device_sm_count() * per_sm;
-  const int grid = (int)(items < slots ? items : slots);
+  dim3 grid(a.C / Cfg::CC, (unsigned)t_chunks, a.B);
   kern<<<grid, Cfg::THREADS, smem, stream>>>(tm, p);
   return (int)cudaGetLastError();
 }
