@@ -37,6 +37,10 @@ N_UTTS = 512
 D, I = synth.D_MODEL, synth.D_INNER
 GEMM1_FLOP_PER_FRAME = 2 * D * 2 * I          # 8.389 MFLOP
 GEMM2_FLOP_PER_FRAME = 2 * I * D              # 4.194 MFLOP
+# DRAM bytes (read + write) of the up_conv + GLU GEMM per row of the 128-row tiles it computes, from one ncu capture
+# of a B=48, T=1536 chunk (profiles/gemm_conv_module_b48_t1536.md: 72.3 + 84.2 MB over 31,104 rows); the traffic
+# of a launch scales with the rows it computes.
+GEMM1_DRAM_BYTES_PER_ROW = 5032
 DW_BYTES_PER_FRAME = 2 * I * 2                # read + write bf16: 8192 B
 METRIC = "conv-module frames/s at 1/2/4/8 B200; % of HBM / tensor-pipe roofline"
 
@@ -377,7 +381,10 @@ def run_ours(args):
         g1 = kernels["gemm1_glu"]
         roof = {"kernel": "gemm_kernel<GLU> (up_conv 1024->4096 + GLU)", "bound": "tensor",
                 "achieved": g1["achieved"], "peak": g1["peak"], "unit": "TFLOP/s", "frac": g1["frac"],
-                "traffic": None, "per_launch_ms": g1["ms_per_launch"],
+                "traffic": g1["rows_per_launch"] * GEMM1_DRAM_BYTES_PER_ROW,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per computed row, scaled to the "
+                                  "average launch (profiles/gemm_conv_module_b48_t1536.md)",
+                "algorithmic_bytes": g1["rows_per_launch"] * (2 * D + 2 * I), "per_launch_ms": g1["ms_per_launch"],
                 "algorithmic_flop_per_frame": GEMM1_FLOP_PER_FRAME,
                 "frames_counted": "rows of the 128-row tiles holding valid frames (tiles of pure padding are "
                                   "skipped by the kernel)",
@@ -439,6 +446,7 @@ def _kernel_breakdown(layer_events, peaks):
         pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
         out[n] = {"ms_per_launch": tot[n] / len(layer_events), "share": tot[n] / all_ms, "achieved": ach,
                   "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
+    out["gemm1_glu"]["rows_per_launch"] = work["gemm1_glu"] / GEMM1_FLOP_PER_FRAME / len(layer_events)
     return out
 
 
@@ -456,12 +464,38 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
     h2d = sum(x.numel() * 2 + l.numel() * 4 for x, l in zip(hx, hl))
     d2h = sum(o.numel() * 2 for o in ho)
 
+    # copies run on their own streams so chunk i+1's upload and chunk i-1's download overlap chunk i's layers;
+    # a chunk's device input is overwritten only after the previous step's compute of that chunk has finished
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
+    xd = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
+    ld = [torch.empty((c.B,), dtype=torch.int32, device=dev) for c in chunks]
+    done = [None] * len(chunks)
+
     def step():
+        begin = torch.cuda.Event()          # the step's copies start after everything queued before it
+        begin.record(stream)
+        copy_in.wait_event(begin)
         for ci in range(len(chunks)):
-            x = hx[ci].to(dev, non_blocking=True)
-            lens = hl[ci].to(dev, non_blocking=True)
-            y = stack(x, lens)
-            ho[ci].copy_(y, non_blocking=True)
+            with torch.cuda.stream(copy_in):
+                if done[ci] is not None:
+                    copy_in.wait_event(done[ci])
+                xd[ci].copy_(hx[ci], non_blocking=True)
+                ld[ci].copy_(hl[ci], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(copy_in)
+            stream.wait_event(ready)
+            with torch.cuda.stream(stream):
+                y = stack(xd[ci], ld[ci])
+                done[ci] = torch.cuda.Event()
+                done[ci].record(stream)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done[ci])
+                ho[ci].copy_(y, non_blocking=True)
+                y.record_stream(copy_out)
+        fin = torch.cuda.Event()
+        fin.record(copy_out)
+        stream.wait_event(fin)
 
     for _ in range(max(1, args.warmup)):
         step()
@@ -485,7 +519,7 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
         valid = float(v.item())
     return {"value": valid * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
-            "path": "torch.ops.granite.conv_module per layer, pinned host in/out"}
+            "path": "torch.ops.granite.conv_module per layer, pinned host in/out on two copy streams"}
 
 
 def main():
