@@ -19,6 +19,8 @@
 //    channels x 128 frames, stages the rows (plus halo) in shared memory as fp32 with plain coalesced loads
 //    (row strides need not be 16-byte multiples there, e.g. T = 37), and transposes the result through shared
 //    memory for coalesced stores.  Any other stride pattern also takes this path.
+#include <type_traits>
+
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
@@ -35,6 +37,12 @@
 #endif
 #ifndef GSN_DW_SEG
 #define GSN_DW_SEG 8
+#endif
+#ifndef GSN_DW_STAGES
+#define GSN_DW_STAGES 3
+#endif
+#ifndef GSN_DW_MIN_CTAS            // resident CTAs per SM the register allocation must allow
+#define GSN_DW_MIN_CTAS 4
 #endif
 
 namespace gsn {
@@ -54,7 +62,7 @@ struct ClCfg {
   static constexpr int ROWS = TT + 2 * HALO;       // staged rows
   static constexpr int ROW_BYTES = CC * 2;
   static constexpr int TILE_BYTES = ROWS * ROW_BYTES;
-  static constexpr int STAGES = 3;
+  static constexpr int STAGES = GSN_DW_STAGES;
   static constexpr int THREADS = 32 * WARPS;
   static constexpr int TILES = GSN_DW_SEG;         // consecutive time tiles per CTA
 };
@@ -111,7 +119,7 @@ __device__ __forceinline__ void stg_words(__nv_bfloat16* p, const uint32_t (&w)[
 }
 
 template <int CPT, int FPW, int WARPS, bool GLU>
-__global__ void __launch_bounds__(32 * WARPS)
+__global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
     dwconv_cl_kernel(const __grid_constant__ CUtensorMap tmX, ClParams p) {
   using Cfg = ClCfg<CPT, FPW, WARPS, GLU>;
   constexpr int NP = Cfg::NP;
@@ -168,7 +176,8 @@ __global__ void __launch_bounds__(32 * WARPS)
     for (; issued < STAGES && issued < n_tiles; ++issued) issue(issued);
   }
 
-  // weights of this lane's channels, as fp32 pairs: wr[j][q] = (channel 2q, channel 2q + 1)
+  // weights of this lane's channels, as fp32 pairs: wr[j][q] = (channel 2q, channel 2q + 1).  Weights and bias are
+  // held halved (exact), so the accumulator is h = x / 2 and silu(x) = h + h * tanh(h) needs no extra multiply.
   float2 wr[KW][NP];
   float2 bias[NP];
   {
@@ -177,11 +186,12 @@ __global__ void __launch_bounds__(32 * WARPS)
     for (int j = 0; j < KW; ++j)
 #pragma unroll
       for (int q = 0; q < NP; ++q)
-        wr[j][q] = make_float2(__bfloat162float(wp[(2 * q) * KW + j]), __bfloat162float(wp[(2 * q + 1) * KW + j]));
+        wr[j][q] = make_float2(0.5f * __bfloat162float(wp[(2 * q) * KW + j]),
+                               0.5f * __bfloat162float(wp[(2 * q + 1) * KW + j]));
 #pragma unroll
     for (int q = 0; q < NP; ++q)
-      bias[q] = make_float2(__bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
-                            __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
+      bias[q] = make_float2(0.5f * __bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
+                            0.5f * __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
   }
 
   bool alive = true;
@@ -202,52 +212,64 @@ __global__ void __launch_bounds__(32 * WARPS)
         if (t < T) stg_words<NP>(yb + (int64_t)t * p.syT, z);
       }
     } else if (alive) {
-      const bool fast = t0 + TT + HALO <= len;   // every staged row and output frame is inside the utterance
-      float2 acc[FPW][NP];
+      // MASKED: some staged row or output frame lies past the utterance's end.  The unmasked body is a separate
+      // instantiation, so the common case carries no per-row or per-frame selects.
+      auto tile = [&](auto masked_tag) {
+        constexpr bool MASKED = decltype(masked_tag)::value;
+        float2 acc[FPW][NP];
 #pragma unroll
-      for (int f = 0; f < FPW; ++f)
+        for (int f = 0; f < FPW; ++f)
 #pragma unroll
-        for (int q = 0; q < NP; ++q) acc[f][q] = bias[q];
-      const int t_row0 = t0 - HALO + row0;
-      const uint8_t* xa = s.x[st][0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
-      const uint8_t* xg = s.x[st][GLU ? 1 : 0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
+          for (int q = 0; q < NP; ++q) acc[f][q] = bias[q];
+        const int t_row0 = t0 - HALO + row0;
+        const uint8_t* xa = s.x[st][0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
+        const uint8_t* xg = s.x[st][GLU ? 1 : 0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
 #pragma unroll
-      for (int r = 0; r < FPW + 2 * HALO; ++r) {
-        uint32_t va[NP];
-        lds_words<NP>(xa + r * Cfg::ROW_BYTES, va);
-        float2 xv[NP];
-        if (GLU) {
-          uint32_t vg[NP];
-          lds_words<NP>(xg + r * Cfg::ROW_BYTES, vg);
+        for (int r = 0; r < FPW + 2 * HALO; ++r) {
+          uint32_t va[NP];
+          lds_words<NP>(xa + r * Cfg::ROW_BYTES, va);
+          float2 xv[NP];
+          if (GLU) {
+            uint32_t vg[NP];
+            lds_words<NP>(xg + r * Cfg::ROW_BYTES, vg);
 #pragma unroll
-          for (int q = 0; q < NP; ++q) xv[q] = glu_pair(va[q], vg[q]);
-        } else {
+            for (int q = 0; q < NP; ++q) xv[q] = glu_pair(va[q], vg[q]);
+          } else {
 #pragma unroll
-          for (int q = 0; q < NP; ++q) xv[q] = bf16x2_to_f2(va[q]);
-        }
-        if (!fast && t_row0 + r >= len) {  // frames past the utterance read as zero (t >= T is zero-filled)
+            for (int q = 0; q < NP; ++q) xv[q] = bf16x2_to_f2(va[q]);
+          }
+          if (MASKED && t_row0 + r >= len) {  // frames past the utterance read as zero (t >= T is zero-filled)
 #pragma unroll
-          for (int q = 0; q < NP; ++q) xv[q] = make_float2(0.f, 0.f);
-        }
+            for (int q = 0; q < NP; ++q) xv[q] = make_float2(0.f, 0.f);
+          }
 #pragma unroll
-        for (int f = 0; f < FPW; ++f) {
-          const int j = r - f;
-          if (j >= 0 && j < KW) {
+          for (int f = 0; f < FPW; ++f) {
+            const int j = r - f;
+            if (j >= 0 && j < KW) {
 #pragma unroll
-            for (int q = 0; q < NP; ++q) acc[f][q] = ffma2(wr[j][q], xv[q], acc[f][q]);
+              for (int q = 0; q < NP; ++q) acc[f][q] = ffma2(wr[j][q], xv[q], acc[f][q]);
+            }
           }
         }
-      }
+        __nv_bfloat16* yt = yb + (int64_t)(t0 + row0) * p.syT;
 #pragma unroll
-      for (int f = 0; f < FPW; ++f) {
-        const int t = t0 + row0 + f;
-        uint32_t o[NP];
-        const bool valid = fast || t < len;
+        for (int f = 0; f < FPW; ++f, yt += p.syT) {
+          const int t = t0 + row0 + f;
+          uint32_t o[NP];
+          const bool valid = !MASKED || t < len;
 #pragma unroll
-        for (int q = 0; q < NP; ++q)
-          o[q] = valid ? pack_bf16x2(silu_fast(acc[f][q].x), silu_fast(acc[f][q].y)) : 0u;
-        if (fast || t < T) stg_words<NP>(yb + (int64_t)t * p.syT, o);
-      }
+          for (int q = 0; q < NP; ++q) {
+            const float2 h = acc[f][q];
+            const float2 s2 = ffma2(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);  // silu(2h) per lane
+            o[q] = valid ? pack_bf16x2(s2.x, s2.y) : 0u;
+          }
+          if (!MASKED || t < T) stg_words<NP>(yt, o);
+        }
+      };
+      if (t0 + TT + HALO <= len)
+        tile(std::false_type{});
+      else
+        tile(std::true_type{});
     }
     __syncthreads();  // stage st fully consumed by every warp
     if (tid == 0 && alive && !s.abort_flag && issued < n_tiles) {

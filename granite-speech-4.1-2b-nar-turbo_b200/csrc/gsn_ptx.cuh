@@ -367,6 +367,9 @@ __device__ __forceinline__ float silu_fast(float x) {
   return fmaf(h, tanh_approx(h), h);
 }
 
+// silu(2h) given h = x / 2.
+__device__ __forceinline__ float silu_half(float h) { return fmaf(h, tanh_approx(h), h); }
+
 __device__ __forceinline__ float bf16lo_to_f32(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16hi_to_f32(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
