@@ -86,6 +86,31 @@ struct ClParams {
 
 __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t v) { return make_float2(bf16lo_to_f32(v), bf16hi_to_f32(v)); }
 
+// Packed fp32 pairs kept as 64-bit registers from the unpack through the FMAs, so the pair operands of
+// fma.rn.f32x2 never have to be assembled from separately allocated halves.
+typedef uint64_t pk2;
+__device__ __forceinline__ pk2 pk_from_bf16x2(uint32_t v) {
+  pk2 d;
+  asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xFFFF0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+      : "=l"(d) : "r"(v));
+  return d;
+}
+__device__ __forceinline__ pk2 pk_make(float lo, float hi) {
+  pk2 d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ float2 pk_split(pk2 v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+__device__ __forceinline__ pk2 pk_fma(pk2 a, pk2 b, pk2 c) {
+  pk2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // GLU of one packed bf16 pair, rounded to bf16 and widened back (conv1d.py:70-73 rounds the product to bf16)
 __device__ __forceinline__ float2 glu_pair(uint32_t a, uint32_t g) {
   const float a0 = bf16lo_to_f32(a), a1 = bf16hi_to_f32(a);
@@ -178,20 +203,20 @@ __global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
 
   // weights of this lane's channels, as fp32 pairs: wr[j][q] = (channel 2q, channel 2q + 1).  Weights and bias are
   // held halved (exact), so the accumulator is h = x / 2 and silu(x) = h + h * tanh(h) needs no extra multiply.
-  float2 wr[KW][NP];
-  float2 bias[NP];
+  pk2 wr[KW][NP];
+  pk2 bias[NP];
   {
     const __nv_bfloat16* wp = p.w + (int64_t)(c0 + lane * CPT) * KW;
 #pragma unroll
     for (int j = 0; j < KW; ++j)
 #pragma unroll
       for (int q = 0; q < NP; ++q)
-        wr[j][q] = make_float2(0.5f * __bfloat162float(wp[(2 * q) * KW + j]),
-                               0.5f * __bfloat162float(wp[(2 * q + 1) * KW + j]));
+        wr[j][q] = pk_make(0.5f * __bfloat162float(wp[(2 * q) * KW + j]),
+                           0.5f * __bfloat162float(wp[(2 * q + 1) * KW + j]));
 #pragma unroll
     for (int q = 0; q < NP; ++q)
-      bias[q] = make_float2(0.5f * __bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
-                            0.5f * __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
+      bias[q] = pk_make(0.5f * __bfloat162float(p.bias[c0 + lane * CPT + 2 * q]),
+                        0.5f * __bfloat162float(p.bias[c0 + lane * CPT + 2 * q + 1]));
   }
 
   bool alive = true;
@@ -216,11 +241,7 @@ __global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
       // instantiation, so the common case carries no per-row or per-frame selects.
       auto tile = [&](auto masked_tag) {
         constexpr bool MASKED = decltype(masked_tag)::value;
-        float2 acc[FPW][NP];
-#pragma unroll
-        for (int f = 0; f < FPW; ++f)
-#pragma unroll
-          for (int q = 0; q < NP; ++q) acc[f][q] = bias[q];
+        pk2 acc[FPW][NP];  // frame f starts from the bias at its first tap (row r = f), as bias + w0 x0 + w1 x1 ...
         const int t_row0 = t0 - HALO + row0;
         const uint8_t* xa = s.x[st][0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
         const uint8_t* xg = s.x[st][GLU ? 1 : 0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
@@ -228,26 +249,29 @@ __global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
         for (int r = 0; r < FPW + 2 * HALO; ++r) {
           uint32_t va[NP];
           lds_words<NP>(xa + r * Cfg::ROW_BYTES, va);
-          float2 xv[NP];
+          pk2 xv[NP];
           if (GLU) {
             uint32_t vg[NP];
             lds_words<NP>(xg + r * Cfg::ROW_BYTES, vg);
 #pragma unroll
-            for (int q = 0; q < NP; ++q) xv[q] = glu_pair(va[q], vg[q]);
+            for (int q = 0; q < NP; ++q) {
+              const float2 g2 = glu_pair(va[q], vg[q]);
+              xv[q] = pk_make(g2.x, g2.y);
+            }
           } else {
 #pragma unroll
-            for (int q = 0; q < NP; ++q) xv[q] = bf16x2_to_f2(va[q]);
+            for (int q = 0; q < NP; ++q) xv[q] = pk_from_bf16x2(va[q]);
           }
           if (MASKED && t_row0 + r >= len) {  // frames past the utterance read as zero (t >= T is zero-filled)
 #pragma unroll
-            for (int q = 0; q < NP; ++q) xv[q] = make_float2(0.f, 0.f);
+            for (int q = 0; q < NP; ++q) xv[q] = 0ull;
           }
 #pragma unroll
           for (int f = 0; f < FPW; ++f) {
             const int j = r - f;
             if (j >= 0 && j < KW) {
 #pragma unroll
-              for (int q = 0; q < NP; ++q) acc[f][q] = ffma2(wr[j][q], xv[q], acc[f][q]);
+              for (int q = 0; q < NP; ++q) acc[f][q] = pk_fma(wr[j][q], xv[q], j == 0 ? bias[q] : acc[f][q]);
             }
           }
         }
@@ -259,8 +283,8 @@ __global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
           const bool valid = !MASKED || t < len;
 #pragma unroll
           for (int q = 0; q < NP; ++q) {
-            const float2 h = acc[f][q];
-            const float2 s2 = ffma2(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);  // silu(2h) per lane
+            const float2 h = pk_split(acc[f][q]);
+            const float2 s2 = pk_split(pk_fma(acc[f][q], pk_make(tanh_approx(h.x), tanh_approx(h.y)), acc[f][q]));
             o[q] = valid ? pack_bf16x2(s2.x, s2.y) : 0u;
           }
           if (!MASKED || t < T) stg_words<NP>(yt, o);
