@@ -265,19 +265,33 @@ def run_ours(args):
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     h_buf = ws                                                         # [M, I] GLU output
     t_off = ((max_m * I * 2 + 255) // 256) * 256
+    # int8: both weight matrices widened to bf16 once per layer call, as gsn_conv_module_i8w does when its
+    # workspace has room for them
+    w1b = torch.empty((2 * I, D), dtype=torch.bfloat16, device=dev) if int8 else None
+    w2b = torch.empty((D, I), dtype=torch.bfloat16, device=dev) if int8 else None
     act = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]   # ping-pong buffers
     act2 = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
 
     layer_events = []      # per recorded layer: (events[5], chunk) around layernorm, gemm1, dwconv, gemm2
+    widen_events = []      # int8: per recorded layer, the events around the weight widening
 
     def layer_kernels(x, out, c, p, lens, record):
-        """The four kernels of one conv module (the same launches gsn_conv_module_* makes), with CUDA events
-        between them when `record`."""
+        """The kernels of one conv module (the same launches gsn_conv_module_* makes), with CUDA events between
+        them when `record`."""
         M = c.padded_frames
         hp = h_buf.data_ptr()
         tp = h_buf.data_ptr() + t_off
         lp, T = lens.data_ptr(), c.T
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        if int8:
+            wev = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None
+            if record:
+                wev[0].record(stream)
+            _lib.check(L.gsn_widen_i8_bf16(p.w1q_glu.data_ptr(), w1b.data_ptr(), 2 * I * D, p.w2q.data_ptr(),
+                                           w2b.data_ptr(), D * I, sp), "widen")
+            if record:
+                wev[1].record(stream)
+                widen_events.append(wev)
         if record:
             ev[0].record(stream)
         _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
@@ -285,8 +299,8 @@ def run_ours(args):
         if record:
             ev[1].record(stream)
         if int8:
-            _lib.check(L.gsn_gemm1_glu_i8w(tp, p.w1q_glu.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), hp,
-                                           M, D, 2 * I, lp, T, sp), "gemm1")
+            _lib.check(L.gsn_gemm1_glu_bf16s(tp, w1b.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), hp,
+                                             M, D, 2 * I, lp, T, sp), "gemm1")
         else:
             _lib.check(L.gsn_gemm1_glu_bf16(tp, p.w1_glu.data_ptr(), p.b1_glu.data_ptr(), hp, M, D, 2 * I, lp, T,
                                             sp), "gemm1")
@@ -297,8 +311,8 @@ def run_ours(args):
         if record:
             ev[3].record(stream)
         if int8:
-            _lib.check(L.gsn_gemm2_residual_i8w(tp, p.w2q.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(), x.data_ptr(),
-                                                D, out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
+            _lib.check(L.gsn_gemm2_residual_bf16s(tp, w2b.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
+                                                  x.data_ptr(), D, out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
         else:
             _lib.check(L.gsn_gemm2_residual_bf16(tp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
                                                  out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
@@ -329,7 +343,7 @@ def run_ours(args):
                 dst = act[ci] if li % 2 == 0 else act2[ci]
                 layer_kernels(src, dst, c, p, lens_dev[ci], record)
                 src = dst
-                n += 4
+                n += 5 if int8 else 4
         return n
 
     def barrier():
@@ -377,7 +391,7 @@ def run_ours(args):
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
     else:
-        kernels = _kernel_breakdown(layer_events, peaks)
+        kernels = _kernel_breakdown(layer_events, peaks, widen_events)
         g1 = kernels["gemm1_glu"]
         roof = {"kernel": "gemm_kernel<GLU> (up_conv 1024->4096 + GLU)", "bound": "tensor",
                 "achieved": g1["achieved"], "peak": g1["peak"], "unit": "TFLOP/s", "frac": g1["frac"],
@@ -420,17 +434,21 @@ def _tile_rows(c, tile=128):
     return int(sum(((int(L) + tile - 1) // tile) * tile for L in c.lengths))
 
 
-def _kernel_breakdown(layer_events, peaks):
-    """Average launch time, share of the recorded kernel time and achieved rate of each of the four kernels.
+def _kernel_breakdown(layer_events, peaks, widen_events=()):
+    """Average launch time, share of the recorded kernel time and achieved rate of each kernel.
     Work per launch: LayerNorm reads and writes the valid frames (2 x 2 KB); the GEMMs compute the rows of the
     128-row tiles that hold valid frames; the depthwise kernel reads the valid frames and writes every frame
-    (4 KB each way per frame)."""
+    (4 KB each way per frame); the int8 weight widening reads 1 byte and writes 2 per weight."""
     names = ("layernorm", "gemm1_glu", "dwconv_silu", "gemm2_residual")
     tot = {n: 0.0 for n in names}
     work = {n: 0.0 for n in names}
+    if widen_events:
+        names = ("widen_i8",) + names
+        tot["widen_i8"] = sum(a.elapsed_time(b) for a, b in widen_events) * len(layer_events) / len(widen_events)
+        work["widen_i8"] = 3.0 * (2 * I * D + D * I) * len(layer_events)
     for ev, c in layer_events:
         m = c.padded_frames
-        for k, n in enumerate(names):
+        for k, n in enumerate(names[-4:]):
             tot[n] += ev[k].elapsed_time(ev[k + 1])
         valid = c.valid_frames
         rows = _tile_rows(c)

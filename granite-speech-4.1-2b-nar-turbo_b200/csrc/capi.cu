@@ -208,52 +208,78 @@ static int check_lengths(const char* name, const int32_t* lengths, int T, int M)
   return 0;
 }
 
+// i8: W is int8; scaled: the accumulator is multiplied by a per-column scale (int8 weights, staged as int8 or
+// already widened to bf16)
 static int gemm1(const void* a, const void* w, const float* scale, const float* b, void* h, int M, int K, int N,
-                 const int32_t* lengths, int T, int i8, gsn_stream_t stream, const char* name) {
+                 const int32_t* lengths, int T, int i8, int scaled, gsn_stream_t stream, const char* name) {
   if (int rc = check_gemm(name, a, w, b, h, M, K, N)) return rc < 0 ? ok() : rc;
-  if (i8 && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
+  if (scaled && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
   if (int rc = check_lengths(name, lengths, T, M)) return rc;
-  GemmArgs g{(const __nv_bfloat16*)a, w, b, i8 ? scale : nullptr, nullptr, (__nv_bfloat16*)h, (int64_t)(N / 2), 0,
-             M, N, K, i8, lengths, T};
+  GemmArgs g{(const __nv_bfloat16*)a, w, b, scaled ? scale : nullptr, nullptr, (__nv_bfloat16*)h, (int64_t)(N / 2),
+             0, M, N, K, i8, lengths, T};
   return finish(launch_gemm(g, kEpiGlu, (cudaStream_t)stream), name);
 }
 
 static int gemm2(const void* d, const void* w, const float* scale, const float* b, const void* res, int64_t ld_res,
                  void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths, int T, int i8,
-                 gsn_stream_t stream, const char* name) {
+                 int scaled, gsn_stream_t stream, const char* name) {
   if (int rc = check_gemm(name, d, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
   if (res && !aligned(res, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: residual must be 16-byte aligned", name);
-  if (i8 && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
+  if (scaled && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
   if (ld_out % 8 || ld_out < N || (res && (ld_res % 8 || ld_res < N)))
     return fail(GSN_ERR_UNSUPPORTED, "%s: row strides must be >= N and multiples of 8", name);
   if (int rc = check_lengths(name, lengths, T, M)) return rc;
-  GemmArgs g{(const __nv_bfloat16*)d, w, b, i8 ? scale : nullptr, (const __nv_bfloat16*)res, (__nv_bfloat16*)out,
-             ld_out, ld_res, M, N, K, i8, lengths, T};
+  GemmArgs g{(const __nv_bfloat16*)d, w, b, scaled ? scale : nullptr, (const __nv_bfloat16*)res,
+             (__nv_bfloat16*)out, ld_out, ld_res, M, N, K, i8, lengths, T};
   return finish(launch_gemm(g, kEpiResidual, (cudaStream_t)stream), name);
 }
 
 int gsn_gemm1_glu_bf16(const void* a, const void* w1_glu, const float* b1_glu, void* h, int M, int K, int N,
                        const int32_t* lengths, int T, gsn_stream_t stream) {
-  return gemm1(a, w1_glu, nullptr, b1_glu, h, M, K, N, lengths, T, 0, stream, "gsn_gemm1_glu_bf16");
+  return gemm1(a, w1_glu, nullptr, b1_glu, h, M, K, N, lengths, T, 0, 0, stream, "gsn_gemm1_glu_bf16");
 }
 
 int gsn_gemm1_glu_i8w(const void* a, const void* w1q_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
                       int K, int N, const int32_t* lengths, int T, gsn_stream_t stream) {
-  return gemm1(a, w1q_glu, s1_glu, b1_glu, h, M, K, N, lengths, T, 1, stream, "gsn_gemm1_glu_i8w");
+  return gemm1(a, w1q_glu, s1_glu, b1_glu, h, M, K, N, lengths, T, 1, 1, stream, "gsn_gemm1_glu_i8w");
+}
+
+int gsn_gemm1_glu_bf16s(const void* a, const void* w1_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
+                        int K, int N, const int32_t* lengths, int T, gsn_stream_t stream) {
+  return gemm1(a, w1_glu, s1_glu, b1_glu, h, M, K, N, lengths, T, 0, 1, stream, "gsn_gemm1_glu_bf16s");
 }
 
 int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, const void* residual, int64_t ld_res,
                             void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths, int T,
                             gsn_stream_t stream) {
-  return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 0, stream,
+  return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 0, 0, stream,
                "gsn_gemm2_residual_bf16");
 }
 
 int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, const float* b2, const void* residual,
                            int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
                            int T, gsn_stream_t stream) {
-  return gemm2(d, w2q, s2, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 1, stream,
+  return gemm2(d, w2q, s2, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 1, 1, stream,
                "gsn_gemm2_residual_i8w");
+}
+
+int gsn_gemm2_residual_bf16s(const void* d, const void* w2, const float* s2, const float* b2, const void* residual,
+                             int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
+                             int T, gsn_stream_t stream) {
+  return gemm2(d, w2, s2, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 0, 1, stream,
+               "gsn_gemm2_residual_bf16s");
+}
+
+int gsn_widen_i8_bf16(const void* q0, void* out0, int64_t n0, const void* q1, void* out1, int64_t n1,
+                      gsn_stream_t stream) {
+  const char* name = "gsn_widen_i8_bf16";
+  if (n0 < 0 || n1 < 0 || n0 % 16 || n1 % 16)
+    return fail(GSN_ERR_INVALID_ARG, "%s: sizes %lld, %lld must be non-negative multiples of 16", name,
+                (long long)n0, (long long)n1);
+  if ((n0 && (!q0 || !out0)) || (n1 && (!q1 || !out1))) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if ((n0 && (!aligned(q0, 16) || !aligned(out0, 16))) || (n1 && (!aligned(q1, 16) || !aligned(out1, 16))))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: pointers must be 16-byte aligned", name);
+  return finish(launch_widen_i8(q0, out0, n0, q1, out1, n1, (cudaStream_t)stream), name);
 }
 
 size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
@@ -261,6 +287,12 @@ size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
   const size_t M = (size_t)B * (size_t)T;
   const size_t wide = (size_t)(inner > D ? inner : D);
   return align256(M * (size_t)inner * 2) + align256(M * wide * 2);
+}
+
+size_t gsn_conv_module_i8w_workspace_bytes(int B, int T, int D, int inner) {
+  const size_t base = gsn_conv_module_workspace_bytes(B, T, D, inner);
+  if (base == 0) return 0;
+  return base + align256((size_t)2 * inner * D * 2) + align256((size_t)D * inner * 2);
 }
 
 static int conv_module(const void* x, const void* ln_w, const void* ln_b, const void* w1, const float* s1,
@@ -284,17 +316,30 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   if (!aligned(ws, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
   if (!aligned(x, 16) || !aligned(out, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: x/out must be 16-byte aligned", name);
 
-  // workspace: h = GLU output [M, inner]; t = LayerNorm output [M, D], later reused for the depthwise output
+  // workspace: h = GLU output [M, inner]; t = LayerNorm output [M, D], later reused for the depthwise output;
+  // int8 weights with room for them: w1 and w2 widened to bf16 after that
   __nv_bfloat16* h = (__nv_bfloat16*)ws;
   __nv_bfloat16* t = (__nv_bfloat16*)((char*)ws + align256((size_t)M * inner * 2));
   const cudaStream_t st = (cudaStream_t)stream;
+  int w_i8 = i8;
+  if (i8 && ws_bytes >= gsn_conv_module_i8w_workspace_bytes(B, T, D, inner)) {
+    if (!aligned(w1, 16) || !aligned(w2, 16))
+      return fail(GSN_ERR_UNSUPPORTED, "%s: int8 weights must be 16-byte aligned", name);
+    void* w1b = (char*)ws + need;
+    void* w2b = (char*)w1b + align256((size_t)2 * inner * D * 2);
+    int rc = launch_widen_i8(w1, w1b, (int64_t)2 * inner * D, w2, w2b, (int64_t)D * inner, st);
+    if (rc) return finish(rc, name);
+    w1 = w1b;
+    w2 = w2b;
+    w_i8 = 0;   // bf16 tiles from here on; the column scales stay
+  }
 
   // with lengths and T on the 128-frame grid, 128-row tiles of pure padding skip the LayerNorm and GEMM work
   const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
   int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
                             M, D, eps, skip, T, st);
   if (rc) return finish(rc, name);
-  GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, i8, skip, T};
+  GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, w_i8, skip, T};
   rc = launch_gemm(g1, kEpiGlu, st);
   if (rc) return finish(rc, name);
   DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
@@ -302,7 +347,7 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   rc = launch_dwconv(dw, st);
   if (rc) return finish(rc, name);
   GemmArgs g2{t, w2, b2, i8 ? s2 : nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr, (__nv_bfloat16*)out,
-              D, D, M, D, inner, i8, skip, T};
+              D, D, M, D, inner, w_i8, skip, T};
   rc = launch_gemm(g2, kEpiResidual, st);
   return finish(rc, name);
 }

@@ -78,6 +78,26 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_
   hi = pack_bf16x2(f2, f3);
 }
 
+// int8 -> bf16 (exact integers) for whole weight matrices: two arrays in one launch, 16 bytes per thread.
+__global__ void __launch_bounds__(256) widen_i8_kernel(const int8_t* __restrict__ q0, __nv_bfloat16* __restrict__ o0,
+                                                       int64_t n0, const int8_t* __restrict__ q1,
+                                                       __nv_bfloat16* __restrict__ o1, int64_t n1) {
+  const int64_t c0 = n0 / 16, c1 = n1 / 16;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c0 + c1; i += (int64_t)gridDim.x * blockDim.x) {
+    const bool first = i < c0;
+    const int64_t j = first ? i : i - c0;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(first ? q0 : q1) + j);
+    uint4 lo, hi;
+    i8x4_to_bf16x4(v.x, lo.x, lo.y);
+    i8x4_to_bf16x4(v.y, lo.z, lo.w);
+    i8x4_to_bf16x4(v.z, hi.x, hi.y);
+    i8x4_to_bf16x4(v.w, hi.z, hi.w);
+    uint4* dst = reinterpret_cast<uint4*>(first ? o0 : o1) + 2 * j;
+    dst[0] = lo;
+    dst[1] = hi;
+  }
+}
+
 // Shared-memory area of the four epilogue warps.
 struct __align__(1024) EpiSmem {
   uint8_t stage[4][2][BOX_BYTES];         // two staging boxes per warp, 64-byte swizzle
@@ -86,8 +106,9 @@ struct __align__(1024) EpiSmem {
 };
 
 // ------------------------------------------------------------------------------------------------------------
-// Epilogue of one warp (state lives in registers; one object per epilogue warp).
-template <int EPI, bool W_I8>
+// Epilogue of one warp (state lives in registers; one object per epilogue warp).  SCALED: the accumulator is
+// multiplied by a per-output-column scale (int8 weights, staged as int8 or already widened to bf16).
+template <int EPI, bool SCALED>
 struct Epilogue {
   static constexpr int NU = (EPI == kEpiGlu ? BN / 2 : BN) / BOX;   // 32-column output sub-tiles per tile
   float* vb;
@@ -124,7 +145,7 @@ struct Epilogue {
       float4 b = __ldg(src + lane + 32 * i);
       b.x *= h; b.y *= h; b.z *= h; b.w *= h;
       reinterpret_cast<float4*>(vb)[lane + 32 * i] = b;
-      if (W_I8) {
+      if (SCALED) {
         float4 sc = __ldg(reinterpret_cast<const float4*>(p.col_scale + nb) + lane + 32 * i);
         sc.x *= h; sc.y *= h; sc.z *= h; sc.w *= h;
         reinterpret_cast<float4*>(vs)[lane + 32 * i] = sc;
@@ -176,7 +197,7 @@ struct Epilogue {
           const int j = u * BOX + c4;
           const float4 ba = lds4(vb + j), bg = lds4(vb + BN / 2 + j);
           float4 sa = make_float4(0.5f, 0.5f, 0.5f, 0.5f), sg = sa;
-          if (W_I8) {
+          if (SCALED) {
             sa = lds4(vs + j);
             sg = lds4(vs + BN / 2 + j);
           }
@@ -205,7 +226,7 @@ struct Epilogue {
           const int j = u * BOX + c4;
           const float4 bb = lds4(vb + j);
           float4 sc = make_float4(1.f, 1.f, 1.f, 1.f);
-          if (W_I8) sc = lds4(vs + j);
+          if (SCALED) sc = lds4(vs + j);
           const float bv[4] = {bb.x, bb.y, bb.z, bb.w}, sv[4] = {sc.x, sc.y, sc.z, sc.w};
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -290,7 +311,7 @@ static_assert(offsetof(Smem<false>, b) % 1024 == 0 && offsetof(Smem<true>, b8) %
 static_assert(offsetof(Smem<false>, epi) % 1024 == 0 && offsetof(Smem<true>, epi) % 1024 == 0, "box alignment");
 static_assert(sizeof(Smem<false>) + 1024 <= 232448 && sizeof(Smem<true>) + 1024 <= 232448, "shared memory size");
 
-template <int EPI, bool W_I8>
+template <int EPI, bool W_I8, bool SCALED>
 __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, KParams p) {
@@ -436,7 +457,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int q = warp & 3;           // a warp may only read its own 32-lane quarter of TMEM
-    Epilogue<EPI, W_I8> epi;
+    Epilogue<EPI, SCALED> epi;
     epi.init(s.epi, warp - 2, &tmO, &tmR, p);
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -800,13 +821,13 @@ KParams make_params(const GemmArgs& a) {
   return p;
 }
 
-template <int EPI, bool W_I8>
+template <int EPI, bool W_I8, bool SCALED>
 int launch_single(const GemmArgs& a, cudaStream_t stream) {
   CUtensorMap tmA, tmW, tmO, tmR;
   if (int rc = encode_operands(a, EPI, BM, BN, &tmA, &tmW, &tmO, &tmR)) return rc;
   const KParams p = make_params(a);
   const int smem = (int)sizeof(Smem<W_I8>) + 1024;
-  auto kern = gemm_kernel<EPI, W_I8>;
+  auto kern = gemm_kernel<EPI, W_I8, SCALED>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
@@ -874,16 +895,35 @@ using namespace gemm_impl;
 #define GSN_GEMM_PAIR 0
 #endif
 
+int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* o1, int64_t n1,
+                    cudaStream_t stream) {
+  if (n0 % 16 || n1 % 16) return (int)cudaErrorInvalidValue;
+  const int64_t chunks = (n0 + n1) / 16;
+  if (chunks == 0) return 0;
+  const int64_t want = (chunks + 255) / 256;
+  const int64_t cap = 8LL * device_sm_count();
+  const int grid = (int)(want < cap ? want : cap);
+  widen_i8_kernel<<<grid, 256, 0, stream>>>((const int8_t*)q0, (__nv_bfloat16*)o0, n0, (const int8_t*)q1,
+                                            (__nv_bfloat16*)o1, n1);
+  return (int)cudaGetLastError();
+}
+
 int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
-  if (GSN_GEMM_PAIR && !a.w_int8) {
+  if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale) {
     bool launched = false;
     const int rc = epilogue == kEpiGlu ? launch_pair<kEpiGlu>(a, stream, &launched)
                                        : launch_pair<kEpiResidual>(a, stream, &launched);
     if (rc || launched) return rc;
   }
-  if (epilogue == kEpiGlu)
-    return a.w_int8 ? launch_single<kEpiGlu, true>(a, stream) : launch_single<kEpiGlu, false>(a, stream);
-  return a.w_int8 ? launch_single<kEpiResidual, true>(a, stream) : launch_single<kEpiResidual, false>(a, stream);
+  // int8 weights staged as int8 (widened per tile in shared memory), bf16 weights with a column scale (int8
+  // weights widened beforehand), plain bf16 weights
+  if (epilogue == kEpiGlu) {
+    if (a.w_int8) return launch_single<kEpiGlu, true, true>(a, stream);
+    return a.col_scale ? launch_single<kEpiGlu, false, true>(a, stream) : launch_single<kEpiGlu, false, false>(a, stream);
+  }
+  if (a.w_int8) return launch_single<kEpiResidual, true, true>(a, stream);
+  return a.col_scale ? launch_single<kEpiResidual, false, true>(a, stream)
+                     : launch_single<kEpiResidual, false, false>(a, stream);
 }
 
 }  // namespace gsn

@@ -41,6 +41,8 @@ struct GemmArgs {
 enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1 };
 
 int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
+// int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).
+int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* o1, int64_t n1, cudaStream_t stream);
 
 // ---- depthwise conv k=15 + bias + SiLU (dwconv.cu) -------------------------------------------------------
 // x: (B, C, T) logical, element strides sxB, sxC, sxT; y likewise.  GLU: x holds 2C channels (value | gate).

@@ -121,7 +121,7 @@ def _(x, weight, bias, lengths):
 
 # ---------------------------------------------------------------------------------------------------------------
 def _module_common(name: str, x: torch.Tensor, ln_w: torch.Tensor, dw_w: torch.Tensor,
-                   lengths: Optional[torch.Tensor]):
+                   lengths: Optional[torch.Tensor], size_fn: str = "gsn_conv_module_workspace_bytes"):
     if x.dim() != 3 or x.dtype != torch.bfloat16:
         raise RuntimeError(f"{name}: x must be bf16 [B, T, D], got {x.dtype} {tuple(x.shape)}")
     B, T, D = x.shape
@@ -131,7 +131,7 @@ def _module_common(name: str, x: torch.Tensor, ln_w: torch.Tensor, dw_w: torch.T
     xc = x.contiguous()
     lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
     out = torch.empty_like(xc)
-    nbytes = int(_lib.lib().gsn_conv_module_workspace_bytes(B, T, D, inner)) if B * T > 0 else 0
+    nbytes = int(getattr(_lib.lib(), size_fn)(B, T, D, inner)) if B * T > 0 else 0
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
     return xc, lens, out, ws, nbytes, B, T, D, inner
 
@@ -165,7 +165,9 @@ def conv_module_i8w(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w1q
     accumulate, the scale applied in the epilogue)."""
     name = "granite::conv_module_i8w"
     _require_cuda(name, x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths)
-    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(name, x, ln_w, dw_w, lengths)
+    # workspace with room for both weight matrices widened to bf16: the GEMMs then run on bf16 tiles
+    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(name, x, ln_w, dw_w, lengths,
+                                                               "gsn_conv_module_i8w_workspace_bytes")
     _lib.call("gsn_conv_module_i8w", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w1q_glu.data_ptr(),
               s1_glu.data_ptr(), b1_glu.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), w2q.data_ptr(), s2.data_ptr(),
               b2.data_ptr(), _ptr(lens), 1 if add_residual else 0, out.data_ptr(), B, T, D, inner, float(ln_eps),

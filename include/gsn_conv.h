@@ -93,6 +93,23 @@ int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, cons
                            int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
                            int T, gsn_stream_t stream);
 
+/* ---- int8 weights widened once per call -------------------------------------------------------------------
+ * No counterpart in the reference (its int8 analogue is torchao W8A8, bench_asr.py:92-105).  For large M the
+ * weight bytes are negligible next to the activations, so the int8 module widens both weight matrices to bf16
+ * (exact integers) once per call and runs the GEMMs on bf16 tiles, keeping the per-column scale in the epilogue.
+ * gsn_widen_i8_bf16 widens two int8 arrays (n0, n1 bytes, multiples of 16, 16-byte aligned; either may be 0) into
+ * bf16 arrays of 2 * n bytes.  gsn_gemm1_glu_bf16s / gsn_gemm2_residual_bf16s are gsn_gemm1_glu_i8w /
+ * gsn_gemm2_residual_i8w with those widened bf16 weights; results are bit-identical to the int8-staged forms. */
+int gsn_widen_i8_bf16(const void* q0, void* out0, int64_t n0, const void* q1, void* out1, int64_t n1,
+                      gsn_stream_t stream);
+
+int gsn_gemm1_glu_bf16s(const void* a, const void* w1_glu, const float* s1_glu, const float* b1_glu, void* h, int M,
+                        int K, int N, const int32_t* lengths, int T, gsn_stream_t stream);
+
+int gsn_gemm2_residual_bf16s(const void* d, const void* w2, const float* s2, const float* b2, const void* residual,
+                             int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
+                             int T, gsn_stream_t stream);
+
 /* ---- whole conv module + residual -------------------------------------------------------------------------
  * Replaces ConformerConvModule.forward (conformer.py:175-189) followed by the residual add of
  * ConformerBlock.forward (conformer.py:207), with BatchNorm folded (fold_bn.py:33-68):
@@ -110,6 +127,14 @@ int gsn_conv_module_bf16(const void* x, const void* ln_w, const void* ln_b, cons
                          const float* b1_glu, const void* dw_w, const void* dw_b, const void* w2, const float* b2,
                          const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
                          float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
+/* int8-weight module (w1q_glu [2*inner, D], w2q [D, inner] int8 with fp32 per-output-channel scales s1_glu, s2;
+ * no reference code: the nearest is torchao W8A8 in bench_asr.py:92-105).  With workspace_bytes >=
+ * gsn_conv_module_i8w_workspace_bytes(B, T, D, inner) both weight matrices are first widened to bf16 (exact
+ * integers) inside the workspace and the GEMMs run on bf16 tiles at the bf16 tensor rate; with at least
+ * gsn_conv_module_workspace_bytes(B, T, D, inner) the GEMMs widen each staged int8 W tile in shared memory
+ * instead.  Both give bit-identical results. */
+size_t gsn_conv_module_i8w_workspace_bytes(int B, int T, int D, int inner);
 
 int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const void* w1q_glu,
                         const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,

@@ -91,6 +91,34 @@ def test_module_int8_weights():
     assert_bf16_close(y, O.conv_module(x, prep, lengths=lens, mode="fused"), "int8 vs bf16 weights")
 
 
+@pytest.mark.parametrize("masked", [False, True])
+def test_module_int8_widened_weights_equal_staged(masked):
+    """The int8 module with room in the workspace (weights widened to bf16 once, GEMMs on bf16 tiles) and with the
+    minimum workspace (int8 W tiles widened in shared memory) give bit-identical outputs."""
+    from granite_conv_b200 import _lib
+    params = synth.make_params(1010)
+    p = prepare_from_params(params, device=DEV, int8=True)
+    B, T = 3, 256
+    x = _t(_x(1510, (B, T, synth.D_MODEL)))
+    lens = torch.tensor([256, 130, 7], dtype=torch.int32, device=DEV) if masked else None
+    L = _lib.lib()
+    D, inner = synth.D_MODEL, p.d_inner
+    small = int(L.gsn_conv_module_workspace_bytes(B, T, D, inner))
+    big = int(L.gsn_conv_module_i8w_workspace_bytes(B, T, D, inner))
+    assert big == small + 2 * inner * D * 2 + D * inner * 2
+    outs = []
+    for nbytes in (small, big):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+        out = torch.empty_like(x)
+        _lib.call("gsn_conv_module_i8w", x.data_ptr(), p.ln_w.data_ptr(), p.ln_b.data_ptr(), p.w1q_glu.data_ptr(),
+                  p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), p.dw_w.data_ptr(), p.dw_b.data_ptr(), p.w2q.data_ptr(),
+                  p.s2.data_ptr(), p.b2.data_ptr(), None if lens is None else lens.data_ptr(), 1, out.data_ptr(),
+                  B, T, D, inner, float(p.ln_eps), ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_module_full_size_batch_independence():
     """Config-3 shape (B=48, lognormal lengths, T on the 128 grid): every utterance of the padded batch equals the
     same module run on that utterance alone, trimmed to its length (size-independent property), and two
