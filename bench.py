@@ -37,10 +37,9 @@ N_UTTS = 512
 D, I = synth.D_MODEL, synth.D_INNER
 GEMM1_FLOP_PER_FRAME = 2 * D * 2 * I          # 8.389 MFLOP
 GEMM2_FLOP_PER_FRAME = 2 * I * D              # 4.194 MFLOP
-# DRAM bytes (read + write) of the up_conv + GLU GEMM per row of the 128-row tiles it computes, from one ncu capture
-# of a B=48, T=1536 chunk (profiles/gemm_conv_module_b48_t1536.md: 72.3 + 84.2 MB over 31,104 rows); the traffic
-# of a launch scales with the rows it computes.
-GEMM1_DRAM_BYTES_PER_ROW = 5032
+# DRAM bytes (read + write) of the fused up_conv + GLU + depthwise kernel per row of the 128-row tiles it computes,
+# from one ncu capture (None until that capture is summarised); the traffic of a launch scales with its rows.
+GEMM1DW_DRAM_BYTES_PER_ROW = None
 DW_BYTES_PER_FRAME = 2 * I * 2                # read + write bf16: 8192 B
 METRIC = "conv-module frames/s at 1/2/4/8 B200; % of HBM / tensor-pipe roofline"
 
@@ -272,17 +271,18 @@ def run_ours(args):
     act = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]   # ping-pong buffers
     act2 = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
 
-    layer_events = []      # per recorded layer: (events[5], chunk) around layernorm, gemm1, dwconv, gemm2
+    layer_events = []      # per recorded layer: (events[4], chunk) around layernorm, gemm1 + dwconv, gemm2
     widen_events = []      # int8: per recorded layer, the events around the weight widening
 
     def layer_kernels(x, out, c, p, lens, record):
-        """The kernels of one conv module (the same launches gsn_conv_module_* makes), with CUDA events between
+        """The kernels of one conv module (the same launches gsn_conv_module_* makes for T on the 128 grid):
+        LayerNorm, up_conv + GLU + depthwise + SiLU in one kernel, down_conv + residual; with CUDA events between
         them when `record`."""
         M = c.padded_frames
-        hp = h_buf.data_ptr()
-        tp = h_buf.data_ptr() + t_off
+        dp = h_buf.data_ptr()                   # depthwise output [M, I]
+        tp = h_buf.data_ptr() + t_off           # LayerNorm output [M, D]
         lp, T = lens.data_ptr(), c.T
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if int8:
             wev = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None
             if record:
@@ -298,26 +298,19 @@ def run_ours(args):
                                         p.ln_eps, lp, T, sp), "layernorm")
         if record:
             ev[1].record(stream)
-        if int8:
-            _lib.check(L.gsn_gemm1_glu_bf16s(tp, w1b.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), hp,
-                                             M, D, 2 * I, lp, T, sp), "gemm1")
-        else:
-            _lib.check(L.gsn_gemm1_glu_bf16(tp, p.w1_glu.data_ptr(), p.b1_glu.data_ptr(), hp, M, D, 2 * I, lp, T,
-                                            sp), "gemm1")
+        w1, s1 = (w1b.data_ptr(), p.s1_glu.data_ptr()) if int8 else (p.w1_glu.data_ptr(), None)
+        _lib.check(L.gsn_gemm1_glu_dwconv_bf16(tp, w1, s1, p.b1_glu.data_ptr(), p.dw_w.data_ptr(),
+                                               p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp, sp), "gemm1_dw")
         if record:
             ev[2].record(stream)
-        _lib.check(L.gsn_dwconv_silu_bf16(hp, p.dw_w.data_ptr(), p.dw_b.data_ptr(), tp, c.B, I, c.T, 15,
-                                          c.T * I, 1, I, c.T * I, 1, I, lp, sp), "dwconv")
-        if record:
-            ev[3].record(stream)
         if int8:
-            _lib.check(L.gsn_gemm2_residual_bf16s(tp, w2b.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
+            _lib.check(L.gsn_gemm2_residual_bf16s(dp, w2b.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
                                                   x.data_ptr(), D, out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
         else:
-            _lib.check(L.gsn_gemm2_residual_bf16(tp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
+            _lib.check(L.gsn_gemm2_residual_bf16(dp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
                                                  out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
         if record:
-            ev[4].record(stream)
+            ev[3].record(stream)
             layer_events.append((ev, c))
 
     dw_events = []
@@ -343,7 +336,7 @@ def run_ours(args):
                 dst = act[ci] if li % 2 == 0 else act2[ci]
                 layer_kernels(src, dst, c, p, lens_dev[ci], record)
                 src = dst
-                n += 5 if int8 else 4
+                n += 4 if int8 else 3
         return n
 
     def barrier():
@@ -392,12 +385,13 @@ def run_ours(args):
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
     else:
         kernels = _kernel_breakdown(layer_events, peaks, widen_events)
-        g1 = kernels["gemm1_glu"]
-        roof = {"kernel": "gemm_kernel<GLU> (up_conv 1024->4096 + GLU)", "bound": "tensor",
+        g1 = kernels["gemm1_glu_dw"]
+        traffic = None if GEMM1DW_DRAM_BYTES_PER_ROW is None else g1["rows_per_launch"] * GEMM1DW_DRAM_BYTES_PER_ROW
+        roof = {"kernel": "gemm_glu_dw_kernel (up_conv 1024->4096 + GLU + depthwise k15 + SiLU)", "bound": "tensor",
                 "achieved": g1["achieved"], "peak": g1["peak"], "unit": "TFLOP/s", "frac": g1["frac"],
-                "traffic": g1["rows_per_launch"] * GEMM1_DRAM_BYTES_PER_ROW,
+                "traffic": traffic,
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per computed row, scaled to the "
-                                  "average launch (profiles/gemm_conv_module_b48_t1536.md)",
+                                  "average launch (profiles/gemm_glu_dw_b48_t1536.md)",
                 "algorithmic_bytes": g1["rows_per_launch"] * (2 * D + 2 * I), "per_launch_ms": g1["ms_per_launch"],
                 "algorithmic_flop_per_frame": GEMM1_FLOP_PER_FRAME,
                 "frames_counted": "rows of the 128-row tiles holding valid frames (tiles of pure padding are "
@@ -437,9 +431,9 @@ def _tile_rows(c, tile=128):
 def _kernel_breakdown(layer_events, peaks, widen_events=()):
     """Average launch time, share of the recorded kernel time and achieved rate of each kernel.
     Work per launch: LayerNorm reads and writes the valid frames (2 x 2 KB); the GEMMs compute the rows of the
-    128-row tiles that hold valid frames; the depthwise kernel reads the valid frames and writes every frame
-    (4 KB each way per frame); the int8 weight widening reads 1 byte and writes 2 per weight."""
-    names = ("layernorm", "gemm1_glu", "dwconv_silu", "gemm2_residual")
+    128-row tiles that hold valid frames (the up_conv kernel also runs GLU and the depthwise conv on them, counted
+    as its GEMM FLOPs only); the int8 weight widening reads 1 byte and writes 2 per weight."""
+    names = ("layernorm", "gemm1_glu_dw", "gemm2_residual")
     tot = {n: 0.0 for n in names}
     work = {n: 0.0 for n in names}
     if widen_events:
@@ -447,14 +441,12 @@ def _kernel_breakdown(layer_events, peaks, widen_events=()):
         tot["widen_i8"] = sum(a.elapsed_time(b) for a, b in widen_events) * len(layer_events) / len(widen_events)
         work["widen_i8"] = 3.0 * (2 * I * D + D * I) * len(layer_events)
     for ev, c in layer_events:
-        m = c.padded_frames
-        for k, n in enumerate(names[-4:]):
+        for k, n in enumerate(names[-3:]):
             tot[n] += ev[k].elapsed_time(ev[k + 1])
         valid = c.valid_frames
         rows = _tile_rows(c)
         work["layernorm"] += valid * 2 * D * 2
-        work["gemm1_glu"] += rows * GEMM1_FLOP_PER_FRAME
-        work["dwconv_silu"] += valid * I * 2 + m * I * 2
+        work["gemm1_glu_dw"] += rows * GEMM1_FLOP_PER_FRAME
         work["gemm2_residual"] += rows * GEMM2_FLOP_PER_FRAME
     all_ms = sum(tot.values())
     out = {}
@@ -464,7 +456,7 @@ def _kernel_breakdown(layer_events, peaks, widen_events=()):
         pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
         out[n] = {"ms_per_launch": tot[n] / len(layer_events), "share": tot[n] / all_ms, "achieved": ach,
                   "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
-    out["gemm1_glu"]["rows_per_launch"] = work["gemm1_glu"] / GEMM1_FLOP_PER_FRAME / len(layer_events)
+    out["gemm1_glu_dw"]["rows_per_launch"] = work["gemm1_glu_dw"] / GEMM1_FLOP_PER_FRAME / len(layer_events)
     return out
 
 

@@ -270,6 +270,25 @@ int gsn_gemm2_residual_bf16s(const void* d, const void* w2, const float* s2, con
                "gsn_gemm2_residual_bf16s");
 }
 
+int gsn_gemm1_glu_dwconv_bf16(const void* a, const void* w1_glu, const float* s1_glu, const float* b1_glu,
+                              const void* dw_w, const void* dw_b, void* d, int B, int T, int K, int N,
+                              const int32_t* lengths, gsn_stream_t stream) {
+  const char* name = "gsn_gemm1_glu_dwconv_bf16";
+  if (B < 0 || T < 0 || K <= 0 || N <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d K=%d N=%d", name, B, T, K, N);
+  if ((int64_t)B * T == 0) return ok();
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  if (!a || !w1_glu || !b1_glu || !dw_w || !dw_b || !d) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (T % 128 || K % 64 || N % 256)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: needs T %% 128 == 0, K %% 64 == 0, N %% 256 == 0 (T=%d K=%d N=%d)", name, T,
+                K, N);
+  if (!aligned(a, 16) || !aligned(w1_glu, 16) || !aligned(d, 16) || !aligned(b1_glu, 16) ||
+      (s1_glu && !aligned(s1_glu, 16)) || !aligned(dw_w, 2) || !aligned(dw_b, 2))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: a, w1, d, b1, s1 must be 16-byte aligned", name);
+  GemmDwArgs g{(const __nv_bfloat16*)a, (const __nv_bfloat16*)w1_glu, b1_glu, s1_glu, (const __nv_bfloat16*)dw_w,
+               (const __nv_bfloat16*)dw_b, (__nv_bfloat16*)d, lengths, B, T, K, N};
+  return finish(launch_gemm_glu_dw(g, (cudaStream_t)stream), name);
+}
+
 int gsn_widen_i8_bf16(const void* q0, void* out0, int64_t n0, const void* q1, void* out1, int64_t n1,
                       gsn_stream_t stream) {
   const char* name = "gsn_widen_i8_bf16";
@@ -316,7 +335,8 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   if (!aligned(ws, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
   if (!aligned(x, 16) || !aligned(out, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: x/out must be 16-byte aligned", name);
 
-  // workspace: h = GLU output [M, inner]; t = LayerNorm output [M, D], later reused for the depthwise output;
+  // workspace: h = GLU output [M, inner]; t = LayerNorm output [M, D], later reused for the depthwise output
+  // (with T on the 128 grid the GLU tensor is never materialised and the depthwise output takes h's place);
   // int8 weights with room for them: w1 and w2 widened to bf16 after that
   __nv_bfloat16* h = (__nv_bfloat16*)ws;
   __nv_bfloat16* t = (__nv_bfloat16*)((char*)ws + align256((size_t)M * inner * 2));
@@ -339,15 +359,26 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
                             M, D, eps, skip, T, st);
   if (rc) return finish(rc, name);
-  GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, w_i8, skip, T};
-  rc = launch_gemm(g1, kEpiGlu, st);
-  if (rc) return finish(rc, name);
-  DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
-            (int64_t)T * inner, 1, inner, (int64_t)T * inner, 1, inner, B, inner, T, 0};
-  rc = launch_dwconv(dw, st);
-  if (rc) return finish(rc, name);
-  GemmArgs g2{t, w2, b2, i8 ? s2 : nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr, (__nv_bfloat16*)out,
-              D, D, M, D, inner, w_i8, skip, T};
+  // the depthwise input: d = the depthwise output, [M, inner]
+  const __nv_bfloat16* dsrc = t;
+  if (T % 128 == 0 && !w_i8) {
+    // frames on the 128 grid: GLU and depthwise run inside the up_conv GEMM; d goes to h's place
+    GemmDwArgs gd{t, (const __nv_bfloat16*)w1, b1, i8 ? s1 : nullptr, (const __nv_bfloat16*)dw_w,
+                  (const __nv_bfloat16*)dw_b, h, lengths, B, T, D, 2 * inner};
+    rc = launch_gemm_glu_dw(gd, st);
+    if (rc) return finish(rc, name);
+    dsrc = h;
+  } else {
+    GemmArgs g1{t, w1, b1, i8 ? s1 : nullptr, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, w_i8, skip, T};
+    rc = launch_gemm(g1, kEpiGlu, st);
+    if (rc) return finish(rc, name);
+    DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
+              (int64_t)T * inner, 1, inner, (int64_t)T * inner, 1, inner, B, inner, T, 0};
+    rc = launch_dwconv(dw, st);
+    if (rc) return finish(rc, name);
+  }
+  GemmArgs g2{dsrc, w2, b2, i8 ? s2 : nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr,
+              (__nv_bfloat16*)out, D, D, M, D, inner, w_i8, skip, T};
   rc = launch_gemm(g2, kEpiResidual, st);
   return finish(rc, name);
 }

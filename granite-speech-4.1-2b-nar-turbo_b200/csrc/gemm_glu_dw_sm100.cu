@@ -1,0 +1,485 @@
+// up_conv + GLU with the depthwise conv k=15 (+ folded BatchNorm bias) + SiLU fused into the GEMM epilogue, on
+// sm_100a: the GLU tensor [M, inner] never leaves the SM.
+//
+//   up_conv (models/granite_speech_nar/conformer.py:165,177) + GLU (:166,:181) + depthwise (:134-155,:168-169)
+//   + SiLU (:186): d[b, t, c] = silu(bdw[c] + sum_{j<15} wdw[c, j] * glu(a W1^T + b1)[b, t - 7 + j, c])
+//
+// Work unit: one utterance b and one block of 128 GLU channels (256 GEMM columns: [128 value | 128 gate] rows of
+// the GLU-interleaved W1).  A CTA walks the unit's 128-frame tiles in time order, so each tile's depthwise
+// outputs need only the last 14 GLU rows of the previous tile, which stay in shared memory: nothing is
+// recomputed and the GLU rows are never written to global memory.  Units are ordered longest utterance first
+// (channel block fastest, so the 16 CTAs sharing an utterance's A tiles run together and read them from L2) and
+// dealt to the persistent CTAs in a snake order.
+//
+// Roles (320 threads, one CTA per SM):
+//   warp 0      TMA producer: A 128x64 (frames of the tile) + W 256x64 per stage, 128-byte swizzle, 3 stages
+//   warp 1      TMEM allocator (2 x 256 columns) and single-thread UMMA issuer, M=128 N=256 K=16
+//   warps 2-9   epilogue.  Per tile: (1) TMEM -> GLU -> bf16 rows 14..141 of the staging window (warp w reads
+//               its TMEM lane quarter w % 4, warps 2-5 the first 64 channels, 6-9 the last 64); the accumulator
+//               buffer is released right after; (2) depthwise + SiLU over the window: lane = 4 channels, warp =
+//               16 output frames, weights (halved) in registers, fp32x2 FMAs in the order of the standalone
+//               depthwise kernel, so the result is bit-identical to GEMM -> GLU tensor -> depthwise kernel;
+//               (3) window rows 128..141 move to rows 0..13 for the next tile.  After the last tile a flush pass
+//               computes the final 7 frames with zero GLU rows on the right.
+// Lengths: GLU rows of frames t >= len[b] are zero, depthwise frames in [len, roundup128(len)) are written as
+// zero (the residual GEMM reads whole 128-row tiles), frames beyond are never touched.
+#include "gsn_kernels.cuh"
+#include "gsn_ptx.cuh"
+
+namespace gsn {
+
+namespace gdw_impl {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGES = 3;
+constexpr int EPI_WARPS = 8;
+constexpr int EPI_THREADS = 32 * EPI_WARPS;
+constexpr int THREADS = 64 + EPI_THREADS;
+constexpr int CH = BN / 2;                 // GLU channels per unit
+constexpr int KW = 15, HALO = 7;
+constexpr int WROWS = BM + 2 * HALO;       // staging window: 14 rows of the previous tile + the tile's 128
+constexpr int WPITCH = CH * 2 + 16;        // 272 bytes: 16-byte row stores of consecutive lanes hit distinct banks
+constexpr int MAX_SORT_B = 512;            // utterances ordered by length up to this batch size
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int kEpiBar = 1;                 // named barrier of the epilogue warps
+
+struct Params {
+  const float* bias;          // [N] GLU-interleaved, fp32
+  const float* col_scale;     // [N] or null
+  const __nv_bfloat16* dw_w;  // [inner, 15]
+  const __nv_bfloat16* dw_b;  // [inner]
+  __nv_bfloat16* d;           // [B * T, inner]
+  const int* lengths;         // [B] or null
+  int B, T, K, N;
+};
+
+struct __align__(1024) Smem {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint8_t win[WROWS * WPITCH];
+  float vb[BN];               // the unit's GLU bias columns, halved
+  float vs[BN];               // the unit's column scales, halved (0.5 without scales)
+  int lens[MAX_SORT_B];       // clamped lengths
+  short order[MAX_SORT_B];    // utterances, most tiles first
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(offsetof(Smem, b) % 1024 == 0 && offsetof(Smem, win) % 16 == 0, "alignment");
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory size");
+
+typedef uint64_t pk2;
+__device__ __forceinline__ pk2 pk_from_bf16x2(uint32_t v) {
+  pk2 d;
+  asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xFFFF0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+      : "=l"(d) : "r"(v));
+  return d;
+}
+__device__ __forceinline__ pk2 pk_make(float lo, float hi) {
+  pk2 d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ float2 pk_split(pk2 v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+__device__ __forceinline__ pk2 pk_fma(pk2 a, pk2 b, pk2 c) {
+  pk2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync %0, %1;" ::"n"(kEpiBar), "n"(EPI_THREADS) : "memory"); }
+
+// The unit sequence, identical in every role: utterance rank r (most tiles first) x channel block, dealt to the
+// CTAs in snake order over the passes of gridDim.x units.
+struct Units {
+  const Smem* s;
+  const int* lengths;
+  int B, T, nb, total;
+  bool sorted;
+  __device__ int len_of(int b) const {
+    if (sorted) return s->lens[b];
+    return lengths ? min(max(__ldg(lengths + b), 0), T) : T;
+  }
+  // step-th unit of this CTA: false when there is none; else the utterance, channel block and length
+  __device__ bool get(int step, int& b, int& n_blk, int& len) const {
+    const int G = gridDim.x, j = blockIdx.x;
+    const int i = step * G + ((step & 1) ? (G - 1 - j) : j);
+    if (i >= total) return false;
+    const int r = i / nb;
+    n_blk = i - r * nb;
+    b = sorted ? s->order[r] : r;
+    len = len_of(b);
+    return true;
+  }
+};
+
+template <bool SCALED>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, Params p) {
+  constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = warp_id();
+  const int lane = threadIdx.x & 31;
+  const int num_kb = p.K / BK;
+  const int inner = p.N / 2;
+  const bool sorted = p.B <= MAX_SORT_B;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], EPI_WARPS);
+    }
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  // lengths, then the longest-first order (rank = utterances with more tiles, ties by index)
+  if (sorted) {
+    for (int b = threadIdx.x; b < p.B; b += THREADS)
+      s.lens[b] = p.lengths ? min(max(__ldg(p.lengths + b), 0), p.T) : p.T;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (sorted) {
+    for (int b = threadIdx.x; b < p.B; b += THREADS) {
+      const int nt = (s.lens[b] + BM - 1) / BM;
+      int rank = 0;
+      for (int o = 0; o < p.B; ++o) {
+        const int no = (s.lens[o] + BM - 1) / BM;
+        rank += (no > nt) || (no == nt && o < b);
+      }
+      s.order[rank] = (short)b;
+    }
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+  const Units units{&s, p.lengths, p.B, p.T, p.N / BN, p.B * (p.N / BN), sorted};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    const uint64_t pol_w = l2_policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    int b, n_blk, len;
+    for (int step = 0; ok && units.get(step, b, n_blk, len); ++step) {
+      const int nt = (len + BM - 1) / BM;
+      for (int k = 0; k < nt && ok; ++k) {
+        const int row0 = b * p.T + k * BM;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          bool got = mbar_wait_bounded(&s.empty[stage], phase ^ 1u, abort_flag, kStatusTimeoutProducer);
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES);
+            tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, row0);
+            tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
+          }
+          __syncwarp();
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      // unwinding after a timeout: the last STAGES loads may still be in flight
+      for (int back = 1; back <= STAGES && back <= issued; ++back) {
+        const int idx = issued - back;
+        mbar_wait_bounded(&s.full[idx % STAGES], (uint32_t)((idx / STAGES) & 1), nullptr, kStatusTimeoutProducer,
+                          100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- UMMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int local = 0;
+    int b, n_blk, len;
+    for (int step = 0; ok && units.get(step, b, n_blk, len); ++step) {
+      const int nt = (len + BM - 1) / BM;
+      for (int k = 0; k < nt && ok; ++k) {
+        const int acc = local & 1;
+        const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+        ++local;
+        bool got = mbar_wait_bounded(&s.tempty[acc], use_par ^ 1u, abort_flag, kStatusTimeoutMma);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          bool ready = mbar_wait_bounded(&s.full[stage], phase, abort_flag, kStatusTimeoutMma);
+          ready = __shfl_sync(0xffffffffu, ready, 0);
+          if (!ready) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(s.a[stage]));
+            const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.b[stage]));
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_f16(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), IDESC,
+                       (kb | kk) != 0 ? 1u : 0u);
+            umma_commit(&s.empty[stage]);
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (lane == 0) umma_commit(&s.tfull[acc]);
+        __syncwarp();
+      }
+    }
+    if (lane == 0) umma_commit(&s.mma_done);
+    __syncwarp();
+    mbar_wait_bounded(&s.mma_done, 0, nullptr, kStatusTimeoutMma, 100000000ull);
+  } else {
+    // ---------------------------------------------------------------- epilogue: GLU -> window -> depthwise
+    // Every epilogue warp runs the same unit / tile sequence and meets every named barrier, also after a wait
+    // ran out (ok == false: the work is skipped, the barriers are not), so the barrier counts always match.
+    const int e = warp - 2;             // 0..7
+    const int et = threadIdx.x - 64;    // 0..255
+    const int q = warp & 3;             // TMEM lane quarter of this warp
+    const int half = e >> 2;            // GLU channels [64 * half, 64 * half + 64)
+    bool ok = true;
+    int local = 0;
+    int b, n_blk, len;
+    for (int step = 0; units.get(step, b, n_blk, len); ++step) {
+      const int nt = (len + BM - 1) / BM;
+      if (nt == 0) continue;
+      const int c0 = n_blk * CH;                         // first GLU / depthwise channel of the unit
+      const int store_end = min(nt * BM, p.T);           // frames written: [0, len) values, [len, store_end) zero
+      __nv_bfloat16* drow = p.d + (int64_t)b * p.T * inner + c0 + lane * 4;
+
+      // unit setup: bias / scale columns, zero left halo (frames -14..-1), this lane's depthwise weights
+      epi_bar();
+      {
+        const float bv = __ldg(p.bias + n_blk * BN + et);
+        s.vb[et] = 0.5f * bv;
+        s.vs[et] = SCALED ? 0.5f * __ldg(p.col_scale + n_blk * BN + et) : 0.5f;
+        if (et < 2 * HALO * 16) {
+          const int r = et >> 4, c = et & 15;
+          *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      pk2 wr[KW][2];
+      pk2 wb[2];
+      {
+        const __nv_bfloat16* wp = p.dw_w + (int64_t)(c0 + lane * 4) * KW;
+#pragma unroll
+        for (int j = 0; j < KW; ++j)
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq)
+            wr[j][qq] = pk_make(0.5f * __bfloat162float(wp[(2 * qq) * KW + j]),
+                                0.5f * __bfloat162float(wp[(2 * qq + 1) * KW + j]));
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq)
+          wb[qq] = pk_make(0.5f * __bfloat162float(p.dw_b[c0 + lane * 4 + 2 * qq]),
+                           0.5f * __bfloat162float(p.dw_b[c0 + lane * 4 + 2 * qq + 1]));
+      }
+      epi_bar();
+
+      for (int k = 0; k <= nt; ++k) {
+        const int t0 = k * BM;                           // frame of window row 14
+        const bool flush = k == nt;
+        if (!flush) {
+          // (1) accumulator -> GLU -> window rows 14 + r, r = this lane's row of the tile
+          const int acc = local & 1;
+          const uint32_t use_par = (uint32_t)((local >> 1) & 1);
+          ++local;
+          if (ok) {
+            bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
+            ok = __shfl_sync(0xffffffffu, got, 0);
+          }
+          if (ok) {
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            const int r = q * 32 + lane;
+            const bool valid = t0 + r < len;
+            uint8_t* wrow = s.win + (2 * HALO + r) * WPITCH;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int cb = half * 64 + u * 32;         // first of this sub-tile's 32 GLU channels
+              uint32_t va[2][16], vg[2][16];
+              tmem_ld16(t_row + (uint32_t)cb, va[0]);
+              tmem_ld16(t_row + (uint32_t)(cb + 16), va[1]);
+              tmem_ld16(t_row + (uint32_t)(CH + cb), vg[0]);
+              tmem_ld16(t_row + (uint32_t)(CH + cb + 16), vg[1]);
+              tmem_wait_ld_dep(va[0], va[1]);
+              tmem_wait_ld_dep(vg[0], vg[1]);
+              uint32_t o[16];
+#pragma unroll
+              for (int c = 0; c < 32; c += 2) {
+                float h2[2];
+#pragma unroll
+                for (int z = 0; z < 2; ++z) {
+                  const int kk = c + z;
+                  const float a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
+                  const float g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[CH + cb + kk],
+                                       s.vb[CH + cb + kk]);
+                  h2[z] = fmaf(a, tanh_approx(g), a);
+                }
+                o[c >> 1] = valid ? pack_bf16x2(h2[0], h2[1]) : 0u;
+              }
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(wrow + cb * 2 + c * 16) =
+                    make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+            }
+          }
+          // the accumulator buffer is free for the next tile's MMAs
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tempty[acc]);
+        } else if (et < 2 * HALO * 16) {
+          // flush: the frames after the last tile are past the utterance, i.e. zero GLU rows
+          const int r = 2 * HALO + (et >> 4), c = et & 15;
+          *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        epi_bar();
+
+        // (2) depthwise + SiLU: output frame t0 - 7 + i reads window rows i .. i + 14.  Warp e owns i in
+        // [16e, 16e + 16) as two passes of 8 frames; the flush only needs i in [0, 7) (warp 0, one pass).
+        const int passes = flush ? (e == 0 ? 1 : 0) : 2;
+        for (int ps = 0; ps < passes && ok; ++ps) {
+          const int i0 = e * 16 + ps * 8;
+          const uint8_t* xb = s.win + i0 * WPITCH + lane * 8;
+          pk2 acc[8][2];
+#pragma unroll
+          for (int r = 0; r < 8 + 2 * HALO; ++r) {
+            const uint2 v = *reinterpret_cast<const uint2*>(xb + r * WPITCH);
+            const pk2 xv[2] = {pk_from_bf16x2(v.x), pk_from_bf16x2(v.y)};
+#pragma unroll
+            for (int f = 0; f < 8; ++f) {
+              const int j = r - f;
+              if (j >= 0 && j < KW) {
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) acc[f][qq] = pk_fma(wr[j][qq], xv[qq], j == 0 ? wb[qq] : acc[f][qq]);
+              }
+            }
+          }
+#pragma unroll
+          for (int f = 0; f < 8; ++f) {
+            const int t = t0 - HALO + i0 + f;
+            if (t < 0 || t >= store_end) continue;
+            uint32_t o[2];
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) {
+              const float2 hh = pk_split(acc[f][qq]);
+              const float2 s2 = pk_split(pk_fma(acc[f][qq], pk_make(tanh_approx(hh.x), tanh_approx(hh.y)), acc[f][qq]));
+              o[qq] = t < len ? pack_bf16x2(s2.x, s2.y) : 0u;
+            }
+            *reinterpret_cast<uint2*>(drow + (int64_t)t * inner) = make_uint2(o[0], o[1]);
+          }
+        }
+        epi_bar();
+        if (!flush) {
+          // (3) the tile's last 14 rows become the next window's left halo
+          if (et < 2 * HALO * 16) {
+            const int r = et >> 4, c = et & 15;
+            *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) =
+                *reinterpret_cast<const uint4*>(s.win + (BM + r) * WPITCH + c * 16);
+          }
+          epi_bar();
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gdw_impl
+
+int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
+  namespace G = gdw_impl;
+  if (a.B <= 0 || a.T <= 0) return 0;
+  if (a.T % G::BM || a.K % G::BK || a.N % G::BN) return (int)cudaErrorInvalidValue;
+  CUtensorMap tmA, tmW;
+  const int64_t M = (int64_t)a.B * a.T;
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)a.K * 2};
+    const uint32_t box[2] = {G::BK, G::BM};
+    if (int rc = encode_tmap(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
+    const uint64_t strides[1] = {(uint64_t)a.K * 2};
+    const uint32_t box[2] = {G::BK, G::BN};
+    if (int rc = encode_tmap(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  G::Params p;
+  p.bias = a.bias;
+  p.col_scale = a.col_scale;
+  p.dw_w = a.dw_w;
+  p.dw_b = a.dw_b;
+  p.d = a.d;
+  p.lengths = a.lengths;
+  p.B = a.B;
+  p.T = a.T;
+  p.K = a.K;
+  p.N = a.N;
+  const int smem = (int)sizeof(G::Smem) + 1024;
+  auto kern = a.col_scale ? G::gemm_glu_dw_kernel<true> : G::gemm_glu_dw_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  const int64_t units = (int64_t)a.B * (a.N / G::BN);
+  const int sms = device_sm_count();
+  const int grid = (int)(units < sms ? units : sms);
+  if (grid <= 0) return 0;
+  kern<<<grid, G::THREADS, smem, stream>>>(tmA, tmW, p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace gsn

@@ -3,4 +3,5 @@
 #include "layernorm.cu"
 #include "dwconv.cu"
 #include "gemm_sm100.cu"
+#include "gemm_glu_dw_sm100.cu"
 #include "capi.cu"

@@ -44,6 +44,21 @@ int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
 // int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).
 int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* o1, int64_t n1, cudaStream_t stream);
 
+// ---- up_conv + GLU + depthwise + SiLU in one kernel (gemm_glu_dw_sm100.cu) ------------------------------------
+// a: [B*T, K] bf16; w: [N, K] bf16 GLU-interleaved (N = 2 * inner); d: [B*T, inner] bf16.  T % 128 == 0.
+struct GemmDwArgs {
+  const __nv_bfloat16* a;
+  const __nv_bfloat16* w;
+  const float* bias;             // [N] GLU-interleaved
+  const float* col_scale;        // [N] or null
+  const __nv_bfloat16* dw_w;     // [inner, 15]
+  const __nv_bfloat16* dw_b;     // [inner]
+  __nv_bfloat16* d;
+  const int* lengths;            // [B] or null
+  int B, T, K, N;
+};
+int launch_gemm_glu_dw(const GemmDwArgs& args, cudaStream_t stream);
+
 // ---- depthwise conv k=15 + bias + SiLU (dwconv.cu) -------------------------------------------------------
 // x: (B, C, T) logical, element strides sxB, sxC, sxT; y likewise.  GLU: x holds 2C channels (value | gate).
 struct DwArgs {

@@ -221,6 +221,21 @@ def gemm1_glu(a: torch.Tensor, w_glu: torch.Tensor, b_glu: torch.Tensor, scale_g
     return h
 
 
+def gemm1_glu_dwconv(a: torch.Tensor, w_glu: torch.Tensor, b_glu: torch.Tensor, dw_w: torch.Tensor,
+                     dw_b: torch.Tensor, B: int, T: int, scale_glu: Optional[torch.Tensor] = None,
+                     lengths: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """d = silu(depthwise(GLU(a @ W1^T + b1))) in one kernel, a = [B*T, K] frames (T % 128 == 0), bf16 weights
+    (scale_glu: int8 weights already widened to bf16).  With lengths, d frames in [len, roundup128(len)) are zero
+    and frames past that are left as they were in `out`."""
+    _require_cuda("gemm1_glu_dwconv", a, w_glu, b_glu, dw_w, dw_b, scale_glu, lengths)
+    M, K = a.shape
+    N = w_glu.shape[0]
+    d = torch.empty((M, N // 2), dtype=torch.bfloat16, device=a.device) if out is None else out
+    _lib.call("gsn_gemm1_glu_dwconv_bf16", a.data_ptr(), w_glu.data_ptr(), _ptr(scale_glu), b_glu.data_ptr(),
+              dw_w.data_ptr(), dw_b.data_ptr(), d.data_ptr(), B, T, K, N, _ptr(lengths), _stream(a))
+    return d
+
+
 def gemm2_residual(d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, residual: Optional[torch.Tensor],
                    scale: Optional[torch.Tensor] = None, lengths: Optional[torch.Tensor] = None,
                    T: int = 0) -> torch.Tensor:

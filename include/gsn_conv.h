@@ -93,6 +93,20 @@ int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, cons
                            int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths,
                            int T, gsn_stream_t stream);
 
+/* ---- up_conv + GLU + depthwise + SiLU in one kernel ---------------------------------------------------------
+ * No single counterpart in the reference: the composition up_conv (conformer.py:165,177) -> GLU (:166,:181) ->
+ * granite::dwconv_silu (conv_kernel.py:41-43, i.e. dwconv1d_silu_bf16 of cuda_kernels/conv1d.py:21-42).  The GLU
+ * tensor stays in shared memory: each CTA walks one utterance's frames for one block of 128 channels.
+ * a: [B*T, K] bf16 (the LayerNorm output); w1_glu / b1_glu / s1_glu (NULL for bf16 weights) as for
+ * gsn_gemm1_glu_bf16 / gsn_gemm1_glu_bf16s; dw_w [N/2, 15] bf16, dw_b [N/2] bf16 (BN folded); d: [B*T, N/2] bf16
+ * = silu(depthwise(glu(a W1^T + b1))).  T % 128 == 0, K % 64 == 0, N % 256 == 0.  lengths: NULL or int32[B]:
+ * GLU frames t >= lengths[b] are zero, d frames in [len, roundup128(len)) are written as zero and frames past
+ * that are not written (the residual GEMM with the same lengths skips those tiles).  d equals
+ * gsn_gemm1_glu_bf16 followed by gsn_dwconv_silu_bf16 bit for bit on every frame it writes. */
+int gsn_gemm1_glu_dwconv_bf16(const void* a, const void* w1_glu, const float* s1_glu, const float* b1_glu,
+                              const void* dw_w, const void* dw_b, void* d, int B, int T, int K, int N,
+                              const int32_t* lengths, gsn_stream_t stream);
+
 /* ---- int8 weights widened once per call -------------------------------------------------------------------
  * No counterpart in the reference (its int8 analogue is torchao W8A8, bench_asr.py:92-105).  For large M the
  * weight bytes are negligible next to the activations, so the int8 module widens both weight matrices to bf16
