@@ -29,6 +29,10 @@
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
+#ifndef GSN_GEMM_STAGES
+#define GSN_GEMM_STAGES 4   // TMA ring depth of the bf16 single-CTA mainloop
+#endif
+
 namespace gsn {
 
 namespace gemm_impl {
@@ -288,7 +292,7 @@ __device__ __forceinline__ void init_epi_barriers(EpiSmem& e) {
 // single CTA per SM
 template <bool W_I8>
 struct Cfg {
-  static constexpr int STAGES = W_I8 ? 3 : 4;
+  static constexpr int STAGES = W_I8 ? 3 : GSN_GEMM_STAGES;
   static constexpr int THREADS = W_I8 ? 320 : 192;
 };
 

@@ -56,7 +56,9 @@ def _check(d, ref, B, T, lens):
     (3, 256, [256, 130, 7]),
     (2, 384, [384, 128]),
     (5, 512, [0, 1, 127, 129, 512]),
+    (3, 896, None),
     (6, 1536, [1536, 641, 640, 639, 64, 1500]),
+    (7, 1152, [1152, 1025, 1024, 769, 768, 385, 384]),
 ])
 def test_fused_equals_two_kernels(B, T, lens):
     p = _prep(40 + T)
