@@ -18,7 +18,9 @@
 //               its TMEM lane quarter w % 4, warps 2-5 the first 64 channels, 6-9 the last 64); the accumulator
 //               buffer is released right after; (2) depthwise + SiLU over the window: lane = 4 channels, warp =
 //               16 output frames, weights (halved) in registers, fp32x2 FMAs in the order of the standalone
-//               depthwise kernel, so the result is bit-identical to GEMM -> GLU tensor -> depthwise kernel;
+//               depthwise kernel, so the result is bit-identical to GEMM -> GLU tensor -> depthwise kernel; the
+//               warp's 16 x 128 outputs leave through a staging box in shared memory and one TMA store (boxes
+//               that would start before frame 0 or reach past the written range use plain stores);
 //               (3) window rows 128..141 move to rows 0..13 for the next tile.  After the last tile a flush pass
 //               computes the final 7 frames with zero GLU rows on the right.
 // Lengths: GLU rows of frames t >= len[b] are zero, depthwise frames in [len, roundup128(len)) are written as
@@ -44,6 +46,8 @@ constexpr int WPITCH = CH * 2 + 16;        // 272 bytes: 16-byte row stores of c
 constexpr int MAX_SORT_B = 512;            // utterances ordered by length up to this batch size
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int kEpiBar = 1;                 // named barrier of the epilogue warps
+constexpr int FPW = 16;                    // output frames per epilogue warp and tile
+constexpr int OUT_BOX_BYTES = FPW * CH * 2;   // a warp's 16 x 128 bf16 output box: 4 KB
 
 struct Params {
   const float* bias;          // [N] GLU-interleaved, fp32
@@ -58,6 +62,7 @@ struct Params {
 struct __align__(1024) Smem {
   uint8_t a[STAGES][A_BYTES];
   uint8_t b[STAGES][B_BYTES];
+  uint8_t out[EPI_WARPS][OUT_BOX_BYTES];   // per-warp output box for the TMA store
   uint8_t win[WROWS * WPITCH];
   float vb[BN];               // the unit's GLU bias columns, halved
   float vs[BN];               // the unit's column scales, halved (0.5 without scales)
@@ -71,7 +76,8 @@ struct __align__(1024) Smem {
   uint32_t tmem_base;
   int abort_flag;
 };
-static_assert(offsetof(Smem, b) % 1024 == 0 && offsetof(Smem, win) % 16 == 0, "alignment");
+static_assert(offsetof(Smem, b) % 1024 == 0 && offsetof(Smem, win) % 16 == 0 && offsetof(Smem, out) % 128 == 0,
+              "alignment");
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory size");
 
 typedef uint64_t pk2;
@@ -125,7 +131,8 @@ struct Units {
 
 template <bool SCALED>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, Params p) {
+    gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                       const __grid_constant__ CUtensorMap tmD, Params p) {
   constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -152,6 +159,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, TMEM_COLS);
@@ -380,18 +388,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         epi_bar();
 
         // (2) depthwise + SiLU: output frame t0 - 7 + i reads window rows i .. i + 14.  Warp e owns i in
-        // [16e, 16e + 16) as two passes of 8 frames; the flush only needs i in [0, 7) (warp 0, one pass).
-        const int passes = flush ? (e == 0 ? 1 : 0) : 2;
-        for (int ps = 0; ps < passes && ok; ++ps) {
-          const int i0 = e * 16 + ps * 8;
+        // [16e, 16e + 16); the flush only needs i in [0, 7) (warp 0).
+        const int i_hi = flush ? HALO : BM;
+        if (ok && e * FPW < i_hi) {
+          const int i0 = e * FPW;
           const uint8_t* xb = s.win + i0 * WPITCH + lane * 8;
-          pk2 acc[8][2];
+          pk2 acc[FPW][2];
 #pragma unroll
-          for (int r = 0; r < 8 + 2 * HALO; ++r) {
+          for (int r = 0; r < FPW + 2 * HALO; ++r) {
             const uint2 v = *reinterpret_cast<const uint2*>(xb + r * WPITCH);
             const pk2 xv[2] = {pk_from_bf16x2(v.x), pk_from_bf16x2(v.y)};
 #pragma unroll
-            for (int f = 0; f < 8; ++f) {
+            for (int f = 0; f < FPW; ++f) {
               const int j = r - f;
               if (j >= 0 && j < KW) {
 #pragma unroll
@@ -399,18 +407,36 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
+          const int tf = t0 - HALO + i0;                 // the warp's first output frame
+          const bool boxed = !flush && tf >= 0 && tf + FPW <= store_end;
+          uint8_t* ob = s.out[e];
+          if (boxed) {
+            if (lane == 0) bulk_wait_group_read<0>();  // the previous tile's box has been read by its store
+            __syncwarp();
+          }
 #pragma unroll
-          for (int f = 0; f < 8; ++f) {
-            const int t = t0 - HALO + i0 + f;
-            if (t < 0 || t >= store_end) continue;
+          for (int f = 0; f < FPW; ++f) {
+            const int t = tf + f;
             uint32_t o[2];
 #pragma unroll
             for (int qq = 0; qq < 2; ++qq) {
               const float2 hh = pk_split(acc[f][qq]);
-              const float2 s2 = pk_split(pk_fma(acc[f][qq], pk_make(tanh_approx(hh.x), tanh_approx(hh.y)), acc[f][qq]));
+              const float2 s2 =
+                  pk_split(pk_fma(acc[f][qq], pk_make(tanh_approx(hh.x), tanh_approx(hh.y)), acc[f][qq]));
               o[qq] = t < len ? pack_bf16x2(s2.x, s2.y) : 0u;
             }
-            *reinterpret_cast<uint2*>(drow + (int64_t)t * inner) = make_uint2(o[0], o[1]);
+            if (boxed)
+              *reinterpret_cast<uint2*>(ob + f * (CH * 2) + lane * 8) = make_uint2(o[0], o[1]);
+            else if (i0 + f < i_hi && t >= 0 && t < store_end)
+              *reinterpret_cast<uint2*>(drow + (int64_t)t * inner) = make_uint2(o[0], o[1]);
+          }
+          if (boxed) {
+            fence_proxy_async_smem();                    // generic-proxy writes -> visible to the TMA store
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmD, ob, c0, b * p.T + tf);
+              bulk_commit_group();
+            }
           }
         }
         epi_bar();
@@ -425,6 +451,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_group<0>();   // this warp's output boxes have landed before the CTA ends
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -459,6 +487,15 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
+  CUtensorMap tmD;
+  {
+    const uint64_t dims[2] = {(uint64_t)(a.N / 2), (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)(a.N / 2) * 2};
+    const uint32_t box[2] = {G::CH, G::FPW};
+    if (int rc = encode_tmap(&tmD, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.d, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  }
   G::Params p;
   p.bias = a.bias;
   p.col_scale = a.col_scale;
@@ -478,7 +515,7 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   const int sms = device_sm_count();
   const int grid = (int)(units < sms ? units : sms);
   if (grid <= 0) return 0;
-  kern<<<grid, G::THREADS, smem, stream>>>(tmA, tmW, p);
+  kern<<<grid, G::THREADS, smem, stream>>>(tmA, tmW, tmD, p);
   return (int)cudaGetLastError();
 }
 
