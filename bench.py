@@ -38,8 +38,9 @@ D, I = synth.D_MODEL, synth.D_INNER
 GEMM1_FLOP_PER_FRAME = 2 * D * 2 * I          # 8.389 MFLOP
 GEMM2_FLOP_PER_FRAME = 2 * I * D              # 4.194 MFLOP
 # DRAM bytes (read + write) of the fused up_conv + GLU + depthwise kernel per row of the 128-row tiles it computes,
-# from one ncu capture (None until that capture is summarised); the traffic of a launch scales with its rows.
-GEMM1DW_DRAM_BYTES_PER_ROW = None
+# from one ncu capture of a B=48, T=1536 chunk (profiles/gemm_glu_dw_b48_t1536.md: 73.0 + 83.1 MB over 31,104
+# rows); the traffic of a launch scales with the rows it computes.
+GEMM1DW_DRAM_BYTES_PER_ROW = 5019
 DW_BYTES_PER_FRAME = 2 * I * 2                # read + write bf16: 8192 B
 METRIC = "conv-module frames/s at 1/2/4/8 B200; % of HBM / tensor-pipe roofline"
 
@@ -475,9 +476,12 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
     d2h = sum(o.numel() * 2 for o in ho)
 
     # copies run on their own streams so chunk i+1's upload and chunk i-1's download overlap chunk i's layers;
-    # a chunk's device input is overwritten only after the previous step's compute of that chunk has finished
+    # a chunk's device input is overwritten only after the previous step's compute of that chunk has finished.
+    # Chunks alternate between two compute streams (ConvModuleStack.run_chunks' schedule), so each persistent
+    # kernel's tail is filled by the other chunk's next kernel.
     copy_in = torch.cuda.Stream(dev)
     copy_out = torch.cuda.Stream(dev)
+    comp = [stream, torch.cuda.Stream(dev)]
     xd = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
     ld = [torch.empty((c.B,), dtype=torch.int32, device=dev) for c in chunks]
     done = [None] * len(chunks)
@@ -486,7 +490,9 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
         begin = torch.cuda.Event()          # the step's copies start after everything queued before it
         begin.record(stream)
         copy_in.wait_event(begin)
+        comp[1].wait_event(begin)
         for ci in range(len(chunks)):
+            cs = comp[ci % 2]
             with torch.cuda.stream(copy_in):
                 if done[ci] is not None:
                     copy_in.wait_event(done[ci])
@@ -494,11 +500,11 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
                 ld[ci].copy_(hl[ci], non_blocking=True)
                 ready = torch.cuda.Event()
                 ready.record(copy_in)
-            stream.wait_event(ready)
-            with torch.cuda.stream(stream):
+            cs.wait_event(ready)
+            with torch.cuda.stream(cs):
                 y = stack(xd[ci], ld[ci])
                 done[ci] = torch.cuda.Event()
-                done[ci].record(stream)
+                done[ci].record(cs)
             with torch.cuda.stream(copy_out):
                 copy_out.wait_event(done[ci])
                 ho[ci].copy_(y, non_blocking=True)
@@ -506,6 +512,9 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
         fin = torch.cuda.Event()
         fin.record(copy_out)
         stream.wait_event(fin)
+        side = torch.cuda.Event()
+        side.record(comp[1])
+        stream.wait_event(side)
 
     for _ in range(max(1, args.warmup)):
         step()

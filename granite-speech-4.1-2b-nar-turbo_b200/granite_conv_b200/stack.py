@@ -3,7 +3,7 @@ execution chunks, each layer followed by its residual add (``conformer.py:207``)
 stacked; the attention and feed-forward halves of each block are outside this package."""
 from __future__ import annotations
 
-from typing import Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 
@@ -29,3 +29,35 @@ class ConvModuleStack:
         for p in self.layers:
             x = ops.run_conv_module(x, p, lengths=lengths, add_residual=True, int8=self.int8)
         return x
+
+    def run_chunks(self, chunks: Sequence[Tuple[torch.Tensor, Optional[torch.Tensor]]],
+                   streams: Optional[Sequence[torch.cuda.Stream]] = None) -> List[torch.Tensor]:
+        """Independent execution chunks (x, lengths) through the stack, chunk i on streams[i % len(streams)]
+        (default: two streams).  The kernels are persistent grids of one CTA per SM, so a chunk's kernels start
+        on the SMs another chunk's kernel has already released: the tail of each launch is filled.  Inputs must
+        be ready on the current stream; the outputs are ready on it when this returns."""
+        if not chunks:
+            return []
+        cur = torch.cuda.current_stream(chunks[0][0].device)
+        if streams is None:
+            streams = [cur, torch.cuda.Stream(chunks[0][0].device)]
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        outs = []
+        for i, (x, lengths) in enumerate(chunks):
+            st = streams[i % len(streams)]
+            st.wait_event(ready)
+            with torch.cuda.stream(st):
+                y = self(x, lengths)
+            if st is not cur:
+                x.record_stream(st)
+                if lengths is not None:
+                    lengths.record_stream(st)
+                y.record_stream(cur)
+            outs.append(y)
+        for st in streams:
+            if st is not cur:
+                done = torch.cuda.Event()
+                done.record(st)
+                cur.wait_event(done)
+        return outs

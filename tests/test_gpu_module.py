@@ -158,6 +158,21 @@ def test_stack_on_chunks():
         assert_bf16_close(y, ref, f"stack chunk B={c.B} T={c.T}")
 
 
+def test_stack_run_chunks_two_streams():
+    """ConvModuleStack.run_chunks (chunks alternating between two streams) equals running them one by one."""
+    lens = synth.sample_lengths(5105, 40)
+    chunks = dispatch.plan_chunks(lens, exec_batch=12, logical_batch=24)
+    stack = ConvModuleStack([prepare_from_params(synth.make_params(7100 + i), device=DEV) for i in range(3)])
+    xs = [_t(_x(int(c.index[0]) + 40, (c.B, c.T, synth.D_MODEL))) for c in chunks]
+    ls = [torch.from_numpy(c.lengths).to(DEV) for c in chunks]
+    seq = [stack(x, l) for x, l in zip(xs, ls)]
+    par = stack.run_chunks(list(zip(xs, ls)))
+    torch.cuda.synchronize()
+    assert len(par) == len(seq)
+    for a, b in zip(seq, par):
+        assert torch.equal(a, b)
+
+
 def test_torch_compile_fullgraph():
     params = synth.make_params(9)
     p = prepare_from_params(params, device=DEV)
