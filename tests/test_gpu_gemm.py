@@ -134,7 +134,8 @@ def test_gemms_skip_padding_tiles():
         np.testing.assert_array_equal(o_skip[pad].float().cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("M,D", [(1, 1024), (37, 1024), (1000, 1024), (64, 256), (64, 512), (33, 2048)])
+@pytest.mark.parametrize("M,D", [(1, 1024), (37, 1024), (1000, 1024), (64, 256), (64, 512), (33, 2048),
+                                 (20001, 1024), (5003, 2048), (9999, 512)])
 def test_layernorm(M, D):
     x = _rand(M + D, (M, D)) * 3.0 + 0.5
     x = O.bf16_round(x.astype(np.float32))
