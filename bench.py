@@ -257,7 +257,9 @@ def run_ours(args):
         ys = [torch.empty_like(x) for x in xs]
         layers = []
     else:
-        layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8) for l in range(n_layers)]
+        # bf16: the LayerNorm folded into the up_conv GEMM (the module op's path for T on the 128 grid)
+        layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8, ln_fold=not int8)
+                  for l in range(n_layers)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     lens_dev = [torch.from_numpy(c.lengths).to(dev) for c in chunks]
     max_m = max(c.padded_frames for c in chunks)
@@ -276,9 +278,10 @@ def run_ours(args):
     widen_events = []      # int8: per recorded layer, the events around the weight widening
 
     def layer_kernels(x, out, c, p, lens, record):
-        """The kernels of one conv module (the same launches gsn_conv_module_* makes for T on the 128 grid):
-        LayerNorm, up_conv + GLU + depthwise + SiLU in one kernel, down_conv + residual; with CUDA events between
-        them when `record`."""
+        """The kernels of one conv module (the same launches the module op makes for T on the 128 grid): bf16
+        weights: LayerNorm statistics, up_conv + GLU + depthwise + SiLU on the raw frames with the LayerNorm folded
+        in, down_conv + residual (gsn_conv_module_lnfold_bf16); int8 weights: their widening, LayerNorm, the fused
+        up_conv kernel on the LayerNorm output, down_conv + residual.  CUDA events between them when `record`."""
         M = c.padded_frames
         dp = h_buf.data_ptr()                   # depthwise output [M, I]
         tp = h_buf.data_ptr() + t_off           # LayerNorm output [M, D]
@@ -295,13 +298,22 @@ def run_ours(args):
                 widen_events.append(wev)
         if record:
             ev[0].record(stream)
-        _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
-                                        p.ln_eps, lp, T, sp), "layernorm")
+        if int8:
+            _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
+                                            p.ln_eps, lp, T, sp), "layernorm")
+        else:
+            _lib.check(L.gsn_layernorm_stats_bf16(x.data_ptr(), D, tp, M, D, p.ln_eps, lp, T, sp), "ln_stats")
         if record:
             ev[1].record(stream)
-        w1, s1 = (w1b.data_ptr(), p.s1_glu.data_ptr()) if int8 else (p.w1_glu.data_ptr(), None)
-        _lib.check(L.gsn_gemm1_glu_dwconv_bf16(tp, w1, s1, p.b1_glu.data_ptr(), p.dw_w.data_ptr(),
-                                               p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp, sp), "gemm1_dw")
+        if int8:
+            _lib.check(L.gsn_gemm1_glu_dwconv_bf16(tp, w1b.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(),
+                                                   p.dw_w.data_ptr(), p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp,
+                                                   sp), "gemm1_dw")
+        else:
+            _lib.check(L.gsn_gemm1_lnfold_glu_dwconv_bf16(x.data_ptr(), p.w1g_glu.data_ptr(), p.b1g_glu.data_ptr(),
+                                                          p.c1_glu.data_ptr(), tp, p.dw_w.data_ptr(),
+                                                          p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp, sp),
+                       "gemm1_dw")
         if record:
             ev[2].record(stream)
         if int8:
@@ -385,7 +397,7 @@ def run_ours(args):
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
     else:
-        kernels = _kernel_breakdown(layer_events, peaks, widen_events)
+        kernels = _kernel_breakdown(layer_events, peaks, widen_events, ln_name="layernorm" if int8 else "ln_stats")
         g1 = kernels["gemm1_glu_dw"]
         traffic = None if GEMM1DW_DRAM_BYTES_PER_ROW is None else g1["rows_per_launch"] * GEMM1DW_DRAM_BYTES_PER_ROW
         roof = {"kernel": "gemm_glu_dw_kernel (up_conv 1024->4096 + GLU + depthwise k15 + SiLU)", "bound": "tensor",
@@ -429,12 +441,13 @@ def _tile_rows(c, tile=128):
     return int(sum(((int(L) + tile - 1) // tile) * tile for L in c.lengths))
 
 
-def _kernel_breakdown(layer_events, peaks, widen_events=()):
+def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm"):
     """Average launch time, share of the recorded kernel time and achieved rate of each kernel.
     Work per launch: LayerNorm reads and writes the valid frames (2 x 2 KB); the GEMMs compute the rows of the
     128-row tiles that hold valid frames (the up_conv kernel also runs GLU and the depthwise conv on them, counted
-    as its GEMM FLOPs only); the int8 weight widening reads 1 byte and writes 2 per weight."""
-    names = ("layernorm", "gemm1_glu_dw", "gemm2_residual")
+    as its GEMM FLOPs only); the LayerNorm statistics read 2 KB and write 8 B per valid frame; the int8 weight
+    widening reads 1 byte and writes 2 per weight."""
+    names = (ln_name, "gemm1_glu_dw", "gemm2_residual")
     tot = {n: 0.0 for n in names}
     work = {n: 0.0 for n in names}
     if widen_events:
@@ -446,7 +459,7 @@ def _kernel_breakdown(layer_events, peaks, widen_events=()):
             tot[n] += ev[k].elapsed_time(ev[k + 1])
         valid = c.valid_frames
         rows = _tile_rows(c)
-        work["layernorm"] += valid * 2 * D * 2
+        work[ln_name] += valid * (2 * D * 2 if ln_name == "layernorm" else D * 2 + 8)
         work["gemm1_glu_dw"] += rows * GEMM1_FLOP_PER_FRAME
         work["gemm2_residual"] += rows * GEMM2_FLOP_PER_FRAME
     all_ms = sum(tot.values())

@@ -289,6 +289,58 @@ int gsn_gemm1_glu_dwconv_bf16(const void* a, const void* w1_glu, const float* s1
   return finish(launch_gemm_glu_dw(g, (cudaStream_t)stream), name);
 }
 
+int gsn_gemm1_lnfold_glu_dwconv_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                     const float* row_stats, const void* dw_w, const void* dw_b, void* d, int B,
+                                     int T, int K, int N, const int32_t* lengths, gsn_stream_t stream) {
+  const char* name = "gsn_gemm1_lnfold_glu_dwconv_bf16";
+  if (B < 0 || T < 0 || K <= 0 || N <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d K=%d N=%d", name, B, T, K, N);
+  if ((int64_t)B * T == 0) return ok();
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  if (!x || !w1g_glu || !b1g_glu || !c1_glu || !row_stats || !dw_w || !dw_b || !d)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (T % 128 || K % 64 || N % 256)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: needs T %% 128 == 0, K %% 64 == 0, N %% 256 == 0 (T=%d K=%d N=%d)", name, T,
+                K, N);
+  if (!aligned(x, 16) || !aligned(w1g_glu, 16) || !aligned(d, 16) || !aligned(b1g_glu, 16) || !aligned(c1_glu, 16) ||
+      !aligned(row_stats, 8) || !aligned(dw_w, 2) || !aligned(dw_b, 2))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: x, w1g, d, b1g, c1 must be 16-byte aligned, row_stats 8-byte", name);
+  GemmDwArgs g{(const __nv_bfloat16*)x, (const __nv_bfloat16*)w1g_glu, b1g_glu, nullptr, (const __nv_bfloat16*)dw_w,
+               (const __nv_bfloat16*)dw_b, (__nv_bfloat16*)d, lengths, B, T, K, N, (const float2*)row_stats, c1_glu};
+  return finish(launch_gemm_glu_dw(g, (cudaStream_t)stream), name);
+}
+
+int gsn_layernorm_stats_bf16(const void* x, int64_t ld_x, float* stats, int M, int D, float eps,
+                             const int32_t* lengths, int T, gsn_stream_t stream) {
+  const char* name = "gsn_layernorm_stats_bf16";
+  if (M < 0) return fail(GSN_ERR_INVALID_ARG, "%s: M=%d", name, M);
+  if (!ln_dim_ok(D)) return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d not in {256,512,1024,2048}", name, D);
+  if (M == 0) return ok();
+  if (!x || !stats) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (ld_x % 8 || ld_x < D || !aligned(x, 16) || !aligned(stats, 8))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: rows must be 16-byte aligned (ld %% 8 == 0), stats 8-byte", name);
+  if (lengths && (T <= 0 || M % T != 0))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: with lengths, T=%d must divide M=%d", name, T, M);
+  return finish(launch_ln_stats((const __nv_bfloat16*)x, ld_x, (float2*)stats, M, D, eps, lengths, T,
+                                (cudaStream_t)stream),
+                name);
+}
+
+int gsn_fold_layernorm_bf16(const void* w1_glu, const float* b1_glu, const void* ln_w, const void* ln_b,
+                            void* w1g_glu, float* b1g_glu, float* c1_glu, int N, int K, gsn_stream_t stream) {
+  const char* name = "gsn_fold_layernorm_bf16";
+  if (N < 0 || K <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: N=%d K=%d", name, N, K);
+  if (N == 0) return ok();
+  if (K % 256) return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d must be a multiple of 256", name, K);
+  if (!w1_glu || !b1_glu || !ln_w || !ln_b || !w1g_glu || !b1g_glu || !c1_glu)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned(w1_glu, 16) || !aligned(ln_w, 16) || !aligned(ln_b, 16) || !aligned(w1g_glu, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: weights and LayerNorm vectors must be 16-byte aligned", name);
+  return finish(launch_fold_ln((const __nv_bfloat16*)w1_glu, b1_glu, (const __nv_bfloat16*)ln_w,
+                               (const __nv_bfloat16*)ln_b, (__nv_bfloat16*)w1g_glu, b1g_glu, c1_glu, N, K,
+                               (cudaStream_t)stream),
+                name);
+}
+
 int gsn_widen_i8_bf16(const void* q0, void* out0, int64_t n0, const void* q1, void* out1, int64_t n1,
                       gsn_stream_t stream) {
   const char* name = "gsn_widen_i8_bf16";
@@ -381,6 +433,40 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
               (__nv_bfloat16*)out, D, D, M, D, inner, w_i8, skip, T};
   rc = launch_gemm(g2, kEpiResidual, st);
   return finish(rc, name);
+}
+
+int gsn_conv_module_lnfold_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                                const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
+                                float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  const char* name = "gsn_conv_module_lnfold_bf16";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if ((int64_t)B * T == 0) return ok();
+  if (!x || !w1g_glu || !b1g_glu || !c1_glu || !dw_w || !dw_b || !w2 || !b2 || !out)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!ln_dim_ok(D) || (2 * inner) % 256 != 0 || inner % 128 != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d inner=%d (D in {256..2048}, inner %% 128 == 0)", name, D, inner);
+  if (T % 128) return fail(GSN_ERR_UNSUPPORTED, "%s: T=%d must be a multiple of 128", name, T);
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  const int M = B * T;
+  const size_t need = gsn_conv_module_workspace_bytes(B, T, D, inner);
+  if (!workspace || workspace_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
+  if (!aligned(x, 16) || !aligned(out, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: x/out must be 16-byte aligned", name);
+  // workspace: d = the depthwise output [M, inner], then the row statistics [M] x (rstd, rstd * mean)
+  __nv_bfloat16* d = (__nv_bfloat16*)workspace;
+  float2* stats = (float2*)((char*)workspace + align256((size_t)M * inner * 2));
+  const cudaStream_t st = (cudaStream_t)stream;
+  int rc = launch_ln_stats((const __nv_bfloat16*)x, D, stats, M, D, ln_eps, lengths, T, st);
+  if (rc) return finish(rc, name);
+  GemmDwArgs gd{(const __nv_bfloat16*)x, (const __nv_bfloat16*)w1g_glu, b1g_glu, nullptr, (const __nv_bfloat16*)dw_w,
+                (const __nv_bfloat16*)dw_b, d, lengths, B, T, D, 2 * inner, stats, c1_glu};
+  rc = launch_gemm_glu_dw(gd, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g2{d, w2, b2, nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr, (__nv_bfloat16*)out, D, D, M, D,
+              inner, 0, lengths, T};
+  return finish(launch_gemm(g2, kEpiResidual, st), name);
 }
 
 int gsn_conv_module_bf16(const void* x, const void* ln_w, const void* ln_b, const void* w1_glu,

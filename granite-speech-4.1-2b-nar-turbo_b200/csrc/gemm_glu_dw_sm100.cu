@@ -56,6 +56,8 @@ struct Params {
   const __nv_bfloat16* dw_b;  // [inner]
   __nv_bfloat16* d;           // [B * T, inner]
   const int* lengths;         // [B] or null
+  const float2* row_stats;    // LayerNorm folded in: per-row (rstd, rstd * mean), rows b * T + t
+  const float* colsum;        // LayerNorm folded in: [N] column sums of W'
   int B, T, K, N;
 };
 
@@ -66,6 +68,7 @@ struct __align__(1024) Smem {
   uint8_t win[WROWS * WPITCH];
   float vb[BN];               // the unit's GLU bias columns, halved
   float vs[BN];               // the unit's column scales, halved (0.5 without scales)
+  float vc[BN];               // LayerNorm folded in: the unit's column sums times the halved scales
   int lens[MAX_SORT_B];       // clamped lengths
   short order[MAX_SORT_B];    // utterances, most tiles first
   uint64_t full[STAGES];
@@ -129,7 +132,9 @@ struct Units {
   }
 };
 
-template <bool SCALED>
+// SCALED: per-column scale on the accumulator (int8 weights widened to bf16).  LNF: LayerNorm folded in -- A holds
+// the raw frames, W the weights times gamma, and the accumulator becomes rstd * (acc - mean * colsum) + bias.
+template <bool SCALED, bool LNF>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmD, Params p) {
@@ -306,6 +311,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float bv = __ldg(p.bias + n_blk * BN + et);
         s.vb[et] = 0.5f * bv;
         s.vs[et] = SCALED ? 0.5f * __ldg(p.col_scale + n_blk * BN + et) : 0.5f;
+        if (LNF) s.vc[et] = s.vs[et] * __ldg(p.colsum + n_blk * BN + et);
         if (et < 2 * HALO * 16) {
           const int r = et >> 4, c = et & 15;
           *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -346,6 +352,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int r = q * 32 + lane;
             const bool valid = t0 + r < len;
             uint8_t* wrow = s.win + (2 * HALO + r) * WPITCH;
+            // LayerNorm folded in: this row's statistics (padding rows have none; their GLU row is zero anyway)
+            float rs = 1.f, rsm = 0.f;
+            if (LNF && valid) {
+              const float2 st = __ldg(p.row_stats + (int64_t)b * p.T + t0 + r);
+              rs = st.x;
+              rsm = st.y;
+            }
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int cb = half * 64 + u * 32;         // first of this sub-tile's 32 GLU channels
@@ -363,9 +376,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int z = 0; z < 2; ++z) {
                   const int kk = c + z;
-                  const float a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
-                  const float g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[CH + cb + kk],
-                                       s.vb[CH + cb + kk]);
+                  float a, g;
+                  if (LNF) {
+                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rs * s.vs[cb + kk],
+                             fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
+                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rs * s.vs[CH + cb + kk],
+                             fmaf(-rsm, s.vc[CH + cb + kk], s.vb[CH + cb + kk]));
+                  } else {
+                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
+                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[CH + cb + kk], s.vb[CH + cb + kk]);
+                  }
                   h2[z] = fmaf(a, tanh_approx(g), a);
                 }
                 o[c >> 1] = valid ? pack_bf16x2(h2[0], h2[1]) : 0u;
@@ -503,12 +523,16 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   p.dw_b = a.dw_b;
   p.d = a.d;
   p.lengths = a.lengths;
+  p.row_stats = a.row_stats;
+  p.colsum = a.colsum;
   p.B = a.B;
   p.T = a.T;
   p.K = a.K;
   p.N = a.N;
   const int smem = (int)sizeof(G::Smem) + 1024;
-  auto kern = a.col_scale ? G::gemm_glu_dw_kernel<true> : G::gemm_glu_dw_kernel<false>;
+  if (a.row_stats && !a.colsum) return (int)cudaErrorInvalidValue;
+  auto kern = a.col_scale ? (a.row_stats ? G::gemm_glu_dw_kernel<true, true> : G::gemm_glu_dw_kernel<true, false>)
+                          : (a.row_stats ? G::gemm_glu_dw_kernel<false, true> : G::gemm_glu_dw_kernel<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int64_t units = (int64_t)a.B * (a.N / G::BN);

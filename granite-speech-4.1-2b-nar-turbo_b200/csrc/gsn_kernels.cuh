@@ -56,6 +56,8 @@ struct GemmDwArgs {
   __nv_bfloat16* d;
   const int* lengths;            // [B] or null
   int B, T, K, N;
+  const float2* row_stats;       // LayerNorm folded in: a = raw frames, per-row (rstd, rstd * mean) [B*T]; or null
+  const float* colsum;           // with row_stats: [N] column sums of w
 };
 int launch_gemm_glu_dw(const GemmDwArgs& args, cudaStream_t stream);
 
@@ -79,6 +81,12 @@ int launch_dwconv(const DwArgs& args, cudaStream_t stream);
 int launch_layernorm(const __nv_bfloat16* x, int64_t ld_x, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
                      __nv_bfloat16* y, int64_t ld_y, int M, int D, float eps, const int* lengths, int T,
                      cudaStream_t stream);
+// Row statistics (rstd, rstd * mean) of the LayerNorm, for the LayerNorm folded into the up_conv GEMM.
+int launch_ln_stats(const __nv_bfloat16* x, int64_t ld_x, float2* stats, int M, int D, float eps, const int* lengths,
+                    int T, cudaStream_t stream);
+// W' = bf16(W * gamma), b' = b + W beta, colsum = sum_k W'[n, k] (fp32) for W [N, K] bf16.
+int launch_fold_ln(const __nv_bfloat16* w, const float* bias, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
+                   __nv_bfloat16* w_out, float* bias_out, float* colsum, int N, int K, cudaStream_t stream);
 
 // ---- self-test of the bounded wait (capi.cu) ----------------------------------------------------------------
 int launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);

@@ -36,6 +36,12 @@ SIGNATURES = {
     "gsn_gemm2_residual_i8w": (_i32, [_vp, _vp, _fp, _fp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp, _i32,
                                       _vp]),
     "gsn_gemm1_glu_dwconv_bf16": (_i32, [_vp, _vp, _fp, _fp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "gsn_fold_layernorm_bf16": (_i32, [_vp, _fp, _vp, _vp, _vp, _fp, _fp, _i32, _i32, _vp]),
+    "gsn_layernorm_stats_bf16": (_i32, [_vp, _i64, _fp, _i32, _i32, _f32, _vp, _i32, _vp]),
+    "gsn_gemm1_lnfold_glu_dwconv_bf16": (_i32, [_vp, _vp, _fp, _fp, _fp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp,
+                                                _vp]),
+    "gsn_conv_module_lnfold_bf16": (_i32, [_vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _vp, _i32, _vp, _i32, _i32, _i32,
+                                           _i32, _f32, _vp, _sz, _vp]),
     "gsn_widen_i8_bf16": (_i32, [_vp, _vp, _i64, _vp, _vp, _i64, _vp]),
     "gsn_gemm1_glu_bf16s": (_i32, [_vp, _vp, _fp, _fp, _vp, _i32, _i32, _i32, _vp, _i32, _vp]),
     "gsn_gemm2_residual_bf16s": (_i32, [_vp, _vp, _fp, _fp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp, _i32,

@@ -11,6 +11,8 @@ plus the ops of the whole module (new):
 * ``granite::conv_module(x, ln_w, ln_b, w1_glu, b1_glu, dw_w, dw_b, w2, b2, lengths?, ln_eps, add_residual)``
 * ``granite::conv_module_i8w(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths?, ln_eps,
   add_residual)``
+* ``granite::conv_module_lnfold(x, w1g_glu, b1g_glu, c1_glu, dw_w, dw_b, w2, b2, lengths?, ln_eps, add_residual)``
+  (the LayerNorm folded into the up_conv GEMM; T % 128 == 0)
 
 All are ``mutates_args=()``, CUDA-only, launch on ``torch.cuda.current_stream()`` (as ``jit.py:180-181``) and
 have ``register_fake`` implementations whose strides equal the real outputs', so ``torch.compile(fullgraph=True)``
@@ -156,6 +158,34 @@ def _(x, ln_w, ln_b, w1_glu, b1_glu, dw_w, dw_b, w2, b2, lengths, ln_eps, add_re
     return torch.empty_like(x, memory_format=torch.contiguous_format)
 
 
+@torch.library.custom_op("granite::conv_module_lnfold", mutates_args=(), device_types="cuda")
+def conv_module_lnfold(x: torch.Tensor, w1g_glu: torch.Tensor, b1g_glu: torch.Tensor, c1_glu: torch.Tensor,
+                       dw_w: torch.Tensor, dw_b: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor,
+                       lengths: Optional[torch.Tensor], ln_eps: float, add_residual: bool) -> torch.Tensor:
+    """conv_module with the LayerNorm folded into the up_conv GEMM (weights from ``weights.fold_layernorm_``);
+    T % 128 == 0."""
+    name = "granite::conv_module_lnfold"
+    _require_cuda(name, x, w1g_glu, b1g_glu, c1_glu, dw_w, dw_b, w2, b2, lengths)
+    if x.dim() != 3 or x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: x must be bf16 [B, T, D], got {x.dtype} {tuple(x.shape)}")
+    B, T, D = x.shape
+    inner = dw_w.shape[0]
+    xc = x.contiguous()
+    lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    out = torch.empty_like(xc)
+    nbytes = int(_lib.lib().gsn_conv_module_workspace_bytes(B, T, D, inner)) if B * T > 0 else 0
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    _lib.call("gsn_conv_module_lnfold_bf16", xc.data_ptr(), w1g_glu.data_ptr(), b1g_glu.data_ptr(), c1_glu.data_ptr(),
+              dw_w.data_ptr(), dw_b.data_ptr(), w2.data_ptr(), b2.data_ptr(), _ptr(lens), 1 if add_residual else 0,
+              out.data_ptr(), B, T, D, inner, float(ln_eps), ws.data_ptr(), nbytes, _stream(xc))
+    return out
+
+
+@conv_module_lnfold.register_fake
+def _(x, w1g_glu, b1g_glu, c1_glu, dw_w, dw_b, w2, b2, lengths, ln_eps, add_residual):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
 @torch.library.custom_op("granite::conv_module_i8w", mutates_args=(), device_types="cuda")
 def conv_module_i8w(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w1q_glu: torch.Tensor,
                     s1_glu: torch.Tensor, b1_glu: torch.Tensor, dw_w: torch.Tensor, dw_b: torch.Tensor,
@@ -182,8 +212,16 @@ def _(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, 
 
 # ---------------------------------------------------------------------------------------------------------------
 def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, add_residual: bool = True,
-                    int8: bool = False) -> torch.Tensor:
-    """Call the fused module op with a :class:`~granite_conv_b200.weights.PreparedConvModule`."""
+                    int8: bool = False, ln_fold: Optional[bool] = None) -> torch.Tensor:
+    """Call the fused module op with a :class:`~granite_conv_b200.weights.PreparedConvModule`.  ``ln_fold``: use
+    the LayerNorm-folded op (default: when the weights carry the folded operands and T % 128 == 0)."""
+    if ln_fold is None:
+        ln_fold = (not int8) and p.has_ln_fold and x.dim() == 3 and x.shape[1] % 128 == 0
+    if ln_fold:
+        if int8 or not p.has_ln_fold:
+            raise RuntimeError("run_conv_module(ln_fold=True): needs bf16 weights prepared with ln_fold=True")
+        return torch.ops.granite.conv_module_lnfold(x, p.w1g_glu, p.b1g_glu, p.c1_glu, p.dw_w, p.dw_b, p.w2, p.b2,
+                                                    lengths, p.ln_eps, add_residual)
     if int8:
         if not p.has_int8:
             raise RuntimeError("run_conv_module(int8=True): weights were prepared without int8")
@@ -234,6 +272,17 @@ def gemm1_glu_dwconv(a: torch.Tensor, w_glu: torch.Tensor, b_glu: torch.Tensor, 
     _lib.call("gsn_gemm1_glu_dwconv_bf16", a.data_ptr(), w_glu.data_ptr(), _ptr(scale_glu), b_glu.data_ptr(),
               dw_w.data_ptr(), dw_b.data_ptr(), d.data_ptr(), B, T, K, N, _ptr(lengths), _stream(a))
     return d
+
+
+def layernorm_stats(x2d: torch.Tensor, eps: float = 1e-5, lengths: Optional[torch.Tensor] = None,
+                    T: int = 0) -> torch.Tensor:
+    """Per-row (rstd, rstd * mean) of bf16 rows [M, D] as fp32 [M, 2]; padding rows (with lengths) unwritten."""
+    _require_cuda("layernorm_stats", x2d, lengths)
+    M, D = x2d.shape
+    st = torch.empty((M, 2), dtype=torch.float32, device=x2d.device)
+    _lib.call("gsn_layernorm_stats_bf16", x2d.data_ptr(), x2d.stride(0), st.data_ptr(), M, D, float(eps),
+              _ptr(lengths), T, _stream(x2d))
+    return st
 
 
 def gemm2_residual(d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, residual: Optional[torch.Tensor],

@@ -96,6 +96,10 @@ class PreparedConvModule:
     s1_glu: Optional[torch.Tensor] = None    # [2I] fp32
     w2q: Optional[torch.Tensor] = None       # [D, I] int8
     s2: Optional[torch.Tensor] = None        # [D] fp32
+    # LayerNorm folded into the up_conv GEMM (gsn_fold_layernorm_bf16): W1 * gamma, b1 + W1 beta, column sums
+    w1g_glu: Optional[torch.Tensor] = None   # [2I, D] bf16, GLU-interleaved
+    b1g_glu: Optional[torch.Tensor] = None   # [2I] fp32
+    c1_glu: Optional[torch.Tensor] = None    # [2I] fp32
 
     @property
     def d_model(self) -> int:
@@ -109,13 +113,34 @@ class PreparedConvModule:
     def has_int8(self) -> bool:
         return self.w1q_glu is not None
 
+    @property
+    def has_ln_fold(self) -> bool:
+        return self.w1g_glu is not None
+
+
+@torch.no_grad()
+def fold_layernorm_(p: PreparedConvModule) -> PreparedConvModule:
+    """Add the LayerNorm-folded up_conv operands (on the GPU, by the library's fold kernel): W' = bf16(W1 * gamma),
+    b' = b1 + W1 beta, c = column sums of W'.  Returns ``p``."""
+    from . import _lib
+    n, k = p.w1_glu.shape
+    p.w1g_glu = torch.empty_like(p.w1_glu)
+    p.b1g_glu = torch.empty(n, dtype=torch.float32, device=p.w1_glu.device)
+    p.c1_glu = torch.empty(n, dtype=torch.float32, device=p.w1_glu.device)
+    _lib.call("gsn_fold_layernorm_bf16", p.w1_glu.data_ptr(), p.b1_glu.data_ptr(), p.ln_w.data_ptr(),
+              p.ln_b.data_ptr(), p.w1g_glu.data_ptr(), p.b1g_glu.data_ptr(), p.c1_glu.data_ptr(), n, k,
+              torch.cuda.current_stream(p.w1_glu.device).cuda_stream)
+    return p
+
 
 @torch.no_grad()
 def prepare_from_tensors(ln_w, ln_b, up_w, up_b, dw_w, dw_b, down_w, down_b, ln_eps=1e-5, device="cuda",
-                         int8: bool = False, int8_source: Optional[tuple] = None) -> PreparedConvModule:
+                         int8: bool = False, int8_source: Optional[tuple] = None,
+                         ln_fold: bool = False) -> PreparedConvModule:
     """Build the kernel operands from folded module tensors (any dtype; up/down weights may keep the trailing
     Conv1d kernel dim of 1).  ``int8_source``, if given, is the (up_w, down_w) pair to quantise (e.g. the fp32
-    originals); otherwise the given weights are quantised."""
+    originals); otherwise the given weights are quantised.  ``ln_fold`` adds the LayerNorm-folded up_conv
+    operands (needs a GPU)."""
     bf = torch.bfloat16
     up_w = up_w.reshape(up_w.shape[0], -1)
     down_w = down_w.reshape(down_w.shape[0], -1)
@@ -135,6 +160,8 @@ def prepare_from_tensors(ln_w, ln_b, up_w, up_b, dw_w, dw_b, down_w, down_b, ln_
         p.s1_glu = glu_interleave(s1.to(dev))
         p.w2q = q2.to(dev).contiguous()
         p.s2 = s2.to(dev).contiguous()
+    if ln_fold:
+        fold_layernorm_(p)
     return p
 
 
@@ -149,7 +176,7 @@ def prepare_conv_module(m: nn.Module, device="cuda", int8: bool = False) -> Prep
                                 int8=int8)
 
 
-def prepare_from_params(params, device="cuda", int8: bool = False) -> PreparedConvModule:
+def prepare_from_params(params, device="cuda", int8: bool = False, ln_fold: bool = False) -> PreparedConvModule:
     """Operands from unfolded float32 parameters (``synth.ConvModuleParams``) as a bf16 model load would make
     them: every tensor cast to bf16, then the BatchNorm fold in fp32 and a cast back to bf16
     (``fold_bn.py:51-64``).  int8 weights are quantised from the bf16 weights."""
@@ -160,4 +187,4 @@ def prepare_from_params(params, device="cuda", int8: bool = False) -> PreparedCo
     dw_b = (t(params.bn_bias).float() - t(params.bn_mean).float() * scale).to(bf)
     return prepare_from_tensors(t(params.norm_weight), t(params.norm_bias), t(params.up_weight), t(params.up_bias),
                                 dw_w, dw_b, t(params.down_weight), t(params.down_bias), ln_eps=params.ln_eps,
-                                device=device, int8=int8)
+                                device=device, int8=int8, ln_fold=ln_fold)

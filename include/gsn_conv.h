@@ -107,6 +107,37 @@ int gsn_gemm1_glu_dwconv_bf16(const void* a, const void* w1_glu, const float* s1
                               const void* dw_w, const void* dw_b, void* d, int B, int T, int K, int N,
                               const int32_t* lengths, gsn_stream_t stream);
 
+/* ---- LayerNorm folded into the up_conv GEMM -----------------------------------------------------------------
+ * No single counterpart in the reference: ConformerConvModule.norm (conformer.py:164,176) followed by up_conv
+ * (:165,177).  LN(x) W^T + b = rstd * (x W'^T) - (rstd * mean) * c + b' with W' = bf16(W * gamma) (per input
+ * channel), b' = b + W beta and c = sum_k W'[n, k]: the GEMM runs on the raw frames and the LayerNorm output is
+ * never written.  Unlike the two-step path it does not round the LayerNorm output to bf16 (the weights carry gamma
+ * instead); results agree with the reference module within the same tolerances.
+ *
+ * gsn_fold_layernorm_bf16: once per weight set.  w1_glu [N, K] bf16 (GLU-interleaved), b1_glu [N] fp32, ln_w /
+ * ln_b [K] bf16 -> w1g_glu [N, K] bf16, b1g_glu [N] fp32, c1_glu [N] fp32.  K % 256 == 0.
+ * gsn_layernorm_stats_bf16: stats [M][2] fp32 = (rstd, rstd * mean) per frame, the statistics of
+ * gsn_layernorm_bf16; frames t >= lengths[b] are left unwritten.
+ * gsn_gemm1_lnfold_glu_dwconv_bf16: gsn_gemm1_glu_dwconv_bf16 on the raw frames x [B*T, K] with the folded
+ * weights and the row statistics.
+ * gsn_conv_module_lnfold_bf16: gsn_conv_module_bf16 with the folded weights (T % 128 == 0), three launches:
+ * statistics, fused up_conv + GLU + depthwise + SiLU, down_conv + residual.  Workspace as for
+ * gsn_conv_module_bf16. */
+int gsn_fold_layernorm_bf16(const void* w1_glu, const float* b1_glu, const void* ln_w, const void* ln_b,
+                            void* w1g_glu, float* b1g_glu, float* c1_glu, int N, int K, gsn_stream_t stream);
+
+int gsn_layernorm_stats_bf16(const void* x, int64_t ld_x, float* stats, int M, int D, float eps,
+                             const int32_t* lengths, int T, gsn_stream_t stream);
+
+int gsn_gemm1_lnfold_glu_dwconv_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                     const float* row_stats, const void* dw_w, const void* dw_b, void* d, int B,
+                                     int T, int K, int N, const int32_t* lengths, gsn_stream_t stream);
+
+int gsn_conv_module_lnfold_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                                const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
+                                float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
 /* ---- int8 weights widened once per call -------------------------------------------------------------------
  * No counterpart in the reference (its int8 analogue is torchao W8A8, bench_asr.py:92-105).  For large M the
  * weight bytes are negligible next to the activations, so the int8 module widens both weight matrices to bf16
