@@ -37,6 +37,7 @@ N_UTTS = 512
 D, I = synth.D_MODEL, synth.D_INNER
 GEMM1_FLOP_PER_FRAME = 2 * D * 2 * I          # 8.389 MFLOP
 GEMM2_FLOP_PER_FRAME = 2 * I * D              # 4.194 MFLOP
+FF_FLOP_PER_FRAME = 2 * D * 4 * D             # 8.389 MFLOP per feed-forward GEMM
 # DRAM bytes (read + write) of the fused up_conv + GLU + depthwise kernel per row of the 128-row tiles it computes,
 # from one ncu capture of a B=48, T=1536 chunk (profiles/gemm_glu_dw_b48_t1536.md: 73.0 + 83.1 MB over 31,104
 # rows); the traffic of a launch scales with the rows it computes.
@@ -128,7 +129,7 @@ def _workload_plan(rank: int, workload: str):
         lens = synth.sample_lengths(1005 + 7919 * rank, N_UTTS)
         return dispatch.plan_chunks(lens, exec_batch=dispatch.EXEC_BATCH, logical_batch=dispatch.LOGICAL_BATCH,
                                     frame_grid=dispatch.FRAME_GRID)
-    if workload in ("module", "module_i8"):
+    if workload in ("module", "module_i8", "ff"):
         lens = synth.sample_lengths(1003 + 7919 * rank, 48)
         T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
         return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
@@ -146,10 +147,13 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
     """frames/s (valid frames x layers per second) of the numpy oracle (float32, all host threads through BLAS) on a
     bounded sample of the workload: the shortest chunks of the plan, one layer each, until budget_s is spent."""
     from oracle import conv_module as O
+    from oracle import feed_forward as FFO
     chunks = _workload_plan(rank, workload)
     if workload == "dw":
         w, b = synth.make_dw_weights(1002)
         wb, bb = O.bf16_round(w), O.bf16_round(b)
+    elif workload == "ff":
+        ffprep = FFO.prepare_ff_fp32(synth.make_ff_params(1006))
     else:
         params = synth.make_params(1005)
         prep = O.prepare_fp32(params)
@@ -166,6 +170,8 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
         lens = c.lengths[:B]
         if workload == "dw":
             O.dwconv_silu(x, wb, bb, lengths=lens, round_out=False)
+        elif workload == "ff":
+            FFO.feed_forward_half(x, ffprep, lengths=lens, mode="fp32", dtype=np.float32)
         else:
             O.conv_module(x, prep, lengths=lens, mode="fp32", dtype=np.float32)
         frames += int(lens.sum())
@@ -212,7 +218,9 @@ def _config(args, world):
                  "residual), 512 utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid",
         "module": "one conv module, B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
         "module_i8": "one conv module with int8 per-channel weights, B=48 chunk, lognormal lengths, length mask",
-        "dw": "depthwise k15 + bias + SiLU alone, bf16 [48, 1024, 2048] channels-last, all frames valid"}[w],
+        "dw": "depthwise k15 + bias + SiLU alone, bf16 [48, 1024, 2048] channels-last, all frames valid",
+        "ff": "one feed-forward half of the Conformer block (LN, 1024->4096 GEMM+SiLU, 4096->1024 GEMM + 0.5x "
+              "residual), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask"}[w],
         "d_model": D, "d_inner": I, "kernel": 15, "layers": _layers_for(w),
         "utterances_per_rank": N_UTTS if w == "stack" else 48, "exec_batch": dispatch.EXEC_BATCH,
         "frame_grid": dispatch.FRAME_GRID, "parallelism": f"dp{world} (independent shards, no collective)",
@@ -256,6 +264,10 @@ def run_ours(args):
         xs = [torch.randn((c.B, c.T, I), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
         ys = [torch.empty_like(x) for x in xs]
         layers = []
+    elif workload == "ff":
+        from granite_conv_b200.weights import prepare_ff_from_params
+        layers = [prepare_ff_from_params(synth.make_ff_params(1006), device=dev)]
+        xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     else:
         # bf16: the LayerNorm folded into the up_conv GEMM (the module op's path for T on the 128 grid)
         layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8, ln_fold=not int8)
@@ -264,6 +276,8 @@ def run_ours(args):
     lens_dev = [torch.from_numpy(c.lengths).to(dev) for c in chunks]
     max_m = max(c.padded_frames for c in chunks)
     ws_bytes = int(L.gsn_conv_module_workspace_bytes(1, max_m, D, I))
+    if workload == "ff":
+        ws_bytes = max(ws_bytes, int(L.gsn_ff_half_workspace_bytes(1, max_m, D, 4 * D)))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     h_buf = ws                                                         # [M, I] GLU output
     t_off = ((max_m * I * 2 + 255) // 256) * 256
@@ -326,6 +340,28 @@ def run_ours(args):
             ev[3].record(stream)
             layer_events.append((ev, c))
 
+    def ff_kernels(x, out, c, p, lens, record):
+        """The three launches of gsn_ff_half_bf16: LayerNorm, up_proj + SiLU, down_proj + half-step residual."""
+        M, T, F = c.padded_frames, c.T, p.d_ff
+        tp = ws.data_ptr()                                   # LayerNorm output [M, D]
+        hp = ws.data_ptr() + ((M * D * 2 + 255) // 256) * 256   # SiLU output [M, F]
+        lp = lens.data_ptr()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            ev[0].record(stream)
+        _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
+                                        p.ln_eps, lp, T, sp), "layernorm")
+        if record:
+            ev[1].record(stream)
+        _lib.check(L.gsn_gemm_silu_bf16(tp, p.w_up.data_ptr(), p.b_up.data_ptr(), hp, M, D, F, lp, T, sp), "ff up")
+        if record:
+            ev[2].record(stream)
+        _lib.check(L.gsn_gemm_residual_scaled_bf16(hp, p.w_down.data_ptr(), p.b_down.data_ptr(), x.data_ptr(), D,
+                                                   out.data_ptr(), D, M, F, D, 0.5, lp, T, sp), "ff down")
+        if record:
+            ev[3].record(stream)
+            layer_events.append((ev, c))
+
     dw_events = []
 
     def step(record=False):
@@ -347,9 +383,13 @@ def run_ours(args):
             src = xs[ci]
             for li, p in enumerate(layers):
                 dst = act[ci] if li % 2 == 0 else act2[ci]
-                layer_kernels(src, dst, c, p, lens_dev[ci], record)
+                if workload == "ff":
+                    ff_kernels(src, dst, c, p, lens_dev[ci], record)
+                    n += 3
+                else:
+                    layer_kernels(src, dst, c, p, lens_dev[ci], record)
+                    n += 4 if int8 else 3
                 src = dst
-                n += 4 if int8 else 3
         return n
 
     def barrier():
@@ -396,6 +436,14 @@ def run_ours(args):
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
+    elif workload == "ff":
+        kernels = _ff_breakdown(layer_events, peaks)
+        g1 = kernels["ff_up_silu"]
+        roof = {"kernel": "gemm_kernel<SILU> (up_proj 1024->4096 + SiLU)", "bound": "tensor",
+                "achieved": g1["achieved"], "peak": g1["peak"], "unit": "TFLOP/s", "frac": g1["frac"],
+                "traffic": None, "per_launch_ms": g1["ms_per_launch"], "algorithmic_flop_per_frame": FF_FLOP_PER_FRAME,
+                "frames_counted": "rows of the 128-row tiles holding valid frames",
+                "peak_source": f"bf16_tflops_sustained of {peaks['source']}", "kernels": kernels}
     else:
         kernels = _kernel_breakdown(layer_events, peaks, widen_events, ln_name="layernorm" if int8 else "ln_stats")
         g1 = kernels["gemm1_glu_dw"]
@@ -414,7 +462,7 @@ def run_ours(args):
     # ---- end to end through the public op with pinned host buffers
     e2e = None
     if workload != "dw" and not args.no_e2e:
-        e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier)
+        e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -439,6 +487,30 @@ def run_ours(args):
 def _tile_rows(c, tile=128):
     """Rows of the 128-row tiles that hold at least one valid frame (T is on the 128 grid)."""
     return int(sum(((int(L) + tile - 1) // tile) * tile for L in c.lengths))
+
+
+def _ff_breakdown(layer_events, peaks):
+    """Per-kernel launch time and rate of the feed-forward half: LayerNorm (2 x 2 KB per valid frame), the two
+    GEMMs (8.389 MFLOP per computed row each)."""
+    names = ("layernorm", "ff_up_silu", "ff_down_residual")
+    tot = {n: 0.0 for n in names}
+    work = {n: 0.0 for n in names}
+    for ev, c in layer_events:
+        for k, n in enumerate(names):
+            tot[n] += ev[k].elapsed_time(ev[k + 1])
+        rows = _tile_rows(c)
+        work["layernorm"] += c.valid_frames * 2 * D * 2
+        work["ff_up_silu"] += rows * FF_FLOP_PER_FRAME
+        work["ff_down_residual"] += rows * FF_FLOP_PER_FRAME
+    all_ms = sum(tot.values())
+    out = {}
+    for n in names:
+        tensor = n.startswith("ff_")
+        ach = work[n] / (tot[n] / 1e3) / (1e12 if tensor else 1e9)
+        pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
+        out[n] = {"ms_per_launch": tot[n] / len(layer_events), "share": tot[n] / all_ms, "achieved": ach,
+                  "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
+    return out
 
 
 def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm"):
@@ -474,13 +546,17 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
     return out
 
 
-def _e2e(args, chunks, layers, int8, dev, stream, world, barrier):
-    """Same work through the public op (torch.ops.granite.conv_module per layer) with each chunk's input copied
-    from pinned host memory and its output copied back inside the timed region."""
+def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False):
+    """Same work through the public op (torch.ops.granite.conv_module per layer, or granite::feed_forward_half)
+    with each chunk's input copied from pinned host memory and its output copied back inside the timed region."""
     import torch
 
-    from granite_conv_b200 import ConvModuleStack
-    stack = ConvModuleStack(layers, int8=int8)
+    from granite_conv_b200 import ConvModuleStack, ops
+    if ff:
+        def stack(x, lengths):
+            return ops.run_feed_forward_half(x, layers[0], lengths)
+    else:
+        stack = ConvModuleStack(layers, int8=int8)
     g = torch.Generator().manual_seed(4242)
     hx = [torch.randn((c.B, c.T, D), generator=g).to(torch.bfloat16).pin_memory() for c in chunks]
     hl = [torch.from_numpy(c.lengths).pin_memory() for c in chunks]
@@ -560,7 +636,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff"], default="stack")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

@@ -353,6 +353,72 @@ int gsn_widen_i8_bf16(const void* q0, void* out0, int64_t n0, const void* q1, vo
   return finish(launch_widen_i8(q0, out0, n0, q1, out1, n1, (cudaStream_t)stream), name);
 }
 
+int gsn_gemm_silu_bf16(const void* a, const void* w, const float* b, void* h, int M, int K, int N,
+                       const int32_t* lengths, int T, gsn_stream_t stream) {
+  const char* name = "gsn_gemm_silu_bf16";
+  if (int rc = check_gemm(name, a, w, b, h, M, K, N)) return rc < 0 ? ok() : rc;
+  if (int rc = check_lengths(name, lengths, T, M)) return rc;
+  GemmArgs g{(const __nv_bfloat16*)a, w, b, nullptr, nullptr, (__nv_bfloat16*)h, (int64_t)N, 0, M, N, K, 0,
+             lengths, T};
+  return finish(launch_gemm(g, kEpiSilu, (cudaStream_t)stream), name);
+}
+
+int gsn_gemm_residual_scaled_bf16(const void* d, const void* w, const float* b, const void* residual, int64_t ld_res,
+                                  void* out, int64_t ld_out, int M, int K, int N, float out_scale,
+                                  const int32_t* lengths, int T, gsn_stream_t stream) {
+  const char* name = "gsn_gemm_residual_scaled_bf16";
+  if (int rc = check_gemm(name, d, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
+  if (residual && !aligned(residual, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: residual must be 16-byte aligned", name);
+  if (ld_out % 8 || ld_out < N || (residual && (ld_res % 8 || ld_res < N)))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: row strides must be >= N and multiples of 8", name);
+  if (int rc = check_lengths(name, lengths, T, M)) return rc;
+  GemmArgs g{(const __nv_bfloat16*)d, w, b, nullptr, (const __nv_bfloat16*)residual, (__nv_bfloat16*)out, ld_out,
+             ld_res, M, N, K, 0, lengths, T, out_scale};
+  return finish(launch_gemm(g, kEpiResidual, (cudaStream_t)stream), name);
+}
+
+size_t gsn_ff_half_workspace_bytes(int B, int T, int D, int F) {
+  if (B <= 0 || T <= 0 || D <= 0 || F <= 0) return 0;
+  const size_t M = (size_t)B * (size_t)T;
+  return align256(M * (size_t)D * 2) + align256(M * (size_t)F * 2);
+}
+
+int gsn_ff_half_bf16(const void* x, const void* ln_w, const void* ln_b, const void* w_up, const float* b_up,
+                     const void* w_down, const float* b_down, const int32_t* lengths, void* out, int B, int T, int D,
+                     int F, float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  const char* name = "gsn_ff_half_bf16";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if ((int64_t)B * T == 0) return ok();
+  if (!x || !ln_w || !ln_b || !w_up || !b_up || !w_down || !b_down || !out)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!ln_dim_ok(D) || F % 256 != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d F=%d (D in {256..2048}, F %% 256 == 0)", name, D, F);
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  const int M = B * T;
+  const size_t need = gsn_ff_half_workspace_bytes(B, T, D, F);
+  if (!workspace || workspace_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w_up, 16) || !aligned(w_down, 16) || !aligned(b_up, 16) ||
+      !aligned(b_down, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: x, out, weights and biases must be 16-byte aligned", name);
+  // workspace: t = LayerNorm output [M, D], then h = silu(t W_up^T + b_up) [M, F]
+  __nv_bfloat16* t = (__nv_bfloat16*)workspace;
+  __nv_bfloat16* h = (__nv_bfloat16*)((char*)workspace + align256((size_t)M * D * 2));
+  const cudaStream_t st = (cudaStream_t)stream;
+  const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
+  int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
+                            M, D, ln_eps, skip, T, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g1{t, w_up, b_up, nullptr, nullptr, h, (int64_t)F, 0, M, F, D, 0, skip, T};
+  rc = launch_gemm(g1, kEpiSilu, st);
+  if (rc) return finish(rc, name);
+  // the half-step residual of ConformerBlock.forward: out = x + 0.5 * (h W_down^T + b_down)
+  GemmArgs g2{h, w_down, b_down, nullptr, (const __nv_bfloat16*)x, (__nv_bfloat16*)out, D, D, M, D, F, 0, skip, T,
+              0.5f};
+  return finish(launch_gemm(g2, kEpiResidual, st), name);
+}
+
 size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
   if (B <= 0 || T <= 0 || D <= 0 || inner <= 0) return 0;
   const size_t M = (size_t)B * (size_t)T;

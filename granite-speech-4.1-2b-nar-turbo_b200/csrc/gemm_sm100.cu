@@ -2,6 +2,8 @@
 //
 //   up_conv   (models/granite_speech_nar/conformer.py:165,177) + GLU (:166,:181)  -> kEpiGlu
 //   down_conv (conformer.py:170,187) + the block's residual add (conformer.py:207)  -> kEpiResidual
+//   feed-forward up_proj + SiLU (conformer.py:27-29,35-36)                          -> kEpiSilu
+//   feed-forward down_proj + the block's half-step residual (conformer.py:37,205)   -> kEpiResidual, out_scale 0.5
 //
 // Layout: A = activations [M, K] bf16 row-major (M = B*T frames, channels-last), W = weights [N, K] (the Conv1d
 // weight [N, K, 1] as stored), both K-major, so D = A * W^T accumulates in TMEM in fp32.
@@ -56,6 +58,7 @@ struct KParams {
   int64_t ld_out, ld_res;
   int M, N, K;
   int T;                                  // frames per utterance when lengths != null (T % 128 == 0)
+  float out_scale;                        // residual epilogue: out = out_scale * (acc * scale + bias) + residual
 };
 
 // 128-row block `blk` of the M range holds at least one valid frame (a block lies inside one utterance)
@@ -115,6 +118,9 @@ struct __align__(1024) EpiSmem {
 template <int EPI, bool SCALED>
 struct Epilogue {
   static constexpr int NU = (EPI == kEpiGlu ? BN / 2 : BN) / BOX;   // 32-column output sub-tiles per tile
+  float alpha;                            // residual epilogue: scale of acc * scale + bias
+  const int* lengths;                     // SiLU epilogue: rows of padding frames are written as zero
+  int T;
   float* vb;
   float* vs;
   uint8_t* stage0;                        // stage box b at stage0 + b * BOX_BYTES
@@ -133,6 +139,9 @@ struct Epilogue {
     tmO = o;
     tmR = r;
     has_res = EPI == kEpiResidual && p.residual != nullptr;
+    alpha = EPI == kEpiResidual ? p.out_scale : 1.0f;
+    lengths = p.lengths;
+    T = p.T;
     lane = threadIdx.x & 31;
     swz = (lane >> 1) & 3;
     su = 0;
@@ -141,6 +150,8 @@ struct Epilogue {
   // The tile's 256 bias (and scale) values into the warp's slice.  For the GLU they are halved:
   // a * sigmoid(g) = a' + a' * tanh(g') with a' = a / 2 and g' = g / 2 (exact scalings).
   __device__ void load_vectors(const KParams& p, int nb) {
+    // GLU works on halved pre-activations (a * sigmoid(g) = a' + a' * tanh(g')); SiLU and the residual
+    // epilogue take the vectors as they are
     const float h = EPI == kEpiGlu ? 0.5f : 1.0f;
     __syncwarp();
     const float4* src = reinterpret_cast<const float4*>(p.bias + nb);
@@ -174,6 +185,13 @@ struct Epilogue {
   // Drain one tile: `t_row` is the TMEM address of this warp's accumulator rows (unused when !active, i.e. a
   // residual tile of pure padding).  Returns false if a wait ran out.
   __device__ bool run(int row0, int ocol0, bool active, uint32_t t_row, volatile int* abort_flag) {
+    // SiLU: this lane's row is a padding frame -> zero, so the next GEMM sees what a masked input gives
+    bool row_valid = true;
+    if (EPI == kEpiSilu && lengths != nullptr) {
+      const int row = row0 + lane;
+      const int b = row / T;
+      row_valid = row - b * T < __ldg(lengths + b);
+    }
     for (int u = 0; u < NU; ++u, ++su) {
       const uint32_t buf = su & 1;
       uint8_t* sb = stage0 + buf * BOX_BYTES;
@@ -236,6 +254,16 @@ struct Epilogue {
           for (int c = 0; c < 4; ++c) {
             const int k = c4 + c;
             o[k] = fmaf(__uint_as_float(v[k >> 4][k & 15]), sv[c], bv[c]);
+            if (EPI == kEpiSilu) {
+              // the Linear output is a bf16 tensor before the SiLU (conformer.py:35-36): round it, then
+              // silu(y) = h + h tanh(h) with h = y / 2
+              const float hh = 0.5f * bf16_round_f32(o[k]);
+              o[k] = row_valid ? fmaf(hh, tanh_approx(hh), hh) : 0.f;
+            } else if (alpha != 1.0f) {
+              // the scaled residual of the feed-forward halves: the Linear output is rounded to bf16 before the
+              // 0.5 * ff(x) + x of ConformerBlock.forward (conformer.py:205)
+              o[k] = alpha * bf16_round_f32(o[k]);
+            }
           }
         }
         if (has_res) {
@@ -468,7 +496,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
       const int m_blk = tile / num_n;
       const int n_blk = tile - m_blk * num_n;
       const bool active = rows_active(p, m_blk);
-      if (EPI == kEpiGlu && !active) continue;   // GLU rows of padding frames are never read downstream
+      if (EPI != kEpiResidual && !active) continue;   // GLU / SiLU rows of padding frames are never read downstream
       const int nb = n_blk * BN;
       epi.load_vectors(p, nb);
       const int row0 = m_blk * BM + q * 32;
@@ -728,7 +756,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const int mp = tile / num_n;
       const int n_blk = tile - mp * num_n;
       const bool active = pair_active(mp);
-      if (EPI == kEpiGlu && !active) continue;
+      if (EPI != kEpiResidual && !active) continue;
       const int nb = n_blk * BN;
       epi.load_vectors(p, nb);
       const int row0 = mp * 256 + (int)rank * 128 + q * 32;
@@ -822,6 +850,7 @@ KParams make_params(const GemmArgs& a) {
   p.N = a.N;
   p.K = a.K;
   p.T = a.T;
+  p.out_scale = a.out_scale;
   return p;
 }
 
@@ -913,7 +942,7 @@ int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* 
 }
 
 int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
-  if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale) {
+  if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale && epilogue != kEpiSilu && a.out_scale == 1.0f) {
     bool launched = false;
     const int rc = epilogue == kEpiGlu ? launch_pair<kEpiGlu>(a, stream, &launched)
                                        : launch_pair<kEpiResidual>(a, stream, &launched);
@@ -924,6 +953,10 @@ int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
   if (epilogue == kEpiGlu) {
     if (a.w_int8) return launch_single<kEpiGlu, true, true>(a, stream);
     return a.col_scale ? launch_single<kEpiGlu, false, true>(a, stream) : launch_single<kEpiGlu, false, false>(a, stream);
+  }
+  if (epilogue == kEpiSilu) {
+    if (a.w_int8 || a.col_scale) return (int)cudaErrorInvalidValue;
+    return launch_single<kEpiSilu, false, false>(a, stream);
   }
   if (a.w_int8) return launch_single<kEpiResidual, true, true>(a, stream);
   return a.col_scale ? launch_single<kEpiResidual, false, true>(a, stream)

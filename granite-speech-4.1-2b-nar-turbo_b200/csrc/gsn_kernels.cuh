@@ -35,10 +35,11 @@ struct GemmArgs {
   int M, N, K;
   int w_int8;
   const int* lengths;            // null, or per-utterance valid frames: 128-row tiles of pure padding are
-  int T;                         //   skipped (GLU) or written as residual + bias (RESIDUAL); needs T % 128 == 0
+  int T;                         //   skipped (GLU, SILU) or written as residual + bias (RESIDUAL); T % 128 == 0
+  float out_scale = 1.0f;        // RESIDUAL: out = out_scale * (acc * col_scale + bias) + residual
 };
 
-enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1 };
+enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2 };
 
 int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
 // int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).

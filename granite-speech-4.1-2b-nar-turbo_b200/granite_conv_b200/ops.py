@@ -13,6 +13,8 @@ plus the ops of the whole module (new):
   add_residual)``
 * ``granite::conv_module_lnfold(x, w1g_glu, b1g_glu, c1_glu, dw_w, dw_b, w2, b2, lengths?, ln_eps, add_residual)``
   (the LayerNorm folded into the up_conv GEMM; T % 128 == 0)
+* ``granite::feed_forward_half(x, ln_w, ln_b, w_up, b_up, w_down, b_down, lengths?, ln_eps)`` (x + 0.5 FF(x))
+* ``granite::layer_norm(x, weight, bias, eps)`` (the block's post LayerNorm)
 
 All are ``mutates_args=()``, CUDA-only, launch on ``torch.cuda.current_stream()`` (as ``jit.py:180-181``) and
 have ``register_fake`` implementations whose strides equal the real outputs', so ``torch.compile(fullgraph=True)``
@@ -211,6 +213,54 @@ def _(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, 
 
 
 # ---------------------------------------------------------------------------------------------------------------
+# ---- the rest of the Conformer block: feed-forward halves and the post LayerNorm -------------------------------
+@torch.library.custom_op("granite::feed_forward_half", mutates_args=(), device_types="cuda")
+def feed_forward_half(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w_up: torch.Tensor,
+                      b_up: torch.Tensor, w_down: torch.Tensor, b_down: torch.Tensor,
+                      lengths: Optional[torch.Tensor], ln_eps: float) -> torch.Tensor:
+    """x + 0.5 * ConformerFeedForward(x) (conformer.py:23-40, :205, :208) on bf16 x [B, T, D]."""
+    name = "granite::feed_forward_half"
+    _require_cuda(name, x, ln_w, ln_b, w_up, b_up, w_down, b_down, lengths)
+    if x.dim() != 3 or x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: x must be bf16 [B, T, D], got {x.dtype} {tuple(x.shape)}")
+    B, T, D = x.shape
+    F = w_up.shape[0]
+    xc = x.contiguous()
+    lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    out = torch.empty_like(xc)
+    nbytes = int(_lib.lib().gsn_ff_half_workspace_bytes(B, T, D, F)) if B * T > 0 else 0
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    _lib.call("gsn_ff_half_bf16", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w_up.data_ptr(), b_up.data_ptr(),
+              w_down.data_ptr(), b_down.data_ptr(), _ptr(lens), out.data_ptr(), B, T, D, F, float(ln_eps),
+              ws.data_ptr(), nbytes, _stream(xc))
+    return out
+
+
+@feed_forward_half.register_fake
+def _(x, ln_w, ln_b, w_up, b_up, w_down, b_down, lengths, ln_eps):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+@torch.library.custom_op("granite::layer_norm", mutates_args=(), device_types="cuda")
+def layer_norm_op(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float) -> torch.Tensor:
+    """nn.LayerNorm over the last dim of bf16 x [..., D] (the block's post_norm, conformer.py:199, :209)."""
+    _require_cuda("granite::layer_norm", x, weight, bias)
+    D = x.shape[-1]
+    x2 = x.contiguous().view(-1, D)
+    return layernorm(x2, weight, bias, eps).view(x.shape)
+
+
+@layer_norm_op.register_fake
+def _(x, weight, bias, eps):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+def run_feed_forward_half(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x + 0.5 * FF(x) with a :class:`~granite_conv_b200.weights.PreparedFeedForward`."""
+    return torch.ops.granite.feed_forward_half(x, p.ln_w, p.ln_b, p.w_up, p.b_up, p.w_down, p.b_down, lengths,
+                                               p.ln_eps)
+
+
 def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, add_residual: bool = True,
                     int8: bool = False, ln_fold: Optional[bool] = None) -> torch.Tensor:
     """Call the fused module op with a :class:`~granite_conv_b200.weights.PreparedConvModule`.  ``ln_fold``: use

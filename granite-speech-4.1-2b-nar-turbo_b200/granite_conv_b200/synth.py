@@ -73,6 +73,38 @@ def make_params(seed: int, d_model: int = D_MODEL, d_inner: int = D_INNER, kerne
     )
 
 
+FF_MULT = 4              # EncoderConfig.feedforward_mult
+
+
+@dataclass
+class FeedForwardParams:
+    """Parameters of one ConformerFeedForward (``models/granite_speech_nar/conformer.py:23-40``), named after its
+    state_dict keys (pre_norm, up_proj, down_proj).  All arrays are float32."""
+
+    norm_weight: np.ndarray        # (D,)
+    norm_bias: np.ndarray          # (D,)
+    up_weight: np.ndarray          # (F, D)    up_proj.weight, F = 4 D
+    up_bias: np.ndarray            # (F,)
+    down_weight: np.ndarray        # (D, F)    down_proj.weight
+    down_bias: np.ndarray          # (D,)
+    ln_eps: float = 1e-5
+
+
+def make_ff_params(seed: int, d_model: int = D_MODEL, mult: int = FF_MULT, w_std: float = 0.02) -> FeedForwardParams:
+    """Random-init parameters of one feed-forward half, the same distributions as :func:`make_params`."""
+    g = np.random.default_rng(seed)
+    f32 = np.float32
+    d_ff = mult * d_model
+    return FeedForwardParams(
+        norm_weight=(1.0 + g.normal(0.0, 0.02, d_model)).astype(f32),
+        norm_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+        up_weight=g.normal(0.0, w_std, (d_ff, d_model)).astype(f32),
+        up_bias=g.normal(0.0, 0.02, d_ff).astype(f32),
+        down_weight=g.normal(0.0, w_std, (d_model, d_ff)).astype(f32),
+        down_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+    )
+
+
 def make_activations(seed: int, shape: tuple[int, ...]) -> np.ndarray:
     """x ~ N(0, 1), float32."""
     return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)

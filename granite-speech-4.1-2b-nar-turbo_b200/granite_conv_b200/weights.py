@@ -188,3 +188,49 @@ def prepare_from_params(params, device="cuda", int8: bool = False, ln_fold: bool
     return prepare_from_tensors(t(params.norm_weight), t(params.norm_bias), t(params.up_weight), t(params.up_bias),
                                 dw_w, dw_b, t(params.down_weight), t(params.down_bias), ln_eps=params.ln_eps,
                                 device=device, int8=int8, ln_fold=ln_fold)
+
+
+@dataclass
+class PreparedFeedForward:
+    """Device operands of one ConformerFeedForward (``models/granite_speech_nar/conformer.py:23-40``)."""
+
+    ln_w: torch.Tensor          # [D] bf16
+    ln_b: torch.Tensor          # [D] bf16
+    w_up: torch.Tensor          # [F, D] bf16 (up_proj.weight as stored)
+    b_up: torch.Tensor          # [F] fp32
+    w_down: torch.Tensor        # [D, F] bf16
+    b_down: torch.Tensor        # [D] fp32
+    ln_eps: float = 1e-5
+
+    @property
+    def d_model(self) -> int:
+        return int(self.ln_w.shape[0])
+
+    @property
+    def d_ff(self) -> int:
+        return int(self.w_up.shape[0])
+
+
+@torch.no_grad()
+def prepare_ff_from_tensors(ln_w, ln_b, up_w, up_b, down_w, down_b, ln_eps=1e-5, device="cuda") -> PreparedFeedForward:
+    bf = torch.bfloat16
+    dev = torch.device(device)
+    return PreparedFeedForward(
+        ln_w=ln_w.to(dev, bf).contiguous(), ln_b=ln_b.to(dev, bf).contiguous(),
+        w_up=up_w.to(dev, bf).contiguous(), b_up=up_b.to(dev, bf).float().contiguous(),
+        w_down=down_w.to(dev, bf).contiguous(), b_down=down_b.to(dev, bf).float().contiguous(), ln_eps=float(ln_eps))
+
+
+@torch.no_grad()
+def prepare_feed_forward(m: nn.Module, device="cuda") -> PreparedFeedForward:
+    """Operands of a ConformerFeedForward with the reference attribute names (pre_norm, up_proj, down_proj)."""
+    return prepare_ff_from_tensors(m.pre_norm.weight, m.pre_norm.bias, m.up_proj.weight, m.up_proj.bias,
+                                   m.down_proj.weight, m.down_proj.bias, ln_eps=m.pre_norm.eps, device=device)
+
+
+def prepare_ff_from_params(params, device="cuda") -> PreparedFeedForward:
+    """Operands from float32 parameters (``synth.FeedForwardParams``) as a bf16 model load makes them."""
+    t = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    return prepare_ff_from_tensors(t(params.norm_weight), t(params.norm_bias), t(params.up_weight),
+                                   t(params.up_bias), t(params.down_weight), t(params.down_bias),
+                                   ln_eps=params.ln_eps, device=device)

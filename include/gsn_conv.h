@@ -187,6 +187,30 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                         int add_residual, void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
                         size_t workspace_bytes, gsn_stream_t stream);
 
+/* ---- feed-forward halves of the Conformer block ---------------------------------------------------------------
+ * Replace ConformerFeedForward (conformer.py:23-40: pre_norm -> up_proj -> SiLU -> down_proj) together with the
+ * block's half-step residual x + 0.5 * ff(x) (conformer.py:205, :208).  Dropout is the identity (inference).
+ * gsn_gemm_silu_bf16: h = silu(a W^T + b), a [M, K], W [N, K] bf16 (the Linear weight as stored), b [N] fp32;
+ * lengths / T as for gsn_gemm1_glu_bf16: rows of pure-padding tiles are left unwritten, other padding rows are
+ * written as zero (what a masked input gives).  K % 64, N % 256 == 0.
+ * gsn_gemm_residual_scaled_bf16: out = out_scale * (d W^T + b) + residual (residual may be NULL), otherwise as
+ * gsn_gemm2_residual_bf16.
+ * gsn_ff_half_bf16: out = x + 0.5 * down(silu(up(layernorm(x)))) on x [B, T, D] bf16, w_up [F, D], w_down [D, F]
+ * bf16, b_up [F], b_down [D] fp32, LayerNorm gamma / beta bf16; with lengths and T % 128 == 0, padded frames of
+ * out are x + 0.5 * b_down.  Workspace: gsn_ff_half_workspace_bytes(B, T, D, F) bytes, 256-byte aligned. */
+int gsn_gemm_silu_bf16(const void* a, const void* w, const float* b, void* h, int M, int K, int N,
+                       const int32_t* lengths, int T, gsn_stream_t stream);
+
+int gsn_gemm_residual_scaled_bf16(const void* d, const void* w, const float* b, const void* residual, int64_t ld_res,
+                                  void* out, int64_t ld_out, int M, int K, int N, float out_scale,
+                                  const int32_t* lengths, int T, gsn_stream_t stream);
+
+size_t gsn_ff_half_workspace_bytes(int B, int T, int D, int F);
+
+int gsn_ff_half_bf16(const void* x, const void* ln_w, const void* ln_b, const void* w_up, const float* b_up,
+                     const void* w_down, const float* b_down, const int32_t* lengths, void* out, int B, int T, int D,
+                     int F, float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
 /* ---- whole module without any allocation ------------------------------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory where they run the module —
  * a plugin inside a host application that owns the GPU memory budget and its allocator, or a latency-critical

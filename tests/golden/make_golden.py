@@ -12,7 +12,9 @@ What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/
   ``conv_kernel.py:91-95``), with and without trimming each utterance to its length;
 * the post-fold eager chain that ``granite::dwconv_silu`` replaces, ``F.silu(conv0(x))``
   (``conv_kernel.py:95-96``), and the fp64 golden of ``script/cuda_kernels/conv1d.py:135-138``;
-* the GLU variant's eager chain ``F.silu(conv0(F.glu(x2, dim=1)))`` (``conv_kernel.py:91-92``).
+* the GLU variant's eager chain ``F.silu(conv0(F.glu(x2, dim=1)))`` (``conv_kernel.py:91-92``);
+* ``ConformerFeedForward`` (``conformer.py:23-40``) as the block applies it, ``x + 0.5 * ff(x)``
+  (``conformer.py:205``, ``:208``), in fp32 and bf16 on the test-fire shape.
 
 Inputs and parameters come from ``granite_conv_b200.synth`` (numpy PCG64 seeds), so the tests regenerate them
 bit-for-bit and only the reference outputs are stored.  bf16 tensors are stored as uint16 bit patterns.
@@ -130,6 +132,29 @@ def main(ref_root: str) -> None:
     np.savez_compressed(os.path.join(HERE, "dwconv_silu_stats_c2048t261.npz"),
                         chan_sum=g.sum(axis=-1).reshape(-1), chan_sumsq=(g * g).sum(axis=-1).reshape(-1))
     out["dwconv_silu_stats"] = g.shape
+
+    # ---- feed-forward half of the block: x + 0.5 * ConformerFeedForward(x) (conformer.py:23-40, :205, :208) ------
+    from models.granite_speech_nar.conformer import ConformerFeedForward  # noqa: E402
+    for tag, seed, w_std in (("w002", 1101, 0.02), ("w006", 1102, 0.06)):
+        fp = synth.make_ff_params(seed, w_std=w_std)
+        ff = ConformerFeedForward(EC())
+        with torch.no_grad():
+            ff.pre_norm.weight.copy_(torch.from_numpy(fp.norm_weight))
+            ff.pre_norm.bias.copy_(torch.from_numpy(fp.norm_bias))
+            ff.up_proj.weight.copy_(torch.from_numpy(fp.up_weight))
+            ff.up_proj.bias.copy_(torch.from_numpy(fp.up_bias))
+            ff.down_proj.weight.copy_(torch.from_numpy(fp.down_weight))
+            ff.down_proj.bias.copy_(torch.from_numpy(fp.down_bias))
+        ff.eval()
+        x = synth.make_activations(seed + 500, (2, 37, synth.D_MODEL))
+        # fp32 and bf16 (a bf16 model load) on the test-fire shape
+        xf = torch.from_numpy(x)
+        y32 = (0.5 * ff(xf) + xf).numpy()
+        ffb = ff.to(torch.bfloat16)
+        xb = xf.to(torch.bfloat16)
+        yb = 0.5 * ffb(xb) + xb
+        np.savez_compressed(os.path.join(HERE, f"ff_half_b2t37_{tag}.npz"), bf16=_bits(yb), fp32=y32)
+        out[f"ff_half_{tag}"] = tuple(yb.shape)
 
     for k, v in out.items():
         print(f"{k}: {v}")

@@ -103,3 +103,19 @@ def test_quantize_per_channel():
     assert np.all(np.abs(q).max(axis=1)[np.arange(64) != 3] == 127)
     assert s[3] == 1.0 and not q[3].any()
     assert np.max(np.abs(q * s[:, None] - w)) <= 0.5 * s.max() + 1e-9
+
+
+@pytest.mark.parametrize("tag,seed", [("w002", 1101), ("w006", 1102)])
+def test_feed_forward_half_oracle(tag, seed):
+    """x + 0.5 * ConformerFeedForward(x): the feed-forward oracle against the reference, fp32 within 1e-5 and the
+    bf16 ("reference" rounding) form within the bf16 gates."""
+    from oracle import feed_forward as FF
+    g = _load(f"ff_half_b2t37_{tag}.npz")
+    p = synth.make_ff_params(seed, w_std=0.02 if tag == "w002" else 0.06)
+    x = synth.make_activations(seed + 500, (2, 37, synth.D_MODEL))
+    y32 = FF.feed_forward_half(x, FF.prepare_ff_fp32(p), mode="fp32")
+    assert np.max(np.abs(y32 - g["fp32"])) <= TOL_FP32 * max(1.0, float(np.abs(g["fp32"]).max()))
+    yb = FF.feed_forward_half(O.bf16_round(x), FF.prepare_ff_bf16(p), mode="reference")
+    ref = O.from_bf16_bits(g["bf16"])
+    assert_bf16_close(yb, ref, f"ff half {tag} oracle vs reference")
+    assert O.rel_l2(yb, ref) <= 1e-3
