@@ -73,3 +73,36 @@ def test_ops_refuse_cpu_tensors():
 
 def test_build_is_current():
     assert not build.needs_build()
+
+
+def test_validation_of_fused_and_block_entry_points():
+    """The fused up_conv + depthwise kernel, the LayerNorm fold, the feed-forward half and the int8 widening
+    reject bad shapes and pointers before any CUDA work; empty problems succeed."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    # fused kernel: T must sit on the 128-frame grid, N on the 256-column tile
+    assert L.gsn_gemm1_glu_dwconv_bf16(p, p, None, p, p, p, p, 2, 100, 1024, 4096, None, None) == 2
+    assert "T % 128" in _lib.last_error()
+    assert L.gsn_gemm1_glu_dwconv_bf16(p, p, None, p, p, p, p, 2, 128, 1024, 4000, None, None) == 2
+    assert L.gsn_gemm1_glu_dwconv_bf16(None, None, None, None, None, None, None, 0, 128, 1024, 4096, None,
+                                       None) == 0
+    assert L.gsn_gemm1_glu_dwconv_bf16(None, p, None, p, p, p, p, 2, 128, 1024, 4096, None, None) == 1
+    # LayerNorm fold and statistics
+    assert L.gsn_fold_layernorm_bf16(p, p, p, p, p, p, p, 4096, 1000, None) == 2
+    assert "multiple of 256" in _lib.last_error()
+    assert L.gsn_layernorm_stats_bf16(p, 768, p, 4, 768, 1e-5, None, 0, None) == 2
+    assert L.gsn_gemm1_lnfold_glu_dwconv_bf16(p, p, p, p, None, p, p, p, 2, 128, 1024, 4096, None, None) == 1
+    assert L.gsn_conv_module_lnfold_bf16(*([p] * 8), None, 1, p, 2, 100, 1024, 2048, 1e-5, p, 1 << 30, None) == 2
+    assert "multiple of 128" in _lib.last_error()
+    # feed-forward half
+    assert L.gsn_ff_half_workspace_bytes(2, 128, 1024, 4096) == 2 * 128 * (1024 * 2 + 4096 * 2)
+    assert L.gsn_ff_half_bf16(*([p] * 7), None, p, 2, 128, 1024, 4000, 1e-5, p, 1 << 30, None) == 2
+    rc = L.gsn_ff_half_bf16(*([p] * 7), None, p, 2, 128, 1024, 4096, 1e-5, p, 100, None)
+    assert rc == 5 and "workspace" in _lib.last_error()
+    assert L.gsn_gemm_silu_bf16(p, p, p, p, 128, 1000, 4096, None, 0, None) == 2
+    assert L.gsn_gemm_residual_scaled_bf16(p, p, p, None, 0, p, 1024, 128, 4096, 1000, 0.5, None, 0, None) == 2
+    # int8 widening: sizes must be multiples of 16
+    assert L.gsn_widen_i8_bf16(p, p, 17, None, None, 0, None) == 1
+    assert L.gsn_widen_i8_bf16(None, None, 0, None, None, 0, None) == 0
+    assert L.gsn_conv_module_i8w_workspace_bytes(2, 128, 1024, 2048) == (
+        L.gsn_conv_module_workspace_bytes(2, 128, 1024, 2048) + 2 * 2048 * 1024 * 2 + 1024 * 2048 * 2)
