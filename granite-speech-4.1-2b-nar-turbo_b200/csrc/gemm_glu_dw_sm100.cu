@@ -25,6 +25,8 @@
 //               computes the final 7 frames with zero GLU rows on the right.
 // Lengths: GLU rows of frames t >= len[b] are zero, depthwise frames in [len, roundup128(len)) are written as
 // zero (the residual GEMM reads whole 128-row tiles), frames beyond are never touched.
+#include <type_traits>
+
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
@@ -109,7 +111,12 @@ __device__ __forceinline__ pk2 pk_fma(pk2 a, pk2 b, pk2 c) {
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync %0, %1;" ::"n"(kEpiBar), "n"(EPI_THREADS) : "memory"); }
 
 // The unit sequence, identical in every role: utterance rank r (most tiles first) x channel block, dealt to the
-// CTAs in snake order over the passes of gridDim.x units.
+// CTAs in snake order over the passes of gridDim.x units.  When the last pass holds at most half a grid of units,
+// each of them is split into two halves of 64 channels (N=128 MMAs) on two CTAs, so that pass ends in half the
+// time: whole units make the busiest CTA take one unit more than most others.
+struct Unit {
+  int b, n_blk, len, half;    // half: -1 for the whole 128-channel block, else 0 / 1 (channels 64 * half + [0, 64))
+};
 struct Units {
   const Smem* s;
   const int* lengths;
@@ -119,15 +126,26 @@ struct Units {
     if (sorted) return s->lens[b];
     return lengths ? min(max(__ldg(lengths + b), 0), T) : T;
   }
-  // step-th unit of this CTA: false when there is none; else the utterance, channel block and length
-  __device__ bool get(int step, int& b, int& n_blk, int& len) const {
+  // step-th unit of this CTA: false when there is none
+  __device__ bool get(int step, Unit& u) const {
     const int G = gridDim.x, j = blockIdx.x;
-    const int i = step * G + ((step & 1) ? (G - 1 - j) : j);
-    if (i >= total) return false;
+    const int passes = total / G, rem = total - passes * G;
+    const bool split = rem > 0 && 2 * rem <= G;
+    const int pos = (step & 1) ? (G - 1 - j) : j;
+    int i;
+    u.half = -1;
+    if (step < passes || !split) {
+      i = step * G + pos;
+      if (i >= total) return false;
+    } else {
+      if (step > passes || pos >= 2 * rem) return false;
+      i = passes * G + (pos >> 1);
+      u.half = pos & 1;
+    }
     const int r = i / nb;
-    n_blk = i - r * nb;
-    b = sorted ? s->order[r] : r;
-    len = len_of(b);
+    u.n_blk = i - r * nb;
+    u.b = sorted ? s->order[r] : r;
+    u.len = len_of(u.b);
     return true;
   }
 };
@@ -137,8 +155,9 @@ struct Units {
 template <bool SCALED, bool LNF>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                       const __grid_constant__ CUtensorMap tmD, Params p) {
+                       const __grid_constant__ CUtensorMap tmW64, const __grid_constant__ CUtensorMap tmD, Params p) {
   constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
+  constexpr uint32_t IDESC_HALF = make_idesc_bf16_f32(BM, BN / 2);
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -164,6 +183,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmW64);
     tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
@@ -201,11 +221,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t phase = 0;
     int issued = 0;
     bool ok = true;
-    int b, n_blk, len;
-    for (int step = 0; ok && units.get(step, b, n_blk, len); ++step) {
-      const int nt = (len + BM - 1) / BM;
+    Unit u;
+    for (int step = 0; ok && units.get(step, u); ++step) {
+      const int nt = (u.len + BM - 1) / BM;
       for (int k = 0; k < nt && ok; ++k) {
-        const int row0 = b * p.T + k * BM;
+        const int row0 = u.b * p.T + k * BM;
         for (int kb = 0; kb < num_kb; ++kb) {
           bool got = mbar_wait_bounded(&s.empty[stage], phase ^ 1u, abort_flag, kStatusTimeoutProducer);
           got = __shfl_sync(0xffffffffu, got, 0);
@@ -214,9 +234,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           if (lane == 0) {
-            mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES);
-            tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, row0);
-            tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
+            if (u.half < 0) {
+              mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES);
+              tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, row0);
+              tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * BK, u.n_blk * BN, pol_w);
+            } else {
+              // half unit: W rows of its 64 value channels, then of their 64 gate channels (8-row swizzle atoms,
+              // so the two 64-row boxes form one 128-row tile)
+              const int w0 = u.n_blk * BN + 64 * u.half;
+              mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES / 2);
+              tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, row0);
+              tma_load_2d_hint(s.b[stage], &tmW64, &s.full[stage], kb * BK, w0, pol_w);
+              tma_load_2d_hint(s.b[stage] + B_BYTES / 4, &tmW64, &s.full[stage], kb * BK, w0 + CH, pol_w);
+            }
           }
           __syncwarp();
           ++issued;
@@ -241,9 +271,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t phase = 0;
     bool ok = true;
     int local = 0;
-    int b, n_blk, len;
-    for (int step = 0; ok && units.get(step, b, n_blk, len); ++step) {
-      const int nt = (len + BM - 1) / BM;
+    Unit u;
+    for (int step = 0; ok && units.get(step, u); ++step) {
+      const int nt = (u.len + BM - 1) / BM;
+      const uint32_t idesc = u.half < 0 ? IDESC : IDESC_HALF;
       for (int k = 0; k < nt && ok; ++k) {
         const int acc = local & 1;
         const uint32_t use_par = (uint32_t)((local >> 1) & 1);
@@ -269,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.b[stage]));
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk)
-              umma_f16(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), IDESC,
+              umma_f16(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
                        (kb | kk) != 0 ? 1u : 0u);
             umma_commit(&s.empty[stage]);
           }
@@ -294,33 +325,41 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int e = warp - 2;             // 0..7
     const int et = threadIdx.x - 64;    // 0..255
     const int q = warp & 3;             // TMEM lane quarter of this warp
-    const int half = e >> 2;            // GLU channels [64 * half, 64 * half + 64)
+    const int grp = e >> 2;             // whole unit: GLU channels [64 grp, 64 grp + 64); half unit: [32 grp, +32)
     bool ok = true;
     int local = 0;
-    int b, n_blk, len;
-    for (int step = 0; units.get(step, b, n_blk, len); ++step) {
+    Unit u;
+    for (int step = 0; units.get(step, u); ++step) {
+      const int b = u.b, len = u.len;
       const int nt = (len + BM - 1) / BM;
       if (nt == 0) continue;
-      const int c0 = n_blk * CH;                         // first GLU / depthwise channel of the unit
+      const bool whole = u.half < 0;
+      const int nch = whole ? CH : CH / 2;               // channels of the unit
+      const int gate_col = whole ? CH : CH / 2;          // accumulator column of the first gate channel
+      const int c0 = u.n_blk * CH + (whole ? 0 : (CH / 2) * u.half);   // first GLU / depthwise channel
+      // depthwise lanes: a whole unit gives each lane 4 of its 128 channels; a half unit gives lanes l and l + 16
+      // the same 4 of its 64 channels, for the first and the second 8 of the warp's 16 frames
+      const int lch = whole ? lane : (lane & 15);
       const int store_end = min(nt * BM, p.T);           // frames written: [0, len) values, [len, store_end) zero
-      __nv_bfloat16* drow = p.d + (int64_t)b * p.T * inner + c0 + lane * 4;
+      __nv_bfloat16* drow = p.d + (int64_t)b * p.T * inner + c0 + lch * 4;
 
-      // unit setup: bias / scale columns, zero left halo (frames -14..-1), this lane's depthwise weights
+      // unit setup: bias / scale columns (value columns, then gate columns, as in the accumulator), zero left
+      // halo (frames -14..-1), this lane's depthwise weights
       epi_bar();
-      {
-        const float bv = __ldg(p.bias + n_blk * BN + et);
-        s.vb[et] = 0.5f * bv;
-        s.vs[et] = SCALED ? 0.5f * __ldg(p.col_scale + n_blk * BN + et) : 0.5f;
-        if (LNF) s.vc[et] = s.vs[et] * __ldg(p.colsum + n_blk * BN + et);
-        if (et < 2 * HALO * 16) {
-          const int r = et >> 4, c = et & 15;
-          *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-        }
+      if (et < 2 * nch) {
+        const int col = u.n_blk * BN + (whole ? et : (et < nch ? nch * u.half + et : CH + nch * u.half + et - nch));
+        s.vb[et] = 0.5f * __ldg(p.bias + col);
+        s.vs[et] = SCALED ? 0.5f * __ldg(p.col_scale + col) : 0.5f;
+        if (LNF) s.vc[et] = s.vs[et] * __ldg(p.colsum + col);
+      }
+      if (et < 2 * HALO * 16) {
+        const int r = et >> 4, c = et & 15;
+        *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) = make_uint4(0u, 0u, 0u, 0u);
       }
       pk2 wr[KW][2];
       pk2 wb[2];
       {
-        const __nv_bfloat16* wp = p.dw_w + (int64_t)(c0 + lane * 4) * KW;
+        const __nv_bfloat16* wp = p.dw_w + (int64_t)(c0 + lch * 4) * KW;
 #pragma unroll
         for (int j = 0; j < KW; ++j)
 #pragma unroll
@@ -329,8 +368,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 0.5f * __bfloat162float(wp[(2 * qq + 1) * KW + j]));
 #pragma unroll
         for (int qq = 0; qq < 2; ++qq)
-          wb[qq] = pk_make(0.5f * __bfloat162float(p.dw_b[c0 + lane * 4 + 2 * qq]),
-                           0.5f * __bfloat162float(p.dw_b[c0 + lane * 4 + 2 * qq + 1]));
+          wb[qq] = pk_make(0.5f * __bfloat162float(p.dw_b[c0 + lch * 4 + 2 * qq]),
+                           0.5f * __bfloat162float(p.dw_b[c0 + lch * 4 + 2 * qq + 1]));
       }
       epi_bar();
 
@@ -359,14 +398,14 @@ __global__ void __launch_bounds__(THREADS, 1)
               rs = st.x;
               rsm = st.y;
             }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int cb = half * 64 + u * 32;         // first of this sub-tile's 32 GLU channels
+            const int nsub = whole ? 2 : 1;              // 32-channel sub-tiles of this warp
+            for (int uu = 0; uu < nsub; ++uu) {
+              const int cb = whole ? grp * 64 + uu * 32 : grp * 32;   // first of the sub-tile's 32 GLU channels
               uint32_t va[2][16], vg[2][16];
               tmem_ld16(t_row + (uint32_t)cb, va[0]);
               tmem_ld16(t_row + (uint32_t)(cb + 16), va[1]);
-              tmem_ld16(t_row + (uint32_t)(CH + cb), vg[0]);
-              tmem_ld16(t_row + (uint32_t)(CH + cb + 16), vg[1]);
+              tmem_ld16(t_row + (uint32_t)(gate_col + cb), vg[0]);
+              tmem_ld16(t_row + (uint32_t)(gate_col + cb + 16), vg[1]);
               tmem_wait_ld_dep(va[0], va[1]);
               tmem_wait_ld_dep(vg[0], vg[1]);
               uint32_t o[16];
@@ -377,14 +416,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int z = 0; z < 2; ++z) {
                   const int kk = c + z;
                   float a, g;
+                  const int ga = gate_col + cb + kk;
                   if (LNF) {
                     a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rs * s.vs[cb + kk],
                              fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
-                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rs * s.vs[CH + cb + kk],
-                             fmaf(-rsm, s.vc[CH + cb + kk], s.vb[CH + cb + kk]));
+                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rs * s.vs[ga], fmaf(-rsm, s.vc[ga], s.vb[ga]));
                   } else {
                     a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
-                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[CH + cb + kk], s.vb[CH + cb + kk]);
+                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[ga], s.vb[ga]);
                   }
                   h2[z] = fmaf(a, tanh_approx(g), a);
                 }
@@ -408,18 +447,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         epi_bar();
 
         // (2) depthwise + SiLU: output frame t0 - 7 + i reads window rows i .. i + 14.  Warp e owns i in
-        // [16e, 16e + 16); the flush only needs i in [0, 7) (warp 0).
+        // [16e, 16e + 16) (a half unit: 8 frames per half-warp); the flush only needs i in [0, 7).
         const int i_hi = flush ? HALO : BM;
-        if (ok && e * FPW < i_hi) {
-          const int i0 = e * FPW;
-          const uint8_t* xb = s.win + i0 * WPITCH + lane * 8;
-          pk2 acc[FPW][2];
+        auto dw_rows = [&](auto nf_tag) {
+          constexpr int NF = decltype(nf_tag)::value;
+          const int i0 = e * FPW + (NF == FPW ? 0 : (lane >> 4) * NF);
+          if (i0 >= i_hi) return;
+          const uint8_t* xb = s.win + i0 * WPITCH + lch * 8;
+          pk2 acc[NF][2];
 #pragma unroll
-          for (int r = 0; r < FPW + 2 * HALO; ++r) {
+          for (int r = 0; r < NF + 2 * HALO; ++r) {
             const uint2 v = *reinterpret_cast<const uint2*>(xb + r * WPITCH);
             const pk2 xv[2] = {pk_from_bf16x2(v.x), pk_from_bf16x2(v.y)};
 #pragma unroll
-            for (int f = 0; f < FPW; ++f) {
+            for (int f = 0; f < NF; ++f) {
               const int j = r - f;
               if (j >= 0 && j < KW) {
 #pragma unroll
@@ -427,15 +468,15 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
-          const int tf = t0 - HALO + i0;                 // the warp's first output frame
-          const bool boxed = !flush && tf >= 0 && tf + FPW <= store_end;
+          const int tf = t0 - HALO + i0;                 // the lane's first output frame
+          const bool boxed = NF == FPW && !flush && tf >= 0 && tf + FPW <= store_end;   // warp-uniform
           uint8_t* ob = s.out[e];
           if (boxed) {
             if (lane == 0) bulk_wait_group_read<0>();  // the previous tile's box has been read by its store
             __syncwarp();
           }
 #pragma unroll
-          for (int f = 0; f < FPW; ++f) {
+          for (int f = 0; f < NF; ++f) {
             const int t = tf + f;
             uint32_t o[2];
 #pragma unroll
@@ -458,6 +499,12 @@ __global__ void __launch_bounds__(THREADS, 1)
               bulk_commit_group();
             }
           }
+        };
+        if (ok && e * FPW < i_hi) {
+          if (whole)
+            dw_rows(std::integral_constant<int, FPW>{});
+          else
+            dw_rows(std::integral_constant<int, FPW / 2>{});
         }
         epi_bar();
         if (!flush) {
@@ -499,11 +546,16 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
+  CUtensorMap tmW64;
   {
     const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
     const uint64_t strides[1] = {(uint64_t)a.K * 2};
     const uint32_t box[2] = {G::BK, G::BN};
     if (int rc = encode_tmap(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    const uint32_t box64[2] = {G::BK, G::BN / 4};
+    if (int rc = encode_tmap(&tmW64, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w, dims, strides, box64,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
@@ -539,7 +591,7 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   const int sms = device_sm_count();
   const int grid = (int)(units < sms ? units : sms);
   if (grid <= 0) return 0;
-  kern<<<grid, G::THREADS, smem, stream>>>(tmA, tmW, tmD, p);
+  kern<<<grid, G::THREADS, smem, stream>>>(tmA, tmW, tmW64, tmD, p);
   return (int)cudaGetLastError();
 }
 

@@ -59,6 +59,8 @@ def _check(d, ref, B, T, lens):
     (3, 896, None),
     (6, 1536, [1536, 641, 640, 639, 64, 1500]),
     (7, 1152, [1152, 1025, 1024, 769, 768, 385, 384]),
+    (10, 384, None),                                     # 160 units on 148 SMs: the last 12 split in halves
+    (12, 640, [640, 639, 600, 513, 512, 300, 257, 256, 129, 128, 1, 0]),
 ])
 def test_fused_equals_two_kernels(B, T, lens):
     p = _prep(40 + T)
