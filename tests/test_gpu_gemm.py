@@ -62,6 +62,44 @@ def test_gemm2_strided_rows():
     assert_bf16_close(out, ref, "gemm2 strided")
 
 
+@pytest.mark.parametrize("epilogue,extra_rows", [("residual", 0), ("residual", 50), ("silu", 0), ("silu", 77)])
+def test_gemm_result_independent_of_grid(epilogue, extra_rows):
+    """A grid with more tiles than SMs (a partial last wave) gives, bit for bit, the same rows as calls small
+    enough to run one tile per CTA: a tile's result does not depend on which CTA computes it or when."""
+    from granite_conv_b200 import _lib
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    K, N = (2048, 1024) if epilogue == "residual" else (1024, 4096)
+    per_m = N // 256
+    m_blocks = sms // per_m + max(1, 12 // per_m)
+    M = m_blocks * 128 - (128 - extra_rows if extra_rows else 0)
+    assert 0 < (-(-M // 128)) * per_m - sms <= sms // 2
+    g = torch.Generator(device=DEV).manual_seed(31 + extra_rows)
+    a = torch.randn((M, K), generator=g, device=DEV).bfloat16()
+    w = (torch.randn((N, K), generator=g, device=DEV) * 0.03).bfloat16()
+    b = torch.randn((N,), generator=g, device=DEV) * 0.1
+    r = torch.randn((M, N), generator=g, device=DEV).bfloat16()
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run(rows):
+        a_, r_ = a[rows], r[rows]
+        m = a_.shape[0]
+        out = torch.empty((m, N), dtype=torch.bfloat16, device=DEV)
+        if epilogue == "residual":
+            _lib.call("gsn_gemm2_residual_bf16", a_.data_ptr(), w.data_ptr(), b.data_ptr(), r_.data_ptr(), N,
+                      out.data_ptr(), N, m, K, N, None, 0, stream)
+        else:
+            _lib.call("gsn_gemm_silu_bf16", a_.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(), m, K, N,
+                      None, 0, stream)
+        return out
+
+    whole = run(slice(0, M))
+    step = 8 * 128
+    parts = torch.cat([run(slice(i, min(M, i + step))) for i in range(0, M, step)])
+    torch.cuda.synchronize()
+    assert torch.equal(whole, parts)
+    assert _lib.device_status(stream) == 0
+
+
 @pytest.mark.parametrize("M", [128, 333])
 def test_gemm_int8_weights(M):
     K1, N1 = 1024, 4096

@@ -189,3 +189,18 @@ def test_torch_compile_fullgraph():
     y0, z0 = f(x, lens)
     assert torch.equal(y0, y1) and torch.equal(z0, z1)
     assert z1.stride() == z0.stride()
+
+
+@pytest.mark.parametrize("d_model,d_inner,ln_fold", [(512, 1024, False), (512, 1024, True), (2048, 4096, True),
+                                                     (256, 256, False)])
+def test_module_other_widths(d_model, d_inner, ln_fold):
+    """Widths other than the Granite encoder's: the fused kernel, the LayerNorm fold and the residual GEMM are
+    generic in D (a LayerNorm width) and inner (a multiple of 128)."""
+    params = synth.make_params(600 + d_model, d_model=d_model, d_inner=d_inner, w_std=0.05)
+    p = prepare_from_params(params, device=DEV, ln_fold=ln_fold)
+    B, T = 3, 256
+    x = O.bf16_round(synth.make_activations(601 + d_model, (B, T, d_model)))
+    lens = np.array([256, 131, 40], dtype=np.int32)
+    y = ops.run_conv_module(_t(x), p, lengths=torch.from_numpy(lens).to(DEV))
+    ref = O.conv_module(x, O.prepare_bf16(params), lengths=lens, mode="fused")
+    assert_bf16_close(y, ref, f"module D={d_model} inner={d_inner} ln_fold={ln_fold}")
