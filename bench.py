@@ -1,6 +1,7 @@
 """Benchmark of the B200 Conformer conv-module kernels.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload stack|module|module_i8|dw] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload stack|module|module_i8|dw|ff|attn]
+                    [--impl ours|reference]
 
 Default workload ("stack"): 16 conv-module layers (independent seeds) over 512 synthetic utterances per rank with
 lognormal lengths (median 600 frames, sigma 0.5, clipped to [64, 1536]), sorted by length, logical batches of 128
@@ -9,7 +10,9 @@ Each rank owns its own 512 utterances (weak scaling, no collective in the loop);
 of all ranks / the slowest rank's time.  Inputs are resident in HBM and larger than L2 (~0.7 GB per step).
 
 Other workloads (single-GPU measurements): "module" = one conv module on one B=48 chunk (lognormal lengths, T on
-the 128 grid), "module_i8" = the same with int8 weights, "dw" = the depthwise kernel alone on [48, 1024, 2048].
+the 128 grid), "module_i8" = the same with int8 weights, "dw" = the depthwise kernel alone on [48, 1024, 2048],
+"ff" = one feed-forward half on the same chunk, "attn" = one attention step (block-local, Shaw relative
+positions) on the same chunk.
 
 ``--impl reference`` times the CPU oracle (numpy restatement of the reference eager module) on the host cores on a
 bounded sample of the same workload and prints the same JSON line with "impl": "reference".
@@ -38,6 +41,11 @@ D, I = synth.D_MODEL, synth.D_INNER
 GEMM1_FLOP_PER_FRAME = 2 * D * 2 * I          # 8.389 MFLOP
 GEMM2_FLOP_PER_FRAME = 2 * I * D              # 4.194 MFLOP
 FF_FLOP_PER_FRAME = 2 * D * 4 * D             # 8.389 MFLOP per feed-forward GEMM
+HEADS, DIM_HEAD, CONTEXT = synth.NUM_HEADS, synth.DIM_HEAD, synth.CONTEXT
+QKV_FLOP_PER_FRAME = 2 * D * 3 * HEADS * DIM_HEAD       # 6.291 MFLOP
+OUT_FLOP_PER_FRAME = 2 * HEADS * DIM_HEAD * D           # 2.097 MFLOP
+# attention: per valid query frame, head and valid key of its block: q.k, q.rel[i - j] and p.v (2 x 128 each)
+ATTN_FLOP_PER_QUERY_KEY = 3 * 2 * DIM_HEAD * HEADS      # 6144
 # DRAM bytes (read + write) of the fused up_conv + GLU + depthwise kernel per row of the 128-row tiles it computes,
 # from one ncu capture of a B=48, T=1536 chunk (profiles/gemm_glu_dw_b48_t1536.md: 73.0 + 83.1 MB over 31,104
 # rows); the traffic of a launch scales with the rows it computes.
@@ -129,7 +137,7 @@ def _workload_plan(rank: int, workload: str):
         lens = synth.sample_lengths(1005 + 7919 * rank, N_UTTS)
         return dispatch.plan_chunks(lens, exec_batch=dispatch.EXEC_BATCH, logical_batch=dispatch.LOGICAL_BATCH,
                                     frame_grid=dispatch.FRAME_GRID)
-    if workload in ("module", "module_i8", "ff"):
+    if workload in ("module", "module_i8", "ff", "attn"):
         lens = synth.sample_lengths(1003 + 7919 * rank, 48)
         T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
         return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
@@ -147,6 +155,7 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
     """frames/s (valid frames x layers per second) of the numpy oracle (float32, all host threads through BLAS) on a
     bounded sample of the workload: the shortest chunks of the plan, one layer each, until budget_s is spent."""
     from oracle import conv_module as O
+    from oracle import attention as ATO
     from oracle import feed_forward as FFO
     chunks = _workload_plan(rank, workload)
     if workload == "dw":
@@ -154,6 +163,8 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
         wb, bb = O.bf16_round(w), O.bf16_round(b)
     elif workload == "ff":
         ffprep = FFO.prepare_ff_fp32(synth.make_ff_params(1006))
+    elif workload == "attn":
+        atprep = ATO.prepare_attn_fp32(synth.make_attn_params(1007))
     else:
         params = synth.make_params(1005)
         prep = O.prepare_fp32(params)
@@ -172,6 +183,8 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
             O.dwconv_silu(x, wb, bb, lengths=lens, round_out=False)
         elif workload == "ff":
             FFO.feed_forward_half(x, ffprep, lengths=lens, mode="fp32", dtype=np.float32)
+        elif workload == "attn":
+            ATO.attention_block(x, atprep, lengths=lens, mode="fp32", dtype=np.float32)
         else:
             O.conv_module(x, prep, lengths=lens, mode="fp32", dtype=np.float32)
         frames += int(lens.sum())
@@ -220,7 +233,10 @@ def _config(args, world):
         "module_i8": "one conv module with int8 per-channel weights, B=48 chunk, lognormal lengths, length mask",
         "dw": "depthwise k15 + bias + SiLU alone, bf16 [48, 1024, 2048] channels-last, all frames valid",
         "ff": "one feed-forward half of the Conformer block (LN, 1024->4096 GEMM+SiLU, 4096->1024 GEMM + 0.5x "
-              "residual), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask"}[w],
+              "residual), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
+        "attn": "one attention step of the Conformer block (LN, 1024->3072 q|k|v GEMM, block-local attention over "
+                "200-frame blocks with Shaw relative positions, 8 heads x 128, 1024->1024 GEMM + residual), B=48 "
+                "chunk, lognormal lengths, T on the 128-frame grid, length mask"}[w],
         "d_model": D, "d_inner": I, "kernel": 15, "layers": _layers_for(w),
         "utterances_per_rank": N_UTTS if w == "stack" else 48, "exec_batch": dispatch.EXEC_BATCH,
         "frame_grid": dispatch.FRAME_GRID, "parallelism": f"dp{world} (independent shards, no collective)",
@@ -268,6 +284,10 @@ def run_ours(args):
         from granite_conv_b200.weights import prepare_ff_from_params
         layers = [prepare_ff_from_params(synth.make_ff_params(1006), device=dev)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+    elif workload == "attn":
+        from granite_conv_b200.weights import prepare_attn_from_params
+        layers = [prepare_attn_from_params(synth.make_attn_params(1007), device=dev)]
+        xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     else:
         # bf16: the LayerNorm folded into the up_conv GEMM (the module op's path for T on the 128 grid)
         layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8, ln_fold=not int8)
@@ -278,6 +298,8 @@ def run_ours(args):
     ws_bytes = int(L.gsn_conv_module_workspace_bytes(1, max_m, D, I))
     if workload == "ff":
         ws_bytes = max(ws_bytes, int(L.gsn_ff_half_workspace_bytes(1, max_m, D, 4 * D)))
+    if workload == "attn":
+        ws_bytes = max(ws_bytes, int(L.gsn_attention_block_workspace_bytes(1, max_m, D, HEADS, DIM_HEAD)))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     h_buf = ws                                                         # [M, I] GLU output
     t_off = ((max_m * I * 2 + 255) // 256) * 256
@@ -362,6 +384,36 @@ def run_ours(args):
             ev[3].record(stream)
             layer_events.append((ev, c))
 
+    def attn_kernels(x, out, c, p, lens, record):
+        """The four launches of gsn_attention_block_bf16: LayerNorm (every frame), the q|k|v GEMM, the attention,
+        to_out + residual."""
+        M, T = c.padded_frames, c.T
+        inner = HEADS * DIM_HEAD
+        tp = ws.data_ptr()                                          # LayerNorm output [M, D]
+        qp = tp + ((M * D * 2 + 255) // 256) * 256                  # q | k | v [M, 3 inner]
+        cp = qp + ((M * 3 * inner * 2 + 255) // 256) * 256          # context [M, inner]
+        lp = lens.data_ptr()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        if record:
+            ev[0].record(stream)
+        _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
+                                        p.ln_eps, None, T, sp), "layernorm")
+        if record:
+            ev[1].record(stream)
+        _lib.check(L.gsn_gemm2_residual_bf16(tp, p.w_qkv.data_ptr(), p.b_qkv.data_ptr(), None, 0, qp, 3 * inner, M,
+                                             D, 3 * inner, lp, T, sp), "qkv")
+        if record:
+            ev[2].record(stream)
+        _lib.check(L.gsn_attention_core_bf16(qp, 3 * inner, p.rel.data_ptr(), p.rel.shape[0], cp, inner, lp, c.B, T,
+                                             HEADS, DIM_HEAD, CONTEXT, p.max_pos, DIM_HEAD ** -0.5, sp), "attention")
+        if record:
+            ev[3].record(stream)
+        _lib.check(L.gsn_gemm2_residual_bf16(cp, p.w_out.data_ptr(), p.b_out.data_ptr(), x.data_ptr(), D,
+                                             out.data_ptr(), D, M, inner, D, lp, T, sp), "to_out")
+        if record:
+            ev[4].record(stream)
+            layer_events.append((ev, c))
+
     dw_events = []
 
     def step(record=False):
@@ -386,6 +438,9 @@ def run_ours(args):
                 if workload == "ff":
                     ff_kernels(src, dst, c, p, lens_dev[ci], record)
                     n += 3
+                elif workload == "attn":
+                    attn_kernels(src, dst, c, p, lens_dev[ci], record)
+                    n += 4
                 else:
                     layer_kernels(src, dst, c, p, lens_dev[ci], record)
                     n += 4 if int8 else 3
@@ -444,6 +499,17 @@ def run_ours(args):
                 "traffic": None, "per_launch_ms": g1["ms_per_launch"], "algorithmic_flop_per_frame": FF_FLOP_PER_FRAME,
                 "frames_counted": "rows of the 128-row tiles holding valid frames",
                 "peak_source": f"bf16_tflops_sustained of {peaks['source']}", "kernels": kernels}
+    elif workload == "attn":
+        kernels = _attn_breakdown(layer_events, peaks)
+        top = max(kernels, key=lambda n: kernels[n]["share"])
+        k = kernels[top]
+        roof = {"kernel": top, "bound": "hbm" if k["unit"] == "GB/s" else "tensor", "achieved": k["achieved"],
+                "peak": k["peak"], "unit": k["unit"], "frac": k["frac"], "traffic": None,
+                "per_launch_ms": k["ms_per_launch"],
+                "work": "q|k|v and to_out GEMMs: 6.291 / 2.097 MFLOP per row of the 128-row tiles holding valid "
+                        "frames; attention: 6144 FLOP per (valid query, valid key of its 200-frame block) "
+                        "(q.k, q.rel[i-j], p.v over 8 heads x 128); LayerNorm: 4 KB per frame",
+                "peak_source": f"bf16_tflops_sustained / hbm_gbs of {peaks['source']}", "kernels": kernels}
     else:
         kernels = _kernel_breakdown(layer_events, peaks, widen_events, ln_name="layernorm" if int8 else "ln_stats")
         g1 = kernels["gemm1_glu_dw"]
@@ -462,7 +528,8 @@ def run_ours(args):
     # ---- end to end through the public op with pinned host buffers
     e2e = None
     if workload != "dw" and not args.no_e2e:
-        e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff")
+        e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff",
+                   attn=workload == "attn")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -513,6 +580,43 @@ def _ff_breakdown(layer_events, peaks):
     return out
 
 
+def _attn_query_keys(c):
+    """Sum over valid query frames of the valid keys in their 200-frame block."""
+    n = 0
+    for L in c.lengths:
+        L = int(L)
+        for m0 in range(0, L, CONTEXT):
+            k = min(CONTEXT, L - m0)
+            n += k * k
+    return n
+
+
+def _attn_breakdown(layer_events, peaks):
+    """Per-kernel launch time and rate of the attention step: LayerNorm over every frame (2 x 2 KB), the q|k|v and
+    to_out GEMMs (rows of the 128-row tiles holding valid frames), the attention (ATTN_FLOP_PER_QUERY_KEY per valid
+    query-key pair of a block)."""
+    names = ("layernorm", "qkv_proj", "attention", "out_proj")
+    tot = {n: 0.0 for n in names}
+    work = {n: 0.0 for n in names}
+    for ev, c in layer_events:
+        for k, n in enumerate(names):
+            tot[n] += ev[k].elapsed_time(ev[k + 1])
+        rows = _tile_rows(c)
+        work["layernorm"] += c.padded_frames * 2 * D * 2
+        work["qkv_proj"] += rows * QKV_FLOP_PER_FRAME
+        work["attention"] += _attn_query_keys(c) * ATTN_FLOP_PER_QUERY_KEY
+        work["out_proj"] += rows * OUT_FLOP_PER_FRAME
+    all_ms = sum(tot.values())
+    out = {}
+    for n in names:
+        tensor = n != "layernorm"
+        ach = work[n] / (tot[n] / 1e3) / (1e12 if tensor else 1e9)
+        pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
+        out[n] = {"ms_per_launch": tot[n] / len(layer_events), "share": tot[n] / all_ms, "achieved": ach,
+                  "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
+    return out
+
+
 def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm"):
     """Average launch time, share of the recorded kernel time and achieved rate of each kernel.
     Work per launch: LayerNorm reads and writes the valid frames (2 x 2 KB); the GEMMs compute the rows of the
@@ -546,7 +650,7 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
     return out
 
 
-def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False):
+def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn=False):
     """Same work through the public op (torch.ops.granite.conv_module per layer, or granite::feed_forward_half)
     with each chunk's input copied from pinned host memory and its output copied back inside the timed region."""
     import torch
@@ -555,6 +659,9 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False):
     if ff:
         def stack(x, lengths):
             return ops.run_feed_forward_half(x, layers[0], lengths)
+    elif attn:
+        def stack(x, lengths):
+            return ops.run_attention_block(x, layers[0], lengths)
     else:
         stack = ConvModuleStack(layers, int8=int8)
     g = torch.Generator().manual_seed(4242)
@@ -627,7 +734,8 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False):
         valid = float(v.item())
     return {"value": valid * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
-            "path": "torch.ops.granite.conv_module per layer, pinned host in/out on two copy streams"}
+            "path": ("torch.ops.granite." + ("feed_forward_half" if ff else "attention_block" if attn else
+                                              "conv_module per layer") + ", pinned host in/out on two copy streams")}
 
 
 def main():
@@ -636,7 +744,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff", "attn"], default="stack")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

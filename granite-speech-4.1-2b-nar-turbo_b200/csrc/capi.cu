@@ -419,6 +419,89 @@ int gsn_ff_half_bf16(const void* x, const void* ln_w, const void* ln_b, const vo
   return finish(launch_gemm(g2, kEpiResidual, st), name);
 }
 
+// ---- block-local Shaw attention ------------------------------------------------------------------------------
+static int check_attention(const char* name, int heads, int dim_head, int context, int max_pos_emb, int n_rel) {
+  if (dim_head != 128 || context != 200)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: dim_head=%d context=%d (only 128 and 200 are supported)", name, dim_head,
+                context);
+  if (heads <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: heads=%d", name, heads);
+  if (max_pos_emb < context || n_rel < max_pos_emb + context)
+    return fail(GSN_ERR_INVALID_ARG, "%s: max_pos_emb=%d n_rel=%d (need max_pos_emb >= %d, n_rel >= max_pos_emb + %d)",
+                name, max_pos_emb, n_rel, context, context);
+  return 0;
+}
+
+int gsn_attention_core_bf16(const void* qkv, int64_t ld_qkv, const void* rel_table, int n_rel, void* ctx,
+                            int64_t ld_ctx, const int32_t* lengths, int B, int T, int heads, int dim_head,
+                            int context, int max_pos_emb, float scale, gsn_stream_t stream) {
+  const char* name = "gsn_attention_core_bf16";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if (int rc = check_attention(name, heads, dim_head, context, max_pos_emb, n_rel)) return rc;
+  if ((int64_t)B * T == 0) return ok();
+  if (!qkv || !rel_table || !ctx) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  const int64_t inner = (int64_t)heads * dim_head;
+  if (ld_qkv < 3 * inner || ld_qkv % 8 || ld_ctx < inner || ld_ctx % 8)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: ld_qkv=%lld (>= %lld) and ld_ctx=%lld (>= %lld) must be multiples of 8", name,
+                (long long)ld_qkv, (long long)(3 * inner), (long long)ld_ctx, (long long)inner);
+  if (!aligned(qkv, 16) || !aligned(ctx, 16) || !aligned(rel_table, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: pointers must be 16-byte aligned", name);
+  AttnArgs a{(const __nv_bfloat16*)qkv, ld_qkv, (const __nv_bfloat16*)rel_table, n_rel, (__nv_bfloat16*)ctx,
+             ld_ctx, lengths, B, T, heads, max_pos_emb, scale};
+  return finish(launch_attention(a, (cudaStream_t)stream), name);
+}
+
+size_t gsn_attention_block_workspace_bytes(int B, int T, int D, int heads, int dim_head) {
+  if (B <= 0 || T <= 0 || D <= 0 || heads <= 0 || dim_head <= 0) return 0;
+  const size_t M = (size_t)B * (size_t)T, inner = (size_t)heads * (size_t)dim_head;
+  return align256(M * (size_t)D * 2) + align256(M * 3 * inner * 2) + align256(M * inner * 2);
+}
+
+int gsn_attention_block_bf16(const void* x, const void* ln_w, const void* ln_b, float ln_eps, const void* w_qkv,
+                             const float* b_qkv, const void* w_out, const float* b_out, const void* rel_table,
+                             int n_rel, const int32_t* lengths, void* out, int B, int T, int D, int heads,
+                             int dim_head, int context, int max_pos_emb, void* workspace, size_t workspace_bytes,
+                             gsn_stream_t stream) {
+  const char* name = "gsn_attention_block_bf16";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if (int rc = check_attention(name, heads, dim_head, context, max_pos_emb, n_rel)) return rc;
+  if ((int64_t)B * T == 0) return ok();
+  if (!x || !ln_w || !ln_b || !w_qkv || !b_qkv || !w_out || !b_out || !rel_table || !out)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  const int inner = heads * dim_head;
+  if (!ln_dim_ok(D) || (3 * inner) % 256 != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d heads=%d (D in {256..2048}, heads even)", name, D, heads);
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  const int M = B * T;
+  const size_t need = gsn_attention_block_workspace_bytes(B, T, D, heads, dim_head);
+  if (!workspace || workspace_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w_qkv, 16) || !aligned(w_out, 16) || !aligned(b_qkv, 16) ||
+      !aligned(b_out, 16) || !aligned(rel_table, 16) || !aligned(ln_w, 16) || !aligned(ln_b, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: tensors must be 16-byte aligned", name);
+  // workspace: t = LayerNorm output [M, D], qkv = t [Wq; Wkv]^T [M, 3 inner], ctx [M, inner]
+  __nv_bfloat16* t = (__nv_bfloat16*)workspace;
+  __nv_bfloat16* qkv = (__nv_bfloat16*)((char*)workspace + align256((size_t)M * D * 2));
+  __nv_bfloat16* ctx = (__nv_bfloat16*)((char*)qkv + align256((size_t)M * 3 * inner * 2));
+  const cudaStream_t st = (cudaStream_t)stream;
+  const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
+  // every frame is normalised (padding frames too), so that every q|k|v row the attention reads is finite
+  int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
+                            M, D, ln_eps, nullptr, T, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g1{t, w_qkv, b_qkv, nullptr, nullptr, qkv, (int64_t)3 * inner, 0, M, 3 * inner, D, 0, skip, T};
+  rc = launch_gemm(g1, kEpiResidual, st);
+  if (rc) return finish(rc, name);
+  AttnArgs a{qkv, (int64_t)3 * inner, (const __nv_bfloat16*)rel_table, n_rel, ctx, (int64_t)inner, lengths, B, T,
+             heads, max_pos_emb, 1.0f / sqrtf((float)dim_head)};
+  rc = launch_attention(a, st);
+  if (rc) return finish(rc, name);
+  // to_out + the block's residual: out = x + ctx W_out^T + b_out
+  GemmArgs g2{ctx, w_out, b_out, nullptr, (const __nv_bfloat16*)x, (__nv_bfloat16*)out, D, D, M, D, inner, 0, skip,
+              T};
+  return finish(launch_gemm(g2, kEpiResidual, st), name);
+}
+
 size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
   if (B <= 0 || T <= 0 || D <= 0 || inner <= 0) return 0;
   const size_t M = (size_t)B * (size_t)T;

@@ -4,4 +4,5 @@
 #include "dwconv.cu"
 #include "gemm_sm100.cu"
 #include "gemm_glu_dw_sm100.cu"
+#include "attention_sm100.cu"
 #include "capi.cu"

@@ -89,6 +89,24 @@ int launch_ln_stats(const __nv_bfloat16* x, int64_t ld_x, float2* stats, int M, 
 int launch_fold_ln(const __nv_bfloat16* w, const float* bias, const __nv_bfloat16* gamma, const __nv_bfloat16* beta,
                    __nv_bfloat16* w_out, float* bias_out, float* colsum, int N, int K, cudaStream_t stream);
 
+// ---- block-local Shaw attention core (attention_sm100.cu) ----------------------------------------------------
+// qkv: [B, T, ld_qkv] bf16 rows holding q | k | v (each H * 128 columns); rel: [n_rel, 128] bf16 (row
+// max_pos + i - j is the relative embedding of query i and key j); ctx: [B, T, ld_ctx] bf16, columns h * 128 + d.
+// Blocks of 200 frames, dim_head 128 (fixed by the kernel); ld_qkv and ld_ctx multiples of 8.
+struct AttnArgs {
+  const __nv_bfloat16* qkv;
+  int64_t ld_qkv;
+  const __nv_bfloat16* rel;
+  int n_rel;
+  __nv_bfloat16* ctx;
+  int64_t ld_ctx;
+  const int* lengths;            // [B] or null
+  int B, T, H;
+  int max_pos;
+  float scale;
+};
+int launch_attention(const AttnArgs& args, cudaStream_t stream);
+
 // ---- self-test of the bounded wait (capi.cu) ----------------------------------------------------------------
 int launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);
 

@@ -15,6 +15,8 @@ plus the ops of the whole module (new):
   (the LayerNorm folded into the up_conv GEMM; T % 128 == 0)
 * ``granite::feed_forward_half(x, ln_w, ln_b, w_up, b_up, w_down, b_down, lengths?, ln_eps)`` (x + 0.5 FF(x))
 * ``granite::layer_norm(x, weight, bias, eps)`` (the block's post LayerNorm)
+* ``granite::attention_block(x, ln_w, ln_b, w_qkv, b_qkv, w_out, b_out, rel, lengths?, heads, context, max_pos,
+  ln_eps)`` (x + ConformerAttention(x), block-local with Shaw relative positions)
 
 All are ``mutates_args=()``, CUDA-only, launch on ``torch.cuda.current_stream()`` (as ``jit.py:180-181``) and
 have ``register_fake`` implementations whose strides equal the real outputs', so ``torch.compile(fullgraph=True)``
@@ -253,6 +255,59 @@ def layer_norm_op(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps
 @layer_norm_op.register_fake
 def _(x, weight, bias, eps):
     return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+# ---- block-local attention with Shaw relative positions -----------------------------------------------------------
+@torch.library.custom_op("granite::attention_block", mutates_args=(), device_types="cuda")
+def attention_block(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w_qkv: torch.Tensor,
+                    b_qkv: torch.Tensor, w_out: torch.Tensor, b_out: torch.Tensor, rel: torch.Tensor,
+                    lengths: Optional[torch.Tensor], heads: int, context: int, max_pos: int,
+                    ln_eps: float) -> torch.Tensor:
+    """x + ConformerAttention(x) (conformer.py:61-131, :206) on bf16 x [B, T, D]."""
+    name = "granite::attention_block"
+    _require_cuda(name, x, ln_w, ln_b, w_qkv, b_qkv, w_out, b_out, rel, lengths)
+    if x.dim() != 3 or x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: x must be bf16 [B, T, D], got {x.dtype} {tuple(x.shape)}")
+    B, T, D = x.shape
+    dh = rel.shape[1]
+    xc = x.contiguous()
+    lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    out = torch.empty_like(xc)
+    nbytes = int(_lib.lib().gsn_attention_block_workspace_bytes(B, T, D, heads, dh)) if B * T > 0 else 0
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    _lib.call("gsn_attention_block_bf16", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), float(ln_eps),
+              w_qkv.data_ptr(), b_qkv.data_ptr(), w_out.data_ptr(), b_out.data_ptr(), rel.data_ptr(), rel.shape[0],
+              _ptr(lens), out.data_ptr(), B, T, D, heads, dh, context, max_pos, ws.data_ptr(), nbytes, _stream(xc))
+    return out
+
+
+@attention_block.register_fake
+def _(x, ln_w, ln_b, w_qkv, b_qkv, w_out, b_out, rel, lengths, heads, context, max_pos, ln_eps):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+def run_attention_block(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x + attention(x) with a :class:`~granite_conv_b200.weights.PreparedAttention`."""
+    return torch.ops.granite.attention_block(x, p.ln_w, p.ln_b, p.w_qkv, p.b_qkv, p.w_out, p.b_out, p.rel, lengths,
+                                             p.heads, p.context, p.max_pos, p.ln_eps)
+
+
+def attention_core(qkv: torch.Tensor, rel: torch.Tensor, heads: int, lengths: Optional[torch.Tensor] = None,
+                   context: int = 200, max_pos: int = 512, scale: Optional[float] = None) -> torch.Tensor:
+    """The attention alone: qkv bf16 [B, T, 3 heads dh] (q | k | v) -> ctx bf16 [B, T, heads dh]."""
+    _require_cuda("attention_core", qkv, rel, lengths)
+    B, T, C = qkv.shape
+    dh = rel.shape[1]
+    inner = heads * dh
+    q = qkv if qkv.stride(-1) == 1 else qkv.contiguous()
+    ctx = torch.empty((B, T, inner), dtype=torch.bfloat16, device=qkv.device)
+    lens = None if lengths is None else lengths.to(device=qkv.device, dtype=torch.int32).contiguous()
+    if q.stride(0) != T * q.stride(1):
+        q = q.contiguous()
+    _lib.call("gsn_attention_core_bf16", q.data_ptr(), q.stride(1), rel.data_ptr(), rel.shape[0], ctx.data_ptr(),
+              inner, _ptr(lens), B, T, heads, dh, context, max_pos, float(dh ** -0.5 if scale is None else scale),
+              _stream(q))
+    return ctx
 
 
 def run_feed_forward_half(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -105,6 +105,49 @@ def make_ff_params(seed: int, d_model: int = D_MODEL, mult: int = FF_MULT, w_std
     )
 
 
+NUM_HEADS = 8            # EncoderConfig.num_heads
+DIM_HEAD = 128           # hidden_dim // num_heads
+CONTEXT = 200            # EncoderConfig.context_size
+MAX_POS_EMB = 512        # EncoderConfig.max_pos_emb
+
+
+@dataclass
+class AttentionParams:
+    """Parameters of one ConformerAttention (``models/granite_speech_nar/conformer.py:43-59``), named after its
+    state_dict keys (pre_norm, to_q, to_kv, to_out, rel_pos_emb).  All arrays are float32."""
+
+    norm_weight: np.ndarray        # (D,)
+    norm_bias: np.ndarray          # (D,)
+    q_weight: np.ndarray           # (inner, D)      to_q.weight (no bias)
+    kv_weight: np.ndarray          # (2 inner, D)    to_kv.weight (no bias): k rows, then v rows
+    out_weight: np.ndarray         # (D, inner)      to_out.weight
+    out_bias: np.ndarray           # (D,)
+    rel_pos: np.ndarray            # (2 max_pos + 1, dim_head)   rel_pos_emb.weight
+    heads: int = NUM_HEADS
+    context: int = CONTEXT
+    max_pos: int = MAX_POS_EMB
+    ln_eps: float = 1e-5
+
+
+def make_attn_params(seed: int, d_model: int = D_MODEL, heads: int = NUM_HEADS, w_std: float = 0.02,
+                     rel_std: float = 1.0) -> AttentionParams:
+    """Random-init parameters of one attention step: projections ~N(0, w_std), the relative-position table
+    ~N(0, rel_std) (nn.Embedding's own initialisation is N(0, 1)), LayerNorm as in :func:`make_params`."""
+    g = np.random.default_rng(seed)
+    f32 = np.float32
+    inner = heads * DIM_HEAD
+    return AttentionParams(
+        norm_weight=(1.0 + g.normal(0.0, 0.02, d_model)).astype(f32),
+        norm_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+        q_weight=g.normal(0.0, w_std, (inner, d_model)).astype(f32),
+        kv_weight=g.normal(0.0, w_std, (2 * inner, d_model)).astype(f32),
+        out_weight=g.normal(0.0, w_std, (d_model, inner)).astype(f32),
+        out_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+        rel_pos=g.normal(0.0, rel_std, (2 * MAX_POS_EMB + 1, DIM_HEAD)).astype(f32),
+        heads=heads,
+    )
+
+
 def make_activations(seed: int, shape: tuple[int, ...]) -> np.ndarray:
     """x ~ N(0, 1), float32."""
     return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)

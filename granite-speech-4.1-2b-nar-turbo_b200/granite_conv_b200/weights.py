@@ -234,3 +234,60 @@ def prepare_ff_from_params(params, device="cuda") -> PreparedFeedForward:
     return prepare_ff_from_tensors(t(params.norm_weight), t(params.norm_bias), t(params.up_weight),
                                    t(params.up_bias), t(params.down_weight), t(params.down_bias),
                                    ln_eps=params.ln_eps, device=device)
+
+
+@dataclass
+class PreparedAttention:
+    """Device operands of one ConformerAttention (``models/granite_speech_nar/conformer.py:43-131``)."""
+
+    ln_w: torch.Tensor          # [D] bf16
+    ln_b: torch.Tensor          # [D] bf16
+    w_qkv: torch.Tensor         # [3 inner, D] bf16: to_q.weight rows, then to_kv.weight rows (k, then v)
+    b_qkv: torch.Tensor         # [3 inner] fp32 zeros (the projections have no bias)
+    w_out: torch.Tensor         # [D, inner] bf16
+    b_out: torch.Tensor         # [D] fp32
+    rel: torch.Tensor           # [2 max_pos + 1, dim_head] bf16 (rel_pos_emb.weight)
+    heads: int = 8
+    context: int = 200
+    max_pos: int = 512
+    ln_eps: float = 1e-5
+
+    @property
+    def d_model(self) -> int:
+        return int(self.ln_w.shape[0])
+
+    @property
+    def dim_head(self) -> int:
+        return int(self.rel.shape[1])
+
+
+@torch.no_grad()
+def prepare_attn_from_tensors(ln_w, ln_b, q_w, kv_w, out_w, out_b, rel, heads=8, context=200, max_pos=512,
+                              ln_eps=1e-5, device="cuda") -> PreparedAttention:
+    bf = torch.bfloat16
+    dev = torch.device(device)
+    w_qkv = torch.cat([q_w.to(dev, bf), kv_w.to(dev, bf)], dim=0).contiguous()
+    return PreparedAttention(
+        ln_w=ln_w.to(dev, bf).contiguous(), ln_b=ln_b.to(dev, bf).contiguous(), w_qkv=w_qkv,
+        b_qkv=torch.zeros(w_qkv.shape[0], dtype=torch.float32, device=dev), w_out=out_w.to(dev, bf).contiguous(),
+        b_out=out_b.to(dev, bf).float().contiguous(), rel=rel.to(dev, bf).contiguous(), heads=int(heads),
+        context=int(context), max_pos=int(max_pos), ln_eps=float(ln_eps))
+
+
+@torch.no_grad()
+def prepare_attention(m: nn.Module, device="cuda") -> PreparedAttention:
+    """Operands of a ConformerAttention with the reference attribute names (pre_norm, to_q, to_kv, to_out,
+    rel_pos_emb, num_heads, context_size, max_pos_emb)."""
+    return prepare_attn_from_tensors(m.pre_norm.weight, m.pre_norm.bias, m.to_q.weight, m.to_kv.weight,
+                                     m.to_out.weight, m.to_out.bias, m.rel_pos_emb.weight, heads=m.num_heads,
+                                     context=m.context_size, max_pos=m.max_pos_emb, ln_eps=m.pre_norm.eps,
+                                     device=device)
+
+
+def prepare_attn_from_params(params, device="cuda") -> PreparedAttention:
+    """Operands from float32 parameters (``synth.AttentionParams``) as a bf16 model load makes them."""
+    t = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    return prepare_attn_from_tensors(t(params.norm_weight), t(params.norm_bias), t(params.q_weight),
+                                     t(params.kv_weight), t(params.out_weight), t(params.out_bias),
+                                     t(params.rel_pos), heads=params.heads, context=params.context,
+                                     max_pos=params.max_pos, ln_eps=params.ln_eps, device=device)

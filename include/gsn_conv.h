@@ -211,6 +211,36 @@ int gsn_ff_half_bf16(const void* x, const void* ln_w, const void* ln_b, const vo
                      const void* w_down, const float* b_down, const int32_t* lengths, void* out, int B, int T, int D,
                      int F, float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream);
 
+/* ---- block-local attention with Shaw relative positions (ConformerAttention) --------------------------------
+ * Replaces ConformerAttention.forward (models/granite_speech_nar/conformer.py:61-131) and, with the residual, the
+ * attention step of ConformerBlock.forward (conformer.py:206): frames are cut into blocks of `context` frames; in
+ * a block, head h of query i attends to the block's keys j with logits
+ *   scale * (q_i . k_j) + scale * (q_i . rel[i - j + max_pos_emb])            (conformer.py:90-104, :114-128)
+ * where rel is the rel_pos_emb table [n_rel = 2 max_pos_emb + 1, dim_head] (the reference's attention_dists,
+ * conformer.py:254-262, index the same rows).  Keys past the frames are masked (conformer.py:108-112).  With
+ * lengths, frames t >= lengths[b] are masked as keys too and get a zero context, so each utterance's result
+ * equals the module run on the utterance alone; without lengths every one of the T frames takes part, as in the
+ * reference.  Supported: dim_head 128, context 200 (the model's EncoderConfig), any even number of heads.
+ * gsn_attention_core_bf16: the attention itself.  qkv [B, T, ld_qkv] bf16 rows hold q | k | v (each heads *
+ * dim_head columns: to_q, then to_kv's two halves, conformer.py:81-82); ctx [B, T, ld_ctx] bf16 receives the
+ * heads' outputs side by side (conformer.py:129).  ld_qkv, ld_ctx multiples of 8; 16-byte aligned pointers.
+ * gsn_attention_block_bf16: out = x + to_out(attention(LayerNorm(x))) on x [B, T, D] bf16; w_qkv [3 inner, D] bf16
+ * = [to_q.weight; to_kv.weight], b_qkv [3 inner] fp32 (zeros for the reference's bias-free projections), w_out
+ * [D, inner] bf16, b_out [D] fp32, LayerNorm gamma / beta bf16.  With lengths and T % 128 == 0, padded frames of
+ * out are x + b_out.  Every frame of x must be finite (padding frames are normalised and projected too).
+ * Workspace: gsn_attention_block_workspace_bytes(B, T, D, heads, dim_head) bytes, 256-byte aligned. */
+int gsn_attention_core_bf16(const void* qkv, int64_t ld_qkv, const void* rel_table, int n_rel, void* ctx,
+                            int64_t ld_ctx, const int32_t* lengths, int B, int T, int heads, int dim_head,
+                            int context, int max_pos_emb, float scale, gsn_stream_t stream);
+
+size_t gsn_attention_block_workspace_bytes(int B, int T, int D, int heads, int dim_head);
+
+int gsn_attention_block_bf16(const void* x, const void* ln_w, const void* ln_b, float ln_eps, const void* w_qkv,
+                             const float* b_qkv, const void* w_out, const float* b_out, const void* rel_table,
+                             int n_rel, const int32_t* lengths, void* out, int B, int T, int D, int heads,
+                             int dim_head, int context, int max_pos_emb, void* workspace, size_t workspace_bytes,
+                             gsn_stream_t stream);
+
 /* ---- whole module without any allocation ------------------------------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory where they run the module —
  * a plugin inside a host application that owns the GPU memory budget and its allocator, or a latency-critical

@@ -14,7 +14,9 @@ What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/
   (``conv_kernel.py:95-96``), and the fp64 golden of ``script/cuda_kernels/conv1d.py:135-138``;
 * the GLU variant's eager chain ``F.silu(conv0(F.glu(x2, dim=1)))`` (``conv_kernel.py:91-92``);
 * ``ConformerFeedForward`` (``conformer.py:23-40``) as the block applies it, ``x + 0.5 * ff(x)``
-  (``conformer.py:205``, ``:208``), in fp32 and bf16 on the test-fire shape.
+  (``conformer.py:205``, ``:208``), in fp32 and bf16 on the test-fire shape;
+* ``ConformerAttention`` (``conformer.py:43-131``) as the block applies it, ``x + attn(x)`` (``conformer.py:206``),
+  in fp32 and bf16, whole and with each utterance trimmed to a length.
 
 Inputs and parameters come from ``granite_conv_b200.synth`` (numpy PCG64 seeds), so the tests regenerate them
 bit-for-bit and only the reference outputs are stored.  bf16 tensors are stored as uint16 bit patterns.
@@ -155,6 +157,38 @@ def main(ref_root: str) -> None:
         yb = 0.5 * ffb(xb) + xb
         np.savez_compressed(os.path.join(HERE, f"ff_half_b2t37_{tag}.npz"), bf16=_bits(yb), fp32=y32)
         out[f"ff_half_{tag}"] = tuple(yb.shape)
+
+    # ---- attention step of the block: x + ConformerAttention(x) (conformer.py:43-131, :206) --------------------
+    # bf16 (a bf16 model load) on CPU, where the attention runs the MATH backend; T = 37 (one partial block) and
+    # T = 237 (a full block and a partial one), with the encoder's attention_dists (conformer.py:254-262)
+    from models.granite_speech_nar.conformer import ConformerAttention  # noqa: E402
+    for tag, seed, w_std, T in (("w002_t237", 1201, 0.02, 237), ("w006_t37", 1202, 0.06, 37),
+                                ("w006_t237", 1203, 0.06, 237)):
+        ap = synth.make_attn_params(seed, w_std=w_std)
+        at = ConformerAttention(EC())
+        with torch.no_grad():
+            at.pre_norm.weight.copy_(torch.from_numpy(ap.norm_weight))
+            at.pre_norm.bias.copy_(torch.from_numpy(ap.norm_bias))
+            at.to_q.weight.copy_(torch.from_numpy(ap.q_weight))
+            at.to_kv.weight.copy_(torch.from_numpy(ap.kv_weight))
+            at.to_out.weight.copy_(torch.from_numpy(ap.out_weight))
+            at.to_out.bias.copy_(torch.from_numpy(ap.out_bias))
+            at.rel_pos_emb.weight.copy_(torch.from_numpy(ap.rel_pos))
+        at.eval()
+        cs = at.context_size
+        seq = torch.arange(cs)
+        dists = torch.clamp(seq.view(-1, 1) - seq.view(1, -1), -cs, cs) + at.max_pos_emb
+        x = synth.make_activations(seed + 500, (2, T, synth.D_MODEL))
+        xf = torch.from_numpy(x)
+        y32 = (at(xf, attention_dists=dists) + xf).numpy()
+        atb = at.to(torch.bfloat16)
+        xb = xf.to(torch.bfloat16)
+        yb = atb(xb, attention_dists=dists) + xb
+        lengths = np.array([T, max(1, (2 * T) // 3)], dtype=np.int32)
+        y_trim = [(atb(xb[b:b + 1, :L], attention_dists=dists) + xb[b:b + 1, :L])[0] for b, L in enumerate(lengths)]
+        np.savez_compressed(os.path.join(HERE, f"attn_b2_{tag}.npz"), bf16=_bits(yb), fp32=y32, lengths=lengths,
+                            trimmed=np.concatenate([_bits(t) for t in y_trim], axis=0))
+        out[f"attn_{tag}"] = tuple(yb.shape)
 
     for k, v in out.items():
         print(f"{k}: {v}")

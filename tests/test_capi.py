@@ -106,3 +106,30 @@ def test_validation_of_fused_and_block_entry_points():
     assert L.gsn_widen_i8_bf16(None, None, 0, None, None, 0, None) == 0
     assert L.gsn_conv_module_i8w_workspace_bytes(2, 128, 1024, 2048) == (
         L.gsn_conv_module_workspace_bytes(2, 128, 1024, 2048) + 2 * 2048 * 1024 * 2 + 1024 * 2048 * 2)
+
+
+def test_validation_of_attention_entry_points():
+    """The attention core and the whole attention step reject unsupported shapes (dim_head, context, heads,
+    the relative-position table, strides) and small workspaces before any CUDA work; empty problems succeed."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    core = L.gsn_attention_core_bf16
+    assert core(p, 3072, p, 1025, p, 1024, None, 2, 200, 8, 64, 200, 512, 0.125, None) == 2
+    assert "dim_head=64" in _lib.last_error()
+    assert core(p, 3072, p, 1025, p, 1024, None, 2, 200, 8, 128, 100, 512, 0.125, None) == 2
+    assert core(p, 3072, p, 1025, p, 1024, None, 2, 200, 0, 128, 200, 512, 0.125, None) == 1
+    assert core(p, 3072, p, 300, p, 1024, None, 2, 200, 8, 128, 200, 512, 0.125, None) == 1
+    assert "n_rel" in _lib.last_error()
+    assert core(p, 3071, p, 1025, p, 1024, None, 2, 200, 8, 128, 200, 512, 0.125, None) == 2
+    assert core(p, 3072, p, 1025, p, 1000, None, 2, 200, 8, 128, 200, 512, 0.125, None) == 2
+    assert core(None, 3072, None, 1025, None, 1024, None, 0, 200, 8, 128, 200, 512, 0.125, None) == 0
+    assert core(None, 3072, p, 1025, p, 1024, None, 2, 200, 8, 128, 200, 512, 0.125, None) == 1
+    ws = L.gsn_attention_block_workspace_bytes(2, 256, 1024, 8, 128)
+    assert ws == 2 * 256 * (1024 * 2 + 3072 * 2 + 1024 * 2)
+    blk = L.gsn_attention_block_bf16
+    assert blk(p, p, p, 1e-5, p, p, p, p, p, 1025, None, p, 2, 256, 1024, 8, 128, 200, 512, p, 100, None) == 5
+    assert "workspace" in _lib.last_error()
+    assert blk(p, p, p, 1e-5, p, p, p, p, p, 1025, None, p, 2, 256, 1024, 7, 128, 200, 512, p, ws, None) == 2
+    assert blk(p, p, p, 1e-5, p, p, p, p, p, 1025, None, p, 2, 256, 768, 8, 128, 200, 512, p, ws, None) == 2
+    assert blk(*([None] * 3), 1e-5, *([None] * 5), 1025, None, None, 0, 256, 1024, 8, 128, 200, 512, None, 0,
+               None) == 0

@@ -119,3 +119,36 @@ def test_feed_forward_half_oracle(tag, seed):
     ref = O.from_bf16_bits(g["bf16"])
     assert_bf16_close(yb, ref, f"ff half {tag} oracle vs reference")
     assert O.rel_l2(yb, ref) <= 1e-3
+
+
+ATTN_GOLDENS = [("w002_t237", 1201, 0.02, 237), ("w006_t37", 1202, 0.06, 37), ("w006_t237", 1203, 0.06, 237)]
+
+
+@pytest.mark.parametrize("tag,seed,w_std,T", ATTN_GOLDENS)
+def test_attention_block_oracle(tag, seed, w_std, T):
+    """x + ConformerAttention(x): the attention oracle against the reference module.  The fp32 form is the
+    algorithmic pin (within 1e-5).  The bf16 ("reference" rounding) form meets the bf16 gates at w_std 0.02; at
+    w_std 0.06 the logits are large enough that one bf16 rounding of q moves the output by several ulps -- the
+    reference's own bf16 and fp32 outputs differ by 7.4x the element gate and 1 % rel-L2 there -- so the bf16 form
+    is held to rel-L2 <= 5e-3 and twice the element gate.  Whole, and per utterance trimmed to a length."""
+    from oracle import attention as AT
+    from parity import stats
+    g = _load(f"attn_b2_{tag}.npz")
+    p = synth.make_attn_params(seed, w_std=w_std)
+    x = synth.make_activations(seed + 500, (2, T, synth.D_MODEL))
+    y32 = AT.attention_block(x, AT.prepare_attn_fp32(p), mode="fp32")
+    assert np.max(np.abs(y32 - g["fp32"])) <= TOL_FP32 * max(1.0, float(np.abs(g["fp32"]).max()))
+    prep = AT.prepare_attn_bf16(p)
+    xb = O.bf16_round(x)
+    lens = g["lengths"]
+    yb = AT.attention_block(xb, prep, mode="reference")
+    yl = AT.attention_block(xb, prep, lengths=lens, mode="reference")
+    valid = np.concatenate([yl[b, :L] for b, L in enumerate(lens)], axis=0)
+    for out, ref, what in ((yb, O.from_bf16_bits(g["bf16"]), "whole"), (valid, O.from_bf16_bits(g["trimmed"]), "trimmed")):
+        if w_std <= 0.02:
+            assert_bf16_close(out, ref, f"attention {tag} {what} oracle vs reference")
+        else:
+            s = stats(out, ref)
+            assert s["rel_l2"] <= 5e-3 and s["worst_ratio"] <= 2.0, f"attention {tag} {what}: {s}"
+    for b, L in enumerate(lens):   # padded frames: x + b_out
+        np.testing.assert_array_equal(yl[b, L:], O.bf16_round(xb[b, L:] + prep["b_out"]))
