@@ -385,8 +385,8 @@ def run_ours(args):
             layer_events.append((ev, c))
 
     def attn_kernels(x, out, c, p, lens, record):
-        """The four launches of gsn_attention_block_bf16: LayerNorm (every frame), the q|k|v GEMM, the attention,
-        to_out + residual."""
+        """The four launches of gsn_attention_block_bf16: LayerNorm (valid frames), the q|k|v GEMM (tiles holding
+        valid frames), the attention, to_out + residual."""
         M, T = c.padded_frames, c.T
         inner = HEADS * DIM_HEAD
         tp = ws.data_ptr()                                          # LayerNorm output [M, D]
@@ -397,11 +397,11 @@ def run_ours(args):
         if record:
             ev[0].record(stream)
         _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
-                                        p.ln_eps, None, T, sp), "layernorm")
+                                        p.ln_eps, lp, T, sp), "layernorm")
         if record:
             ev[1].record(stream)
-        _lib.check(L.gsn_gemm2_residual_bf16(tp, p.w_qkv.data_ptr(), p.b_qkv.data_ptr(), None, 0, qp, 3 * inner, M,
-                                             D, 3 * inner, lp, T, sp), "qkv")
+        _lib.check(L.gsn_gemm_linear_bf16(tp, p.w_qkv.data_ptr(), p.b_qkv.data_ptr(), qp, 3 * inner, M, D, 3 * inner,
+                                          lp, T, sp), "qkv")
         if record:
             ev[2].record(stream)
         _lib.check(L.gsn_attention_core_bf16(qp, 3 * inner, p.rel.data_ptr(), p.rel.shape[0], cp, inner, lp, c.B, T,
@@ -508,7 +508,7 @@ def run_ours(args):
                 "per_launch_ms": k["ms_per_launch"],
                 "work": "q|k|v and to_out GEMMs: 6.291 / 2.097 MFLOP per row of the 128-row tiles holding valid "
                         "frames; attention: 6144 FLOP per (valid query, valid key of its 200-frame block) "
-                        "(q.k, q.rel[i-j], p.v over 8 heads x 128); LayerNorm: 4 KB per frame",
+                        "(q.k, q.rel[i-j], p.v over 8 heads x 128); LayerNorm: 4 KB per valid frame",
                 "peak_source": f"bf16_tflops_sustained / hbm_gbs of {peaks['source']}", "kernels": kernels}
     else:
         kernels = _kernel_breakdown(layer_events, peaks, widen_events, ln_name="layernorm" if int8 else "ln_stats")
@@ -592,7 +592,7 @@ def _attn_query_keys(c):
 
 
 def _attn_breakdown(layer_events, peaks):
-    """Per-kernel launch time and rate of the attention step: LayerNorm over every frame (2 x 2 KB), the q|k|v and
+    """Per-kernel launch time and rate of the attention step: LayerNorm over the valid frames (2 x 2 KB), the q|k|v and
     to_out GEMMs (rows of the 128-row tiles holding valid frames), the attention (ATTN_FLOP_PER_QUERY_KEY per valid
     query-key pair of a block)."""
     names = ("layernorm", "qkv_proj", "attention", "out_proj")
@@ -602,7 +602,7 @@ def _attn_breakdown(layer_events, peaks):
         for k, n in enumerate(names):
             tot[n] += ev[k].elapsed_time(ev[k + 1])
         rows = _tile_rows(c)
-        work["layernorm"] += c.padded_frames * 2 * D * 2
+        work["layernorm"] += c.valid_frames * 2 * D * 2
         work["qkv_proj"] += rows * QKV_FLOP_PER_FRAME
         work["attention"] += _attn_query_keys(c) * ATTN_FLOP_PER_QUERY_KEY
         work["out_proj"] += rows * OUT_FLOP_PER_FRAME

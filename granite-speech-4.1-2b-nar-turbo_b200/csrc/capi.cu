@@ -363,6 +363,16 @@ int gsn_gemm_silu_bf16(const void* a, const void* w, const float* b, void* h, in
   return finish(launch_gemm(g, kEpiSilu, (cudaStream_t)stream), name);
 }
 
+int gsn_gemm_linear_bf16(const void* a, const void* w, const float* b, void* out, int64_t ld_out, int M, int K, int N,
+                         const int32_t* lengths, int T, gsn_stream_t stream) {
+  const char* name = "gsn_gemm_linear_bf16";
+  if (int rc = check_gemm(name, a, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
+  if (ld_out % 8 || ld_out < N) return fail(GSN_ERR_UNSUPPORTED, "%s: ld_out must be >= N and a multiple of 8", name);
+  if (int rc = check_lengths(name, lengths, T, M)) return rc;
+  GemmArgs g{(const __nv_bfloat16*)a, w, b, nullptr, nullptr, (__nv_bfloat16*)out, ld_out, 0, M, N, K, 0, lengths, T};
+  return finish(launch_gemm(g, kEpiLinear, (cudaStream_t)stream), name);
+}
+
 int gsn_gemm_residual_scaled_bf16(const void* d, const void* w, const float* b, const void* residual, int64_t ld_res,
                                   void* out, int64_t ld_out, int M, int K, int N, float out_scale,
                                   const int32_t* lengths, int T, gsn_stream_t stream) {
@@ -485,12 +495,13 @@ int gsn_attention_block_bf16(const void* x, const void* ln_w, const void* ln_b, 
   __nv_bfloat16* ctx = (__nv_bfloat16*)((char*)qkv + align256((size_t)M * 3 * inner * 2));
   const cudaStream_t st = (cudaStream_t)stream;
   const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
-  // every frame is normalised (padding frames too), so that every q|k|v row the attention reads is finite
+  // with lengths, padding frames are neither normalised nor projected (128-row tiles of pure padding are skipped):
+  // the attention masks those keys and zeroes their V rows before use, and writes a zero context for them
   int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
-                            M, D, ln_eps, nullptr, T, st);
+                            M, D, ln_eps, skip, T, st);
   if (rc) return finish(rc, name);
   GemmArgs g1{t, w_qkv, b_qkv, nullptr, nullptr, qkv, (int64_t)3 * inner, 0, M, 3 * inner, D, 0, skip, T};
-  rc = launch_gemm(g1, kEpiResidual, st);
+  rc = launch_gemm(g1, kEpiLinear, st);
   if (rc) return finish(rc, name);
   AttnArgs a{qkv, (int64_t)3 * inner, (const __nv_bfloat16*)rel_table, n_rel, ctx, (int64_t)inner, lengths, B, T,
              heads, max_pos_emb, 1.0f / sqrtf((float)dim_head)};

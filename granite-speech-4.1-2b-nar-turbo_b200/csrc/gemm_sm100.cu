@@ -942,7 +942,8 @@ int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* 
 }
 
 int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
-  if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale && epilogue != kEpiSilu && a.out_scale == 1.0f) {
+  if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale && (epilogue == kEpiGlu || epilogue == kEpiResidual) &&
+      a.out_scale == 1.0f) {
     bool launched = false;
     const int rc = epilogue == kEpiGlu ? launch_pair<kEpiGlu>(a, stream, &launched)
                                        : launch_pair<kEpiResidual>(a, stream, &launched);
@@ -957,6 +958,10 @@ int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
   if (epilogue == kEpiSilu) {
     if (a.w_int8 || a.col_scale) return (int)cudaErrorInvalidValue;
     return launch_single<kEpiSilu, false, false>(a, stream);
+  }
+  if (epilogue == kEpiLinear) {
+    if (a.w_int8 || a.col_scale || a.residual) return (int)cudaErrorInvalidValue;
+    return launch_single<kEpiLinear, false, false>(a, stream);
   }
   if (a.w_int8) return launch_single<kEpiResidual, true, true>(a, stream);
   return a.col_scale ? launch_single<kEpiResidual, false, true>(a, stream)

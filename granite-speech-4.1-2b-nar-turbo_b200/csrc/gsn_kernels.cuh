@@ -39,7 +39,8 @@ struct GemmArgs {
   float out_scale = 1.0f;        // RESIDUAL: out = out_scale * (acc * col_scale + bias) + residual
 };
 
-enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2 };
+// LINEAR: out = acc + b, 128-row tiles of pure padding skipped (nothing written there)
+enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2, kEpiLinear = 3 };
 
 int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
 // int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).

@@ -227,13 +227,19 @@ int gsn_ff_half_bf16(const void* x, const void* ln_w, const void* ln_b, const vo
  * gsn_attention_block_bf16: out = x + to_out(attention(LayerNorm(x))) on x [B, T, D] bf16; w_qkv [3 inner, D] bf16
  * = [to_q.weight; to_kv.weight], b_qkv [3 inner] fp32 (zeros for the reference's bias-free projections), w_out
  * [D, inner] bf16, b_out [D] fp32, LayerNorm gamma / beta bf16.  With lengths and T % 128 == 0, padded frames of
- * out are x + b_out.  Every frame of x must be finite (padding frames are normalised and projected too).
+ * out are x + b_out.  Without lengths every frame of x must be finite.
  * Workspace: gsn_attention_block_workspace_bytes(B, T, D, heads, dim_head) bytes, 256-byte aligned. */
 int gsn_attention_core_bf16(const void* qkv, int64_t ld_qkv, const void* rel_table, int n_rel, void* ctx,
                             int64_t ld_ctx, const int32_t* lengths, int B, int T, int heads, int dim_head,
                             int context, int max_pos_emb, float scale, gsn_stream_t stream);
 
 size_t gsn_attention_block_workspace_bytes(int B, int T, int D, int heads, int dim_head);
+
+/* gsn_gemm_linear_bf16: out = a W^T + b (a [M, K] bf16, W [N, K] bf16, b [N] fp32, out rows of stride ld_out); with
+ * lengths (T % 128 == 0, M a multiple of T) the 128-row tiles made only of padding frames are skipped and left
+ * unwritten.  The q|k|v projection of the attention step.  K % 64, N % 256 == 0. */
+int gsn_gemm_linear_bf16(const void* a, const void* w, const float* b, void* out, int64_t ld_out, int M, int K, int N,
+                         const int32_t* lengths, int T, gsn_stream_t stream);
 
 int gsn_attention_block_bf16(const void* x, const void* ln_w, const void* ln_b, float ln_eps, const void* w_qkv,
                              const float* b_qkv, const void* w_out, const float* b_out, const void* rel_table,

@@ -138,3 +138,39 @@ def test_attention_block_compile_fullgraph():
     x = torch.randn((2, 256, synth.D_MODEL), device=DEV).bfloat16()
     f = lambda x: ops.run_attention_block(x, p)  # noqa: E731
     assert torch.equal(torch.compile(f, fullgraph=True)(x), f(x))
+
+
+def test_gemm_linear_skips_padding_tiles():
+    """out = a W^T + b; with lengths the 128-row tiles of pure padding are left untouched."""
+    B, T, K, N = 3, 256, 1024, 3072
+    M = B * T
+    g = torch.Generator(device=DEV).manual_seed(9)
+    a = torch.randn((M, K), generator=g, device=DEV).bfloat16()
+    w = (torch.randn((N, K), generator=g, device=DEV) * 0.03).bfloat16()
+    b = torch.randn((N,), generator=g, device=DEV) * 0.1
+    out = torch.full((M, N), 7.0, dtype=torch.bfloat16, device=DEV)
+    lens = torch.tensor([256, 100, 0], dtype=torch.int32, device=DEV)
+    _lib.call("gsn_gemm_linear_bf16", a.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(), N, M, K, N,
+              lens.data_ptr(), T, torch.cuda.current_stream().cuda_stream)
+    ref = (a.float() @ w.float().t() + b).cpu().numpy()
+    o = out.float().cpu().numpy()
+    active = np.concatenate([np.arange(0, 256), np.arange(256, 384)])      # tiles holding valid frames
+    assert_bf16_close(o[active], ref[active], "linear gemm")
+    assert (o[384:] == 7.0).all(), "tiles of pure padding are not written"
+
+
+def test_attention_core_ignores_padding_rows():
+    """q|k|v rows of frames past the length hold NaN / Inf: masked keys never reach a valid output (their logits
+    are replaced, their V rows zeroed before P V), and padded frames get a zero context."""
+    B, T = 3, 512
+    qkv = _qkv(21, B, T, q_std=0.3)
+    lens = np.array([512, 201, 77], dtype=np.int32)
+    ref = _core_ref(qkv, _rel(22), lens)
+    bad = qkv.copy()
+    for b, L in enumerate(lens):
+        bad[b, L:, 0::2] = np.nan
+        bad[b, L:, 1::2] = np.inf
+    ctx = ops.attention_core(_t(bad), _t(_rel(22)), H, torch.from_numpy(lens).to(DEV)).float().cpu().numpy()
+    for b, L in enumerate(lens):
+        assert_bf16_close(ctx[b, :L], ref[b, :L], f"b={b} L={L}")
+        assert not ctx[b, L:].any()
