@@ -72,6 +72,98 @@ __device__ __forceinline__ bool rows_active(const KParams& p, int blk) {
 
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
+// The tile list every role of a CTA walks (s = blockIdx.x + k * gridDim.x).  With lengths (B = M / T utterances of
+// T % 128 == 0 frames), the list holds first the tiles of the 128-row blocks that contain valid frames, so those are
+// dealt evenly over the CTAs whatever the utterance lengths, then the tiles of pure padding (only the residual
+// epilogue touches them).  Per-utterance prefix counts of both kinds of blocks live in shared memory.
+constexpr int kMapMaxB = 512;
+
+struct TileMap {
+  int num_n, num_tiles, active_tiles;
+  int mpu, B;                 // 128-row blocks per utterance, utterances (with the map)
+  const int* act;             // act[b]: active blocks of utterances < b (B + 1 entries)
+  const int* pad;             // pad[b]: padding blocks of utterances < b
+  bool mapped;
+
+  __device__ static int upper(const int* pref, int n, int v) {   // largest b with pref[b] <= v
+    int lo = 0, hi = n;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pref[mid] <= v) lo = mid; else hi = mid;
+    }
+    return lo;
+  }
+
+  // tile s -> (m_blk, n_blk); `active` false for a tile of pure padding (or past M)
+  __device__ void get(int s, const KParams& p, int& m_blk, int& n_blk, bool& active) const {
+    const int mi = s / num_n;
+    n_blk = s - mi * num_n;
+    if (!mapped) {
+      m_blk = mi;
+      active = rows_active(p, m_blk);
+      return;
+    }
+    const int na = act[B];
+    if (mi < na) {
+      const int b = upper(act, B, mi);
+      m_blk = b * mpu + (mi - act[b]);
+      active = true;
+    } else {
+      const int ip = mi - na;
+      const int b = upper(pad, B, ip);
+      m_blk = b * mpu + (act[b + 1] - act[b]) + (ip - pad[b]);
+      active = false;
+    }
+  }
+};
+
+// Builds the prefix counts (all threads of the CTA take part; ends with __syncthreads).
+__device__ void build_tile_map(TileMap& tm, int* act, int* pad, const KParams& p, int num_m, int num_n) {
+  tm.num_n = num_n;
+  tm.num_tiles = num_m * num_n;
+  tm.mapped = p.lengths != nullptr && p.T > 0 && p.M % p.T == 0 && p.T % BM == 0 && p.M / p.T <= kMapMaxB;
+  tm.act = act;
+  tm.pad = pad;
+  tm.B = tm.mapped ? p.M / p.T : 0;
+  tm.mpu = p.T / BM;
+  if (tm.mapped) {
+    for (int b = threadIdx.x; b < tm.B; b += blockDim.x) {
+      const int L = min(max(__ldg(p.lengths + b), 0), p.T);
+      act[b + 1] = (L + BM - 1) / BM;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // inclusive scan in chunks of 32, carried across chunks
+      int carry_a = 0, carry_p = 0;
+      for (int base = 0; base < tm.B; base += 32) {
+        const int b = base + (int)threadIdx.x;
+        int a = b < tm.B ? act[b + 1] : 0;
+        int q = b < tm.B ? tm.mpu - a : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int ya = __shfl_up_sync(0xffffffffu, a, o), yq = __shfl_up_sync(0xffffffffu, q, o);
+          if ((int)threadIdx.x >= o) {
+            a += ya;
+            q += yq;
+          }
+        }
+        if (b < tm.B) {
+          act[b + 1] = carry_a + a;
+          pad[b + 1] = carry_p + q;
+        }
+        carry_a += __shfl_sync(0xffffffffu, a, 31);
+        carry_p += __shfl_sync(0xffffffffu, q, 31);
+      }
+      if (threadIdx.x == 0) {
+        act[0] = 0;
+        pad[0] = 0;
+      }
+    }
+  }
+  __syncthreads();
+  tm.active_tiles = tm.mapped ? act[tm.B] * num_n : tm.num_tiles;
+}
+
 // Four signed int8 (one 32-bit word) -> two bf16x2 words, exactly.  Each byte is biased to unsigned
 // (v + 128), placed in the low mantissa bits of the fp32 2^23, and the bias 2^23 + 128 is subtracted; every
 // |v| <= 127 is exact in bf16.
@@ -336,6 +428,8 @@ struct __align__(1024) Smem {
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t mma_done;
+  int map_act[kMapMaxB + 1];
+  int map_pad[kMapMaxB + 1];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -357,7 +451,6 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = p.N / BN;
-  const int num_tiles = num_m * num_n;
   const int num_kb = p.K / BK;
 
   if (threadIdx.x == 0) {
@@ -387,6 +480,8 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  TileMap tmap;
+  build_tile_map(tmap, s.map_act, s.map_pad, p, num_m, num_n);
   const uint32_t tmem_base = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
 
@@ -397,10 +492,11 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     uint32_t phase = 0;
     int issued = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int m_blk = tile / num_n;
-      const int n_blk = tile - m_blk * num_n;
-      if (!rows_active(p, m_blk)) continue;
+    for (int tile = blockIdx.x; tile < tmap.active_tiles && ok; tile += gridDim.x) {
+      int m_blk, n_blk;
+      bool active;
+      tmap.get(tile, p, m_blk, n_blk, active);
+      if (!active) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         bool got = mbar_wait_bounded(&s.empty[stage], phase ^ 1u, abort_flag, kStatusTimeoutProducer);
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -442,8 +538,11 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     uint32_t phase = 0;
     bool ok = true;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      if (!rows_active(p, tile / num_n)) continue;
+    for (int tile = blockIdx.x; tile < tmap.active_tiles && ok; tile += gridDim.x) {
+      int m_blk, n_blk;
+      bool active;
+      tmap.get(tile, p, m_blk, n_blk, active);
+      if (!active) continue;
       const int acc = local & 1;
       const uint32_t use_par = (uint32_t)((local >> 1) & 1);
       ++local;
@@ -492,10 +591,11 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     Epilogue<EPI, SCALED> epi;
     epi.init(s.epi, warp - 2, &tmO, &tmR, p);
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m_blk = tile / num_n;
-      const int n_blk = tile - m_blk * num_n;
-      const bool active = rows_active(p, m_blk);
+    const int epi_tiles = EPI == kEpiResidual ? tmap.num_tiles : tmap.active_tiles;
+    for (int tile = blockIdx.x; tile < epi_tiles; tile += gridDim.x) {
+      int m_blk, n_blk;
+      bool active;
+      tmap.get(tile, p, m_blk, n_blk, active);
       if (EPI != kEpiResidual && !active) continue;   // GLU / SiLU rows of padding frames are never read downstream
       const int nb = n_blk * BN;
       epi.load_vectors(p, nb);
@@ -529,8 +629,11 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      if (!rows_active(p, tile / num_n)) continue;
+    for (int tile = blockIdx.x; tile < tmap.active_tiles && ok; tile += gridDim.x) {
+      int m_blk, n_blk;
+      bool active;
+      tmap.get(tile, p, m_blk, n_blk, active);
+      if (!active) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         bool got = mbar_wait_bounded(&s.full[stage], phase, abort_flag, kStatusTimeoutMma);
         got = __shfl_sync(0xffffffffu, got, 0);
