@@ -12,7 +12,8 @@ of all ranks / the slowest rank's time.  Inputs are resident in HBM and larger t
 Other workloads (single-GPU measurements): "module" = one conv module on one B=48 chunk (lognormal lengths, T on
 the 128 grid), "module_i8" = the same with int8 weights, "dw" = the depthwise kernel alone on [48, 1024, 2048],
 "ff" = one feed-forward half on the same chunk, "attn" = one attention step (block-local, Shaw relative
-positions) on the same chunk.
+positions) on the same chunk, "block" = one whole Conformer block (FF/2, attention, conv, FF/2, post norm) on the
+same chunk, "encoder" = 16 Conformer blocks over the stack's 512 utterances (the encoder body).
 
 ``--impl reference`` times the CPU oracle (numpy restatement of the reference eager module) on the host cores on a
 bounded sample of the same workload and prints the same JSON line with "impl": "reference".
@@ -133,11 +134,11 @@ def _dist_env():
 
 def _workload_plan(rank: int, workload: str):
     """Chunks of this rank (list of dispatch.Chunk) for the workload."""
-    if workload == "stack":
+    if workload in ("stack", "encoder"):
         lens = synth.sample_lengths(1005 + 7919 * rank, N_UTTS)
         return dispatch.plan_chunks(lens, exec_batch=dispatch.EXEC_BATCH, logical_batch=dispatch.LOGICAL_BATCH,
                                     frame_grid=dispatch.FRAME_GRID)
-    if workload in ("module", "module_i8", "ff", "attn"):
+    if workload in ("module", "module_i8", "ff", "attn", "block"):
         lens = synth.sample_lengths(1003 + 7919 * rank, 48)
         T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
         return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
@@ -147,7 +148,7 @@ def _workload_plan(rank: int, workload: str):
 
 
 def _layers_for(workload: str) -> int:
-    return N_LAYERS if workload == "stack" else 1
+    return N_LAYERS if workload in ("stack", "encoder") else 1
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -165,6 +166,9 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
         ffprep = FFO.prepare_ff_fp32(synth.make_ff_params(1006))
     elif workload == "attn":
         atprep = ATO.prepare_attn_fp32(synth.make_attn_params(1007))
+    elif workload in ("block", "encoder"):
+        from oracle import block as BKO
+        bkprep = BKO.prepare_block(synth.make_block_params(1008), mode="fp32")
     else:
         params = synth.make_params(1005)
         prep = O.prepare_fp32(params)
@@ -185,6 +189,8 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
             FFO.feed_forward_half(x, ffprep, lengths=lens, mode="fp32", dtype=np.float32)
         elif workload == "attn":
             ATO.attention_block(x, atprep, lengths=lens, mode="fp32", dtype=np.float32)
+        elif workload in ("block", "encoder"):
+            BKO.conformer_block(x, bkprep, lengths=lens, mode="fp32", dtype=np.float32)
         else:
             O.conv_module(x, prep, lengths=lens, mode="fp32", dtype=np.float32)
         frames += int(lens.sum())
@@ -236,9 +242,13 @@ def _config(args, world):
               "residual), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
         "attn": "one attention step of the Conformer block (LN, 1024->3072 q|k|v GEMM, block-local attention over "
                 "200-frame blocks with Shaw relative positions, 8 heads x 128, 1024->1024 GEMM + residual), B=48 "
-                "chunk, lognormal lengths, T on the 128-frame grid, length mask"}[w],
+                "chunk, lognormal lengths, T on the 128-frame grid, length mask",
+        "block": "one Conformer block (FF/2, block-local Shaw attention, conv module, FF/2, post LayerNorm; 14 "
+                 "launches), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
+        "encoder": "16 Conformer blocks (the encoder body: FF/2, attention, conv, FF/2, post norm per block), 512 "
+                   "utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid"}[w],
         "d_model": D, "d_inner": I, "kernel": 15, "layers": _layers_for(w),
-        "utterances_per_rank": N_UTTS if w == "stack" else 48, "exec_batch": dispatch.EXEC_BATCH,
+        "utterances_per_rank": N_UTTS if w in ("stack", "encoder") else 48, "exec_batch": dispatch.EXEC_BATCH,
         "frame_grid": dispatch.FRAME_GRID, "parallelism": f"dp{world} (independent shards, no collective)",
         "l2": "inputs larger than L2 (no flush)",
         "frames": "valid encoder frames x layers (padding excluded)"}
@@ -288,6 +298,10 @@ def run_ours(args):
         from granite_conv_b200.weights import prepare_attn_from_params
         layers = [prepare_attn_from_params(synth.make_attn_params(1007), device=dev)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+    elif workload in ("block", "encoder"):
+        from granite_conv_b200 import prepare_block_from_params
+        layers = [prepare_block_from_params(synth.make_block_params(1008 + l), device=dev) for l in range(n_layers)]
+        xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     else:
         # bf16: the LayerNorm folded into the up_conv GEMM (the module op's path for T on the 128 grid)
         layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8, ln_fold=not int8)
@@ -298,7 +312,9 @@ def run_ours(args):
     ws_bytes = int(L.gsn_conv_module_workspace_bytes(1, max_m, D, I))
     if workload == "ff":
         ws_bytes = max(ws_bytes, int(L.gsn_ff_half_workspace_bytes(1, max_m, D, 4 * D)))
-    if workload == "attn":
+    if workload in ("ff", "block", "encoder"):
+        ws_bytes = max(ws_bytes, int(L.gsn_ff_half_workspace_bytes(1, max_m, D, 4 * D)))
+    if workload in ("attn", "block", "encoder"):
         ws_bytes = max(ws_bytes, int(L.gsn_attention_block_workspace_bytes(1, max_m, D, HEADS, DIM_HEAD)))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     h_buf = ws                                                         # [M, I] GLU output
@@ -414,6 +430,68 @@ def run_ours(args):
             ev[4].record(stream)
             layer_events.append((ev, c))
 
+    kev = []       # block / encoder: (kernel name, start event, end event, chunk) of every recorded launch
+
+    def timed(name, c, record, fn):
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            kev.append((name, e0, e1, c))
+        else:
+            fn()
+
+    def block_kernels(x, out, tmp, c, p, lens, record):
+        """One Conformer block, the launches run_conformer_block makes: FF/2 (3), attention (4), conv module with
+        the LayerNorm folded (3), FF/2 (3), post LayerNorm over every frame (1).  x -> tmp -> out -> tmp -> out."""
+        M, T = c.padded_frames, c.T
+        lp = lens.data_ptr()
+        inner = HEADS * DIM_HEAD
+
+        def ff(tag, src, dst, q):
+            tp = ws.data_ptr()
+            hp = ws.data_ptr() + ((M * D * 2 + 255) // 256) * 256
+            timed(tag + ".layernorm", c, record, lambda: _lib.check(L.gsn_layernorm_bf16(
+                src.data_ptr(), D, q.ln_w.data_ptr(), q.ln_b.data_ptr(), tp, D, M, D, q.ln_eps, lp, T, sp), "ln"))
+            timed(tag + ".up_silu", c, record, lambda: _lib.check(L.gsn_gemm_silu_bf16(
+                tp, q.w_up.data_ptr(), q.b_up.data_ptr(), hp, M, D, q.d_ff, lp, T, sp), "ff up"))
+            timed(tag + ".down_residual", c, record, lambda: _lib.check(L.gsn_gemm_residual_scaled_bf16(
+                hp, q.w_down.data_ptr(), q.b_down.data_ptr(), src.data_ptr(), D, dst.data_ptr(), D, M, q.d_ff, D, 0.5,
+                lp, T, sp), "ff down"))
+
+        ff("ff1", x, tmp, p.ff1)
+        a = p.attn
+        tp = ws.data_ptr()
+        qp = tp + ((M * D * 2 + 255) // 256) * 256
+        cp = qp + ((M * 3 * inner * 2 + 255) // 256) * 256
+        timed("attn.layernorm", c, record, lambda: _lib.check(L.gsn_layernorm_bf16(
+            tmp.data_ptr(), D, a.ln_w.data_ptr(), a.ln_b.data_ptr(), tp, D, M, D, a.ln_eps, lp, T, sp), "ln"))
+        timed("attn.qkv", c, record, lambda: _lib.check(L.gsn_gemm_linear_bf16(
+            tp, a.w_qkv.data_ptr(), a.b_qkv.data_ptr(), qp, 3 * inner, M, D, 3 * inner, lp, T, sp), "qkv"))
+        timed("attn.attention", c, record, lambda: _lib.check(L.gsn_attention_core_bf16(
+            qp, 3 * inner, a.rel.data_ptr(), a.rel.shape[0], cp, inner, lp, c.B, T, HEADS, DIM_HEAD, CONTEXT,
+            a.max_pos, DIM_HEAD ** -0.5, sp), "attention"))
+        timed("attn.out_proj", c, record, lambda: _lib.check(L.gsn_gemm2_residual_bf16(
+            cp, a.w_out.data_ptr(), a.b_out.data_ptr(), tmp.data_ptr(), D, out.data_ptr(), D, M, inner, D, lp, T,
+            sp), "to_out"))
+        v = p.conv
+        dp = ws.data_ptr()
+        sp_ = ws.data_ptr() + t_off
+        timed("conv.ln_stats", c, record, lambda: _lib.check(L.gsn_layernorm_stats_bf16(
+            out.data_ptr(), D, sp_, M, D, v.ln_eps, lp, T, sp), "ln_stats"))
+        timed("conv.gemm1_glu_dw", c, record, lambda: _lib.check(L.gsn_gemm1_lnfold_glu_dwconv_bf16(
+            out.data_ptr(), v.w1g_glu.data_ptr(), v.b1g_glu.data_ptr(), v.c1_glu.data_ptr(), sp_, v.dw_w.data_ptr(),
+            v.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp, sp), "gemm1_dw"))
+        timed("conv.gemm2_residual", c, record, lambda: _lib.check(L.gsn_gemm2_residual_bf16(
+            dp, v.w2.data_ptr(), v.b2.data_ptr(), out.data_ptr(), D, tmp.data_ptr(), D, M, I, D, lp, T, sp),
+            "gemm2"))
+        ff("ff2", tmp, out, p.ff2)
+        timed("post_ln", c, record, lambda: _lib.check(L.gsn_layernorm_bf16(
+            out.data_ptr(), D, p.post_ln_w.data_ptr(), p.post_ln_b.data_ptr(), out.data_ptr(), D, M, D, p.post_ln_eps,
+            None, T, sp), "post ln"))
+
     dw_events = []
 
     def step(record=False):
@@ -441,6 +519,10 @@ def run_ours(args):
                 elif workload == "attn":
                     attn_kernels(src, dst, c, p, lens_dev[ci], record)
                     n += 4
+                elif workload in ("block", "encoder"):
+                    dst = act[ci]
+                    block_kernels(src, dst, act2[ci], c, p, lens_dev[ci], record)
+                    n += 14
                 else:
                     layer_kernels(src, dst, c, p, lens_dev[ci], record)
                     n += 4 if int8 else 3
@@ -499,6 +581,14 @@ def run_ours(args):
                 "traffic": None, "per_launch_ms": g1["ms_per_launch"], "algorithmic_flop_per_frame": FF_FLOP_PER_FRAME,
                 "frames_counted": "rows of the 128-row tiles holding valid frames",
                 "peak_source": f"bf16_tflops_sustained of {peaks['source']}", "kernels": kernels}
+    elif workload in ("block", "encoder"):
+        kernels = _named_breakdown(kev, peaks)
+        top = max(kernels, key=lambda n: kernels[n]["share"])
+        k = kernels[top]
+        roof = {"kernel": top, "bound": "hbm" if k["unit"] == "GB/s" else "tensor", "achieved": k["achieved"],
+                "peak": k["peak"], "unit": k["unit"], "frac": k["frac"], "traffic": None,
+                "per_launch_ms": k["ms_per_launch"],
+                "peak_source": f"bf16_tflops_sustained / hbm_gbs of {peaks['source']}", "kernels": kernels}
     elif workload == "attn":
         kernels = _attn_breakdown(layer_events, peaks)
         top = max(kernels, key=lambda n: kernels[n]["share"])
@@ -529,7 +619,7 @@ def run_ours(args):
     e2e = None
     if workload != "dw" and not args.no_e2e:
         e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff",
-                   attn=workload == "attn")
+                   attn=workload == "attn", block=workload in ("block", "encoder"))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -591,6 +681,49 @@ def _attn_query_keys(c):
     return n
 
 
+# work of each named launch of the block / encoder workloads: (kind, per-chunk work function)
+def _named_work(name, c):
+    rows = _tile_rows(c)
+    kind = name.split(".")[-1]
+    if kind == "layernorm":
+        return "hbm", c.valid_frames * 2 * D * 2
+    if name == "post_ln":
+        return "hbm", c.padded_frames * 2 * D * 2
+    if kind == "ln_stats":
+        return "hbm", c.valid_frames * (D * 2 + 8)
+    if kind in ("up_silu", "down_residual", "gemm1_glu_dw"):
+        return "tensor", rows * FF_FLOP_PER_FRAME
+    if kind == "gemm2_residual":
+        return "tensor", rows * GEMM2_FLOP_PER_FRAME
+    if kind == "qkv":
+        return "tensor", rows * QKV_FLOP_PER_FRAME
+    if kind == "out_proj":
+        return "tensor", rows * OUT_FLOP_PER_FRAME
+    if kind == "attention":
+        return "tensor", _attn_query_keys(c) * ATTN_FLOP_PER_QUERY_KEY
+    raise KeyError(name)
+
+
+def _named_breakdown(kev, peaks):
+    """Per named launch: average duration, share of the recorded time, achieved rate against the measured peak."""
+    tot, work, cnt, kinds = {}, {}, {}, {}
+    for name, e0, e1, c in kev:
+        kind, w = _named_work(name, c)
+        tot[name] = tot.get(name, 0.0) + e0.elapsed_time(e1)
+        work[name] = work.get(name, 0.0) + w
+        cnt[name] = cnt.get(name, 0) + 1
+        kinds[name] = kind
+    all_ms = sum(tot.values())
+    out = {}
+    for n in tot:
+        tensor = kinds[n] == "tensor"
+        ach = work[n] / (tot[n] / 1e3) / (1e12 if tensor else 1e9)
+        pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
+        out[n] = {"ms_per_launch": tot[n] / cnt[n], "share": tot[n] / all_ms, "achieved": ach,
+                  "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
+    return out
+
+
 def _attn_breakdown(layer_events, peaks):
     """Per-kernel launch time and rate of the attention step: LayerNorm over the valid frames (2 x 2 KB), the q|k|v and
     to_out GEMMs (rows of the 128-row tiles holding valid frames), the attention (ATTN_FLOP_PER_QUERY_KEY per valid
@@ -650,7 +783,7 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
     return out
 
 
-def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn=False):
+def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn=False, block=False):
     """Same work through the public op (torch.ops.granite.conv_module per layer, or granite::feed_forward_half)
     with each chunk's input copied from pinned host memory and its output copied back inside the timed region."""
     import torch
@@ -662,6 +795,9 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
     elif attn:
         def stack(x, lengths):
             return ops.run_attention_block(x, layers[0], lengths)
+    elif block:
+        from granite_conv_b200 import ConformerEncoderStack
+        stack = ConformerEncoderStack(layers)
     else:
         stack = ConvModuleStack(layers, int8=int8)
     g = torch.Generator().manual_seed(4242)
@@ -734,8 +870,9 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
         valid = float(v.item())
     return {"value": valid * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
-            "path": ("torch.ops.granite." + ("feed_forward_half" if ff else "attention_block" if attn else
-                                              "conv_module per layer") + ", pinned host in/out on two copy streams")}
+            "path": ("ConformerEncoderStack (granite:: ops per step of each block)" if block else
+                     "torch.ops.granite." + ("feed_forward_half" if ff else "attention_block" if attn else
+                                             "conv_module per layer")) + ", pinned host in/out on two copy streams"}
 
 
 def main():
@@ -744,7 +881,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff", "attn"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff", "attn", "block", "encoder"],
+                    default="stack")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

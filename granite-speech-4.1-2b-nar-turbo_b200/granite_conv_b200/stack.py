@@ -36,28 +36,35 @@ class ConvModuleStack:
         (default: two streams).  The kernels are persistent grids of one CTA per SM, so a chunk's kernels start
         on the SMs another chunk's kernel has already released: the tail of each launch is filled.  Inputs must
         be ready on the current stream; the outputs are ready on it when this returns."""
-        if not chunks:
-            return []
-        cur = torch.cuda.current_stream(chunks[0][0].device)
-        if streams is None:
-            streams = [cur, torch.cuda.Stream(chunks[0][0].device)]
-        ready = torch.cuda.Event()
-        ready.record(cur)
-        outs = []
-        for i, (x, lengths) in enumerate(chunks):
-            st = streams[i % len(streams)]
-            st.wait_event(ready)
-            with torch.cuda.stream(st):
-                y = self(x, lengths)
-            if st is not cur:
-                x.record_stream(st)
-                if lengths is not None:
-                    lengths.record_stream(st)
-                y.record_stream(cur)
-            outs.append(y)
-        for st in streams:
-            if st is not cur:
-                done = torch.cuda.Event()
-                done.record(st)
-                cur.wait_event(done)
-        return outs
+        return run_on_streams(self, chunks, streams)
+
+
+def run_on_streams(fn, chunks: Sequence[Tuple[torch.Tensor, Optional[torch.Tensor]]],
+                   streams: Optional[Sequence[torch.cuda.Stream]] = None) -> List[torch.Tensor]:
+    """fn(x, lengths) on each chunk, chunk i on streams[i % len(streams)] (default: the current stream and one
+    more); inputs ready on the current stream, outputs ready on it on return."""
+    if not chunks:
+        return []
+    cur = torch.cuda.current_stream(chunks[0][0].device)
+    if streams is None:
+        streams = [cur, torch.cuda.Stream(chunks[0][0].device)]
+    ready = torch.cuda.Event()
+    ready.record(cur)
+    outs = []
+    for i, (x, lengths) in enumerate(chunks):
+        st = streams[i % len(streams)]
+        st.wait_event(ready)
+        with torch.cuda.stream(st):
+            y = fn(x, lengths)
+        if st is not cur:
+            x.record_stream(st)
+            if lengths is not None:
+                lengths.record_stream(st)
+            y.record_stream(cur)
+        outs.append(y)
+    for st in streams:
+        if st is not cur:
+            done = torch.cuda.Event()
+            done.record(st)
+            cur.wait_event(done)
+    return outs

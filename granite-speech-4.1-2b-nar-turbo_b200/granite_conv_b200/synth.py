@@ -148,6 +148,29 @@ def make_attn_params(seed: int, d_model: int = D_MODEL, heads: int = NUM_HEADS, 
     )
 
 
+@dataclass
+class BlockParams:
+    """Parameters of one ConformerBlock (``models/granite_speech_nar/conformer.py:190-199``)."""
+
+    ff1: FeedForwardParams
+    attn: AttentionParams
+    conv: ConvModuleParams
+    ff2: FeedForwardParams
+    post_norm_weight: np.ndarray   # (D,)
+    post_norm_bias: np.ndarray     # (D,)
+    post_ln_eps: float = 1e-5
+
+
+def make_block_params(seed: int, w_std: float = 0.02) -> BlockParams:
+    """Random-init parameters of one Conformer block (each part from its own seed: seed * 10 + part)."""
+    g = np.random.default_rng(seed)
+    return BlockParams(
+        ff1=make_ff_params(seed * 10 + 1, w_std=w_std), attn=make_attn_params(seed * 10 + 2, w_std=w_std),
+        conv=make_params(seed * 10 + 3, w_std=w_std), ff2=make_ff_params(seed * 10 + 4, w_std=w_std),
+        post_norm_weight=(1.0 + g.normal(0.0, 0.02, D_MODEL)).astype(np.float32),
+        post_norm_bias=g.normal(0.0, 0.02, D_MODEL).astype(np.float32))
+
+
 def make_activations(seed: int, shape: tuple[int, ...]) -> np.ndarray:
     """x ~ N(0, 1), float32."""
     return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)

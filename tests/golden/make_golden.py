@@ -16,7 +16,8 @@ What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/
 * ``ConformerFeedForward`` (``conformer.py:23-40``) as the block applies it, ``x + 0.5 * ff(x)``
   (``conformer.py:205``, ``:208``), in fp32 and bf16 on the test-fire shape;
 * ``ConformerAttention`` (``conformer.py:43-131``) as the block applies it, ``x + attn(x)`` (``conformer.py:206``),
-  in fp32 and bf16, whole and with each utterance trimmed to a length.
+  in fp32 and bf16, whole and with each utterance trimmed to a length;
+* a whole ``ConformerBlock`` (``conformer.py:190-210``, BatchNorm folded by ``fold_conv_bn_``) in fp32 and bf16.
 
 Inputs and parameters come from ``granite_conv_b200.synth`` (numpy PCG64 seeds), so the tests regenerate them
 bit-for-bit and only the reference outputs are stored.  bf16 tensors are stored as uint16 bit patterns.
@@ -189,6 +190,64 @@ def main(ref_root: str) -> None:
         np.savez_compressed(os.path.join(HERE, f"attn_b2_{tag}.npz"), bf16=_bits(yb), fp32=y32, lengths=lengths,
                             trimmed=np.concatenate([_bits(t) for t in y_trim], axis=0))
         out[f"attn_{tag}"] = tuple(yb.shape)
+
+    # ---- whole Conformer block: FF/2, attention, conv, FF/2, post norm (conformer.py:190-210) ----------------------
+    from models.granite_speech_nar.conformer import ConformerBlock  # noqa: E402
+    bp = synth.make_block_params(1301, w_std=0.02)
+    blk = ConformerBlock(EC())
+    with torch.no_grad():
+        for name, fp in (("ff1", bp.ff1), ("ff2", bp.ff2)):
+            ff = getattr(blk, name)
+            ff.pre_norm.weight.copy_(torch.from_numpy(fp.norm_weight))
+            ff.pre_norm.bias.copy_(torch.from_numpy(fp.norm_bias))
+            ff.up_proj.weight.copy_(torch.from_numpy(fp.up_weight))
+            ff.up_proj.bias.copy_(torch.from_numpy(fp.up_bias))
+            ff.down_proj.weight.copy_(torch.from_numpy(fp.down_weight))
+            ff.down_proj.bias.copy_(torch.from_numpy(fp.down_bias))
+        ap = bp.attn
+        blk.attn.pre_norm.weight.copy_(torch.from_numpy(ap.norm_weight))
+        blk.attn.pre_norm.bias.copy_(torch.from_numpy(ap.norm_bias))
+        blk.attn.to_q.weight.copy_(torch.from_numpy(ap.q_weight))
+        blk.attn.to_kv.weight.copy_(torch.from_numpy(ap.kv_weight))
+        blk.attn.to_out.weight.copy_(torch.from_numpy(ap.out_weight))
+        blk.attn.to_out.bias.copy_(torch.from_numpy(ap.out_bias))
+        blk.attn.rel_pos_emb.weight.copy_(torch.from_numpy(ap.rel_pos))
+        cp = bp.conv
+        m = blk.conv
+        m.norm.weight.copy_(torch.from_numpy(cp.norm_weight))
+        m.norm.bias.copy_(torch.from_numpy(cp.norm_bias))
+        m.up_conv.weight.copy_(torch.from_numpy(cp.up_weight)[:, :, None])
+        m.up_conv.bias.copy_(torch.from_numpy(cp.up_bias))
+        m.depth_conv.conv.weight.copy_(torch.from_numpy(cp.dw_weight)[:, None, :])
+        m.batch_norm.running_mean.copy_(torch.from_numpy(cp.bn_mean))
+        m.batch_norm.running_var.copy_(torch.from_numpy(cp.bn_var))
+        m.batch_norm.weight.copy_(torch.from_numpy(cp.bn_weight))
+        m.batch_norm.bias.copy_(torch.from_numpy(cp.bn_bias))
+        m.down_conv.weight.copy_(torch.from_numpy(cp.down_weight)[:, :, None])
+        m.down_conv.bias.copy_(torch.from_numpy(cp.down_bias))
+        blk.post_norm.weight.copy_(torch.from_numpy(bp.post_norm_weight))
+        blk.post_norm.bias.copy_(torch.from_numpy(bp.post_norm_bias))
+    blk.eval()
+    cs = blk.attn.context_size
+    seq = torch.arange(cs)
+    dists = torch.clamp(seq.view(-1, 1) - seq.view(1, -1), -cs, cs) + blk.attn.max_pos_emb
+    T = 237
+    x = synth.make_activations(1801, (2, T, synth.D_MODEL))
+    xf = torch.from_numpy(x)
+    b32 = ConformerBlock(EC())
+    b32.load_state_dict(blk.state_dict())
+    b32.eval()
+    assert fold(b32) == 1
+    y32 = b32(xf, attention_dists=dists).numpy()
+    bb = blk.to(torch.bfloat16)
+    assert fold(bb) == 1
+    xb = xf.to(torch.bfloat16)
+    yb = bb(xb, attention_dists=dists)
+    lengths = np.array([T, 150], dtype=np.int32)
+    y_trim = [bb(xb[b:b + 1, :L], attention_dists=dists)[0] for b, L in enumerate(lengths)]
+    np.savez_compressed(os.path.join(HERE, "block_b2_t237_w002.npz"), bf16=_bits(yb), fp32=y32, lengths=lengths,
+                        trimmed=np.concatenate([_bits(t) for t in y_trim], axis=0))
+    out["block_w002_t237"] = tuple(yb.shape)
 
     for k, v in out.items():
         print(f"{k}: {v}")

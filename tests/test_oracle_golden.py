@@ -152,3 +152,21 @@ def test_attention_block_oracle(tag, seed, w_std, T):
             assert s["rel_l2"] <= 5e-3 and s["worst_ratio"] <= 2.0, f"attention {tag} {what}: {s}"
     for b, L in enumerate(lens):   # padded frames: x + b_out
         np.testing.assert_array_equal(yl[b, L:], O.bf16_round(xb[b, L:] + prep["b_out"]))
+
+
+def test_conformer_block_oracle():
+    """A whole ConformerBlock: the block oracle (composition of the step oracles) against the reference block, fp32
+    within 1e-5 x max(1, |y|) and the bf16 form within the bf16 gates, whole and trimmed per utterance."""
+    from oracle import block as BK
+    g = _load("block_b2_t237_w002.npz")
+    p = synth.make_block_params(1301, w_std=0.02)
+    x = synth.make_activations(1801, (2, 237, synth.D_MODEL))
+    y32 = BK.conformer_block(x, BK.prepare_block(p, mode="fp32"), mode="fp32")
+    assert np.max(np.abs(y32 - g["fp32"])) <= TOL_FP32 * max(1.0, float(np.abs(g["fp32"]).max()))
+    prep = BK.prepare_block(p)
+    xb = O.bf16_round(x)
+    assert_bf16_close(BK.conformer_block(xb, prep), O.from_bf16_bits(g["bf16"]), "block oracle vs reference")
+    lens = g["lengths"]
+    yl = BK.conformer_block(xb, prep, lengths=lens)
+    valid = np.concatenate([yl[b, :L] for b, L in enumerate(lens)], axis=0)
+    assert_bf16_close(valid, O.from_bf16_bits(g["trimmed"]), "block oracle trimmed")
