@@ -13,7 +13,9 @@ Other workloads (single-GPU measurements): "module" = one conv module on one B=4
 the 128 grid), "module_i8" = the same with int8 weights, "dw" = the depthwise kernel alone on [48, 1024, 2048],
 "ff" = one feed-forward half on the same chunk, "attn" = one attention step (block-local, Shaw relative
 positions) on the same chunk, "block" = one whole Conformer block (FF/2, attention, conv, FF/2, post norm) on the
-same chunk, "encoder" = 16 Conformer blocks over the stack's 512 utterances (the encoder body).
+same chunk, "encoder" = 16 Conformer blocks over the stack's 512 utterances with the self-conditioning CTC head after
+block 8 and the BPE CTC head (100352-word vocabulary, argmax fused into the GEMM, CTC collapse) at the end, "ctc" =
+those heads alone on the B=48 chunk.
 
 ``--impl reference`` times the CPU oracle (numpy restatement of the reference eager module) on the host cores on a
 bounded sample of the same workload and prints the same JSON line with "impl": "reference".
@@ -138,7 +140,7 @@ def _workload_plan(rank: int, workload: str):
         lens = synth.sample_lengths(1005 + 7919 * rank, N_UTTS)
         return dispatch.plan_chunks(lens, exec_batch=dispatch.EXEC_BATCH, logical_batch=dispatch.LOGICAL_BATCH,
                                     frame_grid=dispatch.FRAME_GRID)
-    if workload in ("module", "module_i8", "ff", "attn", "block"):
+    if workload in ("module", "module_i8", "ff", "attn", "block", "ctc"):
         lens = synth.sample_lengths(1003 + 7919 * rank, 48)
         T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
         return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
@@ -169,6 +171,9 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
     elif workload in ("block", "encoder"):
         from oracle import block as BKO
         bkprep = BKO.prepare_block(synth.make_block_params(1008), mode="fp32")
+    elif workload == "ctc":
+        from oracle import ctc_head as CHO
+        chprep = CHO.prepare_ctc_fp32(synth.make_ctc_params(1009))
     else:
         params = synth.make_params(1005)
         prep = O.prepare_fp32(params)
@@ -191,6 +196,9 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
             ATO.attention_block(x, atprep, lengths=lens, mode="fp32", dtype=np.float32)
         elif workload in ("block", "encoder"):
             BKO.conformer_block(x, bkprep, lengths=lens, mode="fp32", dtype=np.float32)
+        elif workload == "ctc":
+            hh, bl = CHO.selfcond(x, chprep, lengths=lens, mode="fp32", dtype=np.float32)
+            CHO.decode(hh, bl, chprep, lengths=lens, mode="fp32")
         else:
             O.conv_module(x, prep, lengths=lens, mode="fp32", dtype=np.float32)
         frames += int(lens.sum())
@@ -245,8 +253,12 @@ def _config(args, world):
                 "chunk, lognormal lengths, T on the 128-frame grid, length mask",
         "block": "one Conformer block (FF/2, block-local Shaw attention, conv module, FF/2, post LayerNorm; 14 "
                  "launches), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
-        "encoder": "16 Conformer blocks (the encoder body: FF/2, attention, conv, FF/2, post norm per block), 512 "
-                   "utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid"}[w],
+        "encoder": "16 Conformer blocks (FF/2, attention, conv, FF/2, post norm per block) with the self-conditioning "
+                   "CTC head after block 8 and the BPE CTC head (V=100352, fused argmax, collapse) at the end, 512 "
+                   "utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid",
+        "ctc": "the encoder's CTC heads alone: self-conditioning (1024->348 GEMM, softmax, 348->1024 GEMM + residual), "
+               "posterior-weighted pooling by 4, BPE head 1024->100352 GEMM with the argmax in its epilogue, CTC "
+               "collapse; B=48 chunk, lognormal lengths, T on the 128-frame grid"}[w],
         "d_model": D, "d_inner": I, "kernel": 15, "layers": _layers_for(w),
         "utterances_per_rank": N_UTTS if w in ("stack", "encoder") else 48, "exec_batch": dispatch.EXEC_BATCH,
         "frame_grid": dispatch.FRAME_GRID, "parallelism": f"dp{world} (independent shards, no collective)",
@@ -302,11 +314,23 @@ def run_ours(args):
         from granite_conv_b200 import prepare_block_from_params
         layers = [prepare_block_from_params(synth.make_block_params(1008 + l), device=dev) for l in range(n_layers)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+    elif workload == "ctc":
+        layers = []
+        xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     else:
         # bf16: the LayerNorm folded into the up_conv GEMM (the module op's path for T on the 128 grid)
         layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8, ln_fold=not int8)
                   for l in range(n_layers)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+    heads = None
+    if workload in ("encoder", "ctc"):
+        from granite_conv_b200.weights import prepare_bpe_head_from_tensors, prepare_selfcond_from_tensors
+        cp = synth.make_ctc_params(1009)
+        bfh = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+        heads = (prepare_selfcond_from_tensors(bfh(cp.out_weight), bfh(cp.out_bias), bfh(cp.mid_weight),
+                                               bfh(cp.mid_bias), device=dev),
+                 prepare_bpe_head_from_tensors(bfh(cp.bpe_weight), bfh(cp.bpe_bias), cp.blank_id, cp.window,
+                                               device=dev))
     lens_dev = [torch.from_numpy(c.lengths).to(dev) for c in chunks]
     max_m = max(c.padded_frames for c in chunks)
     ws_bytes = int(L.gsn_conv_module_workspace_bytes(1, max_m, D, I))
@@ -323,6 +347,18 @@ def run_ours(args):
     # workspace has room for them
     w1b = torch.empty((2 * I, D), dtype=torch.bfloat16, device=dev) if int8 else None
     w2b = torch.empty((D, I), dtype=torch.bfloat16, device=dev) if int8 else None
+    if heads is not None:
+        from granite_conv_b200.ops import pooled_frames
+        hsc, hbpe = heads
+        sc_ws = torch.empty(int(L.gsn_ctc_selfcond_workspace_bytes(1, max_m, hsc.n_cls)), dtype=torch.uint8, device=dev)
+        blank_buf = torch.empty(max_m, dtype=torch.float32, device=dev)
+        max_pp = max(c.B * pooled_frames(c.T) for c in chunks)
+        pooled_buf = torch.empty((max_pp, D), dtype=torch.bfloat16, device=dev)
+        plen_buf = torch.empty(max(c.B for c in chunks), dtype=torch.int32, device=dev)
+        ids_buf = torch.empty(max_pp, dtype=torch.int32, device=dev)
+        tok_buf = torch.empty(max_pp, dtype=torch.int32, device=dev)
+        cnt_buf = torch.empty(max(c.B for c in chunks), dtype=torch.int32, device=dev)
+        key_ws = torch.empty(int(L.gsn_bpe_head_workspace_bytes(1, max_pp)), dtype=torch.uint8, device=dev)
     act = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]   # ping-pong buffers
     act2 = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
 
@@ -492,6 +528,29 @@ def run_ours(args):
             out.data_ptr(), D, p.post_ln_w.data_ptr(), p.post_ln_b.data_ptr(), out.data_ptr(), D, M, D, p.post_ln_eps,
             None, T, sp), "post ln"))
 
+    def selfcond_kernels(x, out, c, lens, record):
+        """gsn_ctc_selfcond_bf16 (three launches: the 1024->348 (padded 512) linear GEMM, the softmax, the 348
+        (padded 384) -> 1024 GEMM + residual), timed as one."""
+        nb = int(L.gsn_ctc_selfcond_workspace_bytes(c.B, c.T, hsc.n_cls))
+        timed("ctc.selfcond", c, record, lambda: _lib.check(L.gsn_ctc_selfcond_bf16(
+            x.data_ptr(), hsc.w_out.data_ptr(), hsc.b_out.data_ptr(), hsc.n_cls, hsc.w_mid.data_ptr(),
+            hsc.b_mid.data_ptr(), lens.data_ptr(), out.data_ptr(), blank_buf.data_ptr(), c.B, c.T, D,
+            sc_ws.data_ptr(), nb, sp), "selfcond"))
+
+    def decode_kernels(h, c, lens, record):
+        """gsn_bpe_pool_bf16 and gsn_bpe_head_ctc_bf16: pooling, the argmax GEMM (keys zeroed first), collapse."""
+        from granite_conv_b200.ops import pooled_frames
+        T = c.T
+        Pp = pooled_frames(T)
+        nb = int(L.gsn_bpe_head_workspace_bytes(c.B, Pp))
+        timed("ctc.pool", c, record, lambda: _lib.check(L.gsn_bpe_pool_bf16(
+            h.data_ptr(), blank_buf.data_ptr(), lens.data_ptr(), pooled_buf.data_ptr(), plen_buf.data_ptr(), c.B, T,
+            D, Pp, 4, sp), "pool"))
+        timed("ctc.head_argmax_collapse", c, record, lambda: _lib.check(L.gsn_bpe_head_ctc_bf16(
+            pooled_buf.data_ptr(), plen_buf.data_ptr(), hbpe.w.data_ptr(), hbpe.b.data_ptr(), hbpe.w.shape[0],
+            hbpe.blank_id, ids_buf.data_ptr(), tok_buf.data_ptr(), cnt_buf.data_ptr(), c.B, Pp, D, key_ws.data_ptr(),
+            nb, sp), "head"))
+
     dw_events = []
 
     def step(record=False):
@@ -523,10 +582,21 @@ def run_ours(args):
                     dst = act[ci]
                     block_kernels(src, dst, act2[ci], c, p, lens_dev[ci], record)
                     n += 14
+                    if heads is not None and li + 1 == len(layers) // 2:
+                        selfcond_kernels(dst, act2[ci], c, lens_dev[ci], record)
+                        dst = act2[ci]
+                        n += 3
                 else:
                     layer_kernels(src, dst, c, p, lens_dev[ci], record)
                     n += 4 if int8 else 3
                 src = dst
+            if workload == "ctc":
+                selfcond_kernels(xs[ci], act[ci], c, lens_dev[ci], record)
+                src = act[ci]
+                n += 3
+            if heads is not None:
+                decode_kernels(src, c, lens_dev[ci], record)
+                n += 3          # pool, argmax GEMM, collapse (+ the keys' memset, a driver kernel, not counted)
         return n
 
     def barrier():
@@ -581,7 +651,7 @@ def run_ours(args):
                 "traffic": None, "per_launch_ms": g1["ms_per_launch"], "algorithmic_flop_per_frame": FF_FLOP_PER_FRAME,
                 "frames_counted": "rows of the 128-row tiles holding valid frames",
                 "peak_source": f"bf16_tflops_sustained of {peaks['source']}", "kernels": kernels}
-    elif workload in ("block", "encoder"):
+    elif workload in ("block", "encoder", "ctc"):
         kernels = _named_breakdown(kev, peaks)
         top = max(kernels, key=lambda n: kernels[n]["share"])
         k = kernels[top]
@@ -619,7 +689,7 @@ def run_ours(args):
     e2e = None
     if workload != "dw" and not args.no_e2e:
         e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff",
-                   attn=workload == "attn", block=workload in ("block", "encoder"))
+                   attn=workload == "attn", block=workload in ("block", "encoder"), heads=heads)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -701,6 +771,13 @@ def _named_work(name, c):
         return "tensor", rows * OUT_FLOP_PER_FRAME
     if kind == "attention":
         return "tensor", _attn_query_keys(c) * ATTN_FLOP_PER_QUERY_KEY
+    if kind == "selfcond":
+        return "tensor", rows * (2 * D * 512 + 2 * 384 * D)
+    if kind == "pool":
+        return "hbm", c.valid_frames * (D * 2 + 4) + sum(-(-int(L) // 4) for L in c.lengths) * D * 2
+    if kind == "head_argmax_collapse":
+        prow = sum(-(-(-(-int(L) // 4)) // 128) * 128 for L in c.lengths)
+        return "tensor", prow * 2 * D * synth.BPE_VOCAB
     raise KeyError(name)
 
 
@@ -783,7 +860,7 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
     return out
 
 
-def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn=False, block=False):
+def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn=False, block=False, heads=None):
     """Same work through the public op (torch.ops.granite.conv_module per layer, or granite::feed_forward_half)
     with each chunk's input copied from pinned host memory and its output copied back inside the timed region."""
     import torch
@@ -795,17 +872,30 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
     elif attn:
         def stack(x, lengths):
             return ops.run_attention_block(x, layers[0], lengths)
+    elif block and heads is not None:
+        from granite_conv_b200 import ConformerEncoderStack
+        enc = ConformerEncoderStack(layers, selfcond=heads[0], selfcond_layer=len(layers) // 2)
+
+        def stack(x, lengths):            # the transcript: collapsed token ids (int32 [B, Pp]) come back
+            return enc.transcribe(x, heads[1], lengths)[1]
     elif block:
         from granite_conv_b200 import ConformerEncoderStack
         stack = ConformerEncoderStack(layers)
+    elif heads is not None:
+        def stack(x, lengths):
+            h, blank = ops.run_ctc_selfcond(x, heads[0], lengths)
+            return ops.run_bpe_ctc_decode(h, blank, heads[1], lengths)[1]
     else:
         stack = ConvModuleStack(layers, int8=int8)
     g = torch.Generator().manual_seed(4242)
     hx = [torch.randn((c.B, c.T, D), generator=g).to(torch.bfloat16).pin_memory() for c in chunks]
     hl = [torch.from_numpy(c.lengths).pin_memory() for c in chunks]
-    ho = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16).pin_memory() for c in chunks]
+    # the output of one call: bf16 [B, T, D] frames, or with the heads int32 [B, Pp] tokens
+    out_dtype = torch.bfloat16 if heads is None else torch.int32
+    ho = [torch.empty((c.B, c.T, D) if heads is None else (c.B, ops.pooled_frames(c.T)), dtype=out_dtype).pin_memory()
+          for c in chunks]
     h2d = sum(x.numel() * 2 + l.numel() * 4 for x, l in zip(hx, hl))
-    d2h = sum(o.numel() * 2 for o in ho)
+    d2h = sum(o.numel() * o.element_size() for o in ho)
 
     # copies run on their own streams so chunk i+1's upload and chunk i-1's download overlap chunk i's layers;
     # a chunk's device input is overwritten only after the previous step's compute of that chunk has finished.
@@ -870,7 +960,10 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
         valid = float(v.item())
     return {"value": valid * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
-            "path": ("ConformerEncoderStack (granite:: ops per step of each block)" if block else
+            "path": ("ConformerEncoderStack.transcribe (granite:: ops per step, CTC heads; tokens come back)"
+                     if block and heads is not None else
+                     "granite::ctc_selfcond + granite::bpe_ctc_decode (tokens come back)" if heads is not None else
+                     "ConformerEncoderStack (granite:: ops per step of each block)" if block else
                      "torch.ops.granite." + ("feed_forward_half" if ff else "attention_block" if attn else
                                              "conv_module per layer")) + ", pinned host in/out on two copy streams"}
 
@@ -881,8 +974,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff", "attn", "block", "encoder"],
-                    default="stack")
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff", "attn", "block", "encoder",
+                                           "ctc"], default="stack")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

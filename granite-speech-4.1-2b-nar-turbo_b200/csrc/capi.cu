@@ -513,6 +513,100 @@ int gsn_attention_block_bf16(const void* x, const void* ln_w, const void* ln_b, 
   return finish(launch_gemm(g2, kEpiResidual, st), name);
 }
 
+// ---- CTC heads ----------------------------------------------------------------------------------------------
+static int round_up_i(int v, int g) { return (v + g - 1) / g * g; }
+
+size_t gsn_ctc_selfcond_workspace_bytes(int B, int T, int n_cls) {
+  if (B <= 0 || T <= 0 || n_cls <= 0) return 0;
+  const size_t M = (size_t)B * (size_t)T;
+  return align256(M * (size_t)round_up_i(n_cls, 256) * 2) + align256(M * (size_t)round_up_i(n_cls, 64) * 2);
+}
+
+int gsn_ctc_selfcond_bf16(const void* h, const void* w_out, const float* b_out, int n_cls, const void* w_mid,
+                          const float* b_mid, const int32_t* lengths, void* h_out, float* blank, int B, int T, int D,
+                          void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  const char* name = "gsn_ctc_selfcond_bf16";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if (n_cls <= 0 || n_cls > 512) return fail(GSN_ERR_UNSUPPORTED, "%s: n_cls=%d (1..512)", name, n_cls);
+  if (D <= 0 || D % 256) return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d must be a multiple of 256", name, D);
+  if ((int64_t)B * T == 0) return ok();
+  if (!h || !w_out || !b_out || !w_mid || !b_mid || !h_out || !blank)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  const int M = B * T, n_pad = round_up_i(n_cls, 256), k_pad = round_up_i(n_cls, 64);
+  const size_t need = gsn_ctc_selfcond_workspace_bytes(B, T, n_cls);
+  if (!workspace || workspace_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
+  if (!aligned(workspace, 256) || !aligned(h, 16) || !aligned(h_out, 16) || !aligned(w_out, 16) ||
+      !aligned(w_mid, 16) || !aligned(b_out, 16) || !aligned(b_mid, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: tensors must be 16-byte aligned (workspace 256)", name);
+  __nv_bfloat16* logits = (__nv_bfloat16*)workspace;
+  __nv_bfloat16* probs = (__nv_bfloat16*)((char*)workspace + align256((size_t)M * n_pad * 2));
+  const cudaStream_t st = (cudaStream_t)stream;
+  const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
+  GemmArgs g1{(const __nv_bfloat16*)h, w_out, b_out, nullptr, nullptr, logits, (int64_t)n_pad, 0, M, n_pad, D, 0, skip,
+              T};
+  int rc = launch_gemm(g1, kEpiLinear, st);
+  if (rc) return finish(rc, name);
+  rc = launch_ctc_softmax(logits, n_pad, probs, k_pad, blank, M, n_cls, k_pad, lengths, T, st);
+  if (rc) return finish(rc, name);
+  // h_out = h + probs W_mid^T + b_mid (conformer.py:324)
+  GemmArgs g2{probs, w_mid, b_mid, nullptr, (const __nv_bfloat16*)h, (__nv_bfloat16*)h_out, D, D, M, D, k_pad, 0, skip,
+              T};
+  return finish(launch_gemm(g2, kEpiResidual, st), name);
+}
+
+int gsn_bpe_pool_bf16(const void* h, const float* blank, const int32_t* lengths, void* pooled, int32_t* pooled_lengths,
+                      int B, int T, int D, int Pp, int window, gsn_stream_t stream) {
+  const char* name = "gsn_bpe_pool_bf16";
+  if (B < 0 || T < 0 || window < 1 || window > 8)
+    return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d window=%d", name, B, T, window);
+  if (D <= 0 || D % 256) return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d must be a multiple of 256", name, D);
+  if ((int64_t)B * T == 0) return ok();
+  if (Pp < (T + window - 1) / window) return fail(GSN_ERR_INVALID_ARG, "%s: Pp=%d < ceil(T / window)", name, Pp);
+  if (!h || !blank || !pooled || !pooled_lengths) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!aligned(h, 16) || !aligned(pooled, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: 16-byte alignment", name);
+  return finish(launch_bpe_pool((const __nv_bfloat16*)h, blank, (__nv_bfloat16*)pooled, pooled_lengths, lengths, B, T,
+                                D, Pp, window, (cudaStream_t)stream),
+                name);
+}
+
+size_t gsn_bpe_head_workspace_bytes(int B, int Pp) {
+  if (B <= 0 || Pp <= 0) return 0;
+  return align256((size_t)B * (size_t)Pp * 8);
+}
+
+int gsn_bpe_head_ctc_bf16(const void* pooled, const int32_t* pooled_lengths, const void* w_bpe, const float* b_bpe,
+                          int V, int blank_id, int32_t* ids, int32_t* tokens, int32_t* counts, int B, int Pp, int D,
+                          void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  const char* name = "gsn_bpe_head_ctc_bf16";
+  if (B < 0 || Pp < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d Pp=%d", name, B, Pp);
+  if (V <= 0 || V % 256 || D <= 0 || D % 64)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: V=%d (multiple of 256) D=%d (multiple of 64)", name, V, D);
+  if ((int64_t)B * Pp == 0) return ok();
+  if (Pp % 128) return fail(GSN_ERR_UNSUPPORTED, "%s: Pp=%d must be a multiple of 128", name, Pp);
+  if (!pooled || !pooled_lengths || !w_bpe || !b_bpe || !ids || !tokens || !counts)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if ((int64_t)B * Pp > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*Pp too large", name);
+  const size_t need = gsn_bpe_head_workspace_bytes(B, Pp);
+  if (!workspace || workspace_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
+  if (!aligned(workspace, 256) || !aligned(pooled, 16) || !aligned(w_bpe, 16) || !aligned(b_bpe, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: tensors must be 16-byte aligned (workspace 256)", name);
+  const cudaStream_t st = (cudaStream_t)stream;
+  unsigned long long* keys = (unsigned long long*)workspace;
+  cudaError_t e = cudaMemsetAsync(keys, 0, (size_t)B * Pp * 8, st);
+  if (e != cudaSuccess) return cuda_fail((int)e, name);
+  const int M = B * Pp;
+  GemmArgs g{(const __nv_bfloat16*)pooled, w_bpe, b_bpe, nullptr, nullptr, nullptr, 0, 0, M, V, D, 0,
+             pooled_lengths, Pp};
+  g.argmax_keys = keys;
+  g.n_major = 1;
+  int rc = launch_gemm(g, kEpiArgmax, st);
+  if (rc) return finish(rc, name);
+  return finish(launch_ctc_collapse(keys, pooled_lengths, ids, tokens, counts, B, Pp, blank_id, st), name);
+}
+
 size_t gsn_conv_module_workspace_bytes(int B, int T, int D, int inner) {
   if (B <= 0 || T <= 0 || D <= 0 || inner <= 0) return 0;
   const size_t M = (size_t)B * (size_t)T;

@@ -59,6 +59,8 @@ struct KParams {
   int M, N, K;
   int T;                                  // frames per utterance when lengths != null (T % 128 == 0)
   float out_scale;                        // residual epilogue: out = out_scale * (acc * scale + bias) + residual
+  unsigned long long* argmax_keys;        // ARGMAX: per row, the best (bf16 logit, lowest column) as one key
+  int n_major;                            // walk tiles column block by column block (W read once)
 };
 
 // 128-row block `blk` of the M range holds at least one valid frame (a block lies inside one utterance)
@@ -80,6 +82,7 @@ constexpr int kMapMaxB = 512;
 
 struct TileMap {
   int num_n, num_tiles, active_tiles;
+  int n_major, act_m;         // n-major walk over the act_m active 128-row blocks
   int mpu, B;                 // 128-row blocks per utterance, utterances (with the map)
   const int* act;             // act[b]: active blocks of utterances < b (B + 1 entries)
   const int* pad;             // pad[b]: padding blocks of utterances < b
@@ -96,8 +99,14 @@ struct TileMap {
 
   // tile s -> (m_blk, n_blk); `active` false for a tile of pure padding (or past M)
   __device__ void get(int s, const KParams& p, int& m_blk, int& n_blk, bool& active) const {
-    const int mi = s / num_n;
-    n_blk = s - mi * num_n;
+    int mi;
+    if (n_major) {                // only the active tiles are walked this way
+      n_blk = s / act_m;
+      mi = s - n_blk * act_m;
+    } else {
+      mi = s / num_n;
+      n_blk = s - mi * num_n;
+    }
     if (!mapped) {
       m_blk = mi;
       active = rows_active(p, m_blk);
@@ -162,6 +171,8 @@ __device__ void build_tile_map(TileMap& tm, int* act, int* pad, const KParams& p
   }
   __syncthreads();
   tm.active_tiles = tm.mapped ? act[tm.B] * num_n : tm.num_tiles;
+  tm.act_m = tm.mapped ? act[tm.B] : num_m;
+  tm.n_major = p.n_major;
 }
 
 // Four signed int8 (one 32-bit word) -> two bf16x2 words, exactly.  Each byte is biased to unsigned
@@ -219,6 +230,8 @@ struct Epilogue {
   uint64_t* res0;                         // its barrier at res0 + b
   const CUtensorMap* tmO;
   const CUtensorMap* tmR;
+  unsigned long long* argmax_keys;
+  int M;
   bool has_res;
   int lane, swz;
   uint32_t su;                            // sub-tiles handled so far: buffer su & 1, its use count su >> 1
@@ -230,6 +243,8 @@ struct Epilogue {
     res0 = &e.res_full[ew][0];
     tmO = o;
     tmR = r;
+    argmax_keys = p.argmax_keys;
+    M = p.M;
     has_res = EPI == kEpiResidual && p.residual != nullptr;
     alpha = EPI == kEpiResidual ? p.out_scale : 1.0f;
     lengths = p.lengths;
@@ -277,6 +292,36 @@ struct Epilogue {
   // Drain one tile: `t_row` is the TMEM address of this warp's accumulator rows (unused when !active, i.e. a
   // residual tile of pure padding).  Returns false if a wait ran out.
   __device__ bool run(int row0, int ocol0, bool active, uint32_t t_row, volatile int* abort_flag) {
+    if constexpr (EPI == kEpiArgmax) {
+      // best bf16-rounded logit of this lane's row over the tile's 256 columns (first column on ties), folded
+      // into the row's key: (order-preserving bits of the value) << 32 | ~column, so atomicMax keeps the largest
+      // value and, among equal values, the lowest column
+      float best = -INFINITY;
+      int best_col = ocol0;
+      for (int u = 0; u < NU; ++u) {
+        uint32_t v[2][16];
+        tmem_ld16(t_row + (uint32_t)(u * BOX), v[0]);
+        tmem_ld16(t_row + (uint32_t)(u * BOX + 16), v[1]);
+        tmem_wait_ld_dep(v[0], v[1]);
+#pragma unroll
+        for (int k = 0; k < BOX; ++k) {
+          const float x = bf16_round_f32(__uint_as_float(v[k >> 4][k & 15]) + vb[u * BOX + k]);
+          if (x > best) {
+            best = x;
+            best_col = ocol0 + u * BOX + k;
+          }
+        }
+      }
+      const int row = row0 + lane;
+      if (row < M && best_col >= 0) {
+        uint32_t bits = __float_as_uint(best);
+        bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+        const unsigned long long key =
+            ((unsigned long long)bits << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)best_col);
+        atomicMax(argmax_keys + row, key);
+      }
+      return true;
+    }
     // SiLU: this lane's row is a padding frame -> zero, so the next GEMM sees what a masked input gives
     bool row_valid = true;
     if (EPI == kEpiSilu && lengths != nullptr) {
@@ -918,6 +963,7 @@ int encode_operands(const GemmArgs& a, int epilogue, int a_rows, int w_rows, CUt
                          dims, strides, box, a.w_int8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
+  if (tmO == nullptr) return 0;   // no output tensor (argmax epilogue)
   {
     // output (and residual) move as 32 x 32 bf16 boxes with the 64-byte swizzle
     const uint64_t dims[2] = {(uint64_t)(epilogue == kEpiGlu ? a.N / 2 : a.N), (uint64_t)a.M};
@@ -954,13 +1000,22 @@ KParams make_params(const GemmArgs& a) {
   p.K = a.K;
   p.T = a.T;
   p.out_scale = a.out_scale;
+  p.argmax_keys = a.argmax_keys;
+  p.n_major = a.n_major;
   return p;
 }
 
 template <int EPI, bool W_I8, bool SCALED>
 int launch_single(const GemmArgs& a, cudaStream_t stream) {
   CUtensorMap tmA, tmW, tmO, tmR;
-  if (int rc = encode_operands(a, EPI, BM, BN, &tmA, &tmW, &tmO, &tmR)) return rc;
+  if (EPI == kEpiArgmax) {
+    // no output tensor: the keys are written by atomics (the store maps are never read)
+    if (int rc = encode_operands(a, EPI, BM, BN, &tmA, &tmW, nullptr, nullptr)) return rc;
+    tmO = tmA;
+    tmR = tmA;
+  } else if (int rc = encode_operands(a, EPI, BM, BN, &tmA, &tmW, &tmO, &tmR)) {
+    return rc;
+  }
   const KParams p = make_params(a);
   const int smem = (int)sizeof(Smem<W_I8>) + 1024;
   auto kern = gemm_kernel<EPI, W_I8, SCALED>;
@@ -1065,6 +1120,10 @@ int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
   if (epilogue == kEpiLinear) {
     if (a.w_int8 || a.col_scale || a.residual) return (int)cudaErrorInvalidValue;
     return launch_single<kEpiLinear, false, false>(a, stream);
+  }
+  if (epilogue == kEpiArgmax) {
+    if (a.w_int8 || a.col_scale || a.residual || !a.argmax_keys) return (int)cudaErrorInvalidValue;
+    return launch_single<kEpiArgmax, false, false>(a, stream);
   }
   if (a.w_int8) return launch_single<kEpiResidual, true, true>(a, stream);
   return a.col_scale ? launch_single<kEpiResidual, false, true>(a, stream)

@@ -5,4 +5,5 @@
 #include "gemm_sm100.cu"
 #include "gemm_glu_dw_sm100.cu"
 #include "attention_sm100.cu"
+#include "ctc_head.cu"
 #include "capi.cu"

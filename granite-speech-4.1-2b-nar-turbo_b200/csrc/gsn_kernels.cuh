@@ -37,10 +37,13 @@ struct GemmArgs {
   const int* lengths;            // null, or per-utterance valid frames: 128-row tiles of pure padding are
   int T;                         //   skipped (GLU, SILU) or written as residual + bias (RESIDUAL); T % 128 == 0
   float out_scale = 1.0f;        // RESIDUAL: out = out_scale * (acc * col_scale + bias) + residual
+  unsigned long long* argmax_keys = nullptr;   // ARGMAX: [M] keys, zeroed by the caller
+  int n_major = 0;               // walk the tiles column block by column block (each W tile read once)
 };
 
 // LINEAR: out = acc + b, 128-row tiles of pure padding skipped (nothing written there)
-enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2, kEpiLinear = 3 };
+// ARGMAX: no output tensor; per row m, atomicMax(keys[m], (ordered bits of bf16(acc + b[n])) << 32 | ~n) over n
+enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2, kEpiLinear = 3, kEpiArgmax = 4 };
 
 int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
 // int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).
@@ -107,6 +110,14 @@ struct AttnArgs {
   float scale;
 };
 int launch_attention(const AttnArgs& args, cudaStream_t stream);
+
+// ---- CTC heads (ctc_head.cu) ----------------------------------------------------------------------------------
+int launch_ctc_softmax(const __nv_bfloat16* logits, int64_t ld_l, __nv_bfloat16* probs, int64_t ld_p, float* blank,
+                       int M, int C, int kpad, const int* lengths, int T, cudaStream_t stream);
+int launch_bpe_pool(const __nv_bfloat16* h, const float* blank, __nv_bfloat16* pooled, int* plen, const int* lengths,
+                    int B, int T, int D, int Pp, int window, cudaStream_t stream);
+int launch_ctc_collapse(const unsigned long long* keys, const int* plen, int* ids, int* tokens, int* counts, int B,
+                        int Pp, int blank_id, cudaStream_t stream);
 
 // ---- self-test of the bounded wait (capi.cu) ----------------------------------------------------------------
 int launch_wait_selftest(uint64_t limit_ns, cudaStream_t stream);

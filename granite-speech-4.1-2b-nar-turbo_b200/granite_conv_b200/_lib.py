@@ -53,6 +53,13 @@ SIGNATURES = {
                                        _f32, _vp]),
     "gsn_attention_block_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "gsn_gemm_linear_bf16": (_i32, [_vp, _vp, _fp, _vp, _i64, _i32, _i32, _i32, _vp, _i32, _vp]),
+    "gsn_ctc_selfcond_workspace_bytes": (_sz, [_i32, _i32, _i32]),
+    "gsn_ctc_selfcond_bf16": (_i32, [_vp, _vp, _fp, _i32, _vp, _fp, _vp, _vp, _fp, _i32, _i32, _i32, _vp, _sz,
+                                     _vp]),
+    "gsn_bpe_pool_bf16": (_i32, [_vp, _fp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "gsn_bpe_head_workspace_bytes": (_sz, [_i32, _i32]),
+    "gsn_bpe_head_ctc_bf16": (_i32, [_vp, _vp, _vp, _fp, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _sz,
+                                     _vp]),
     "gsn_attention_block_bf16": (_i32, [_vp, _vp, _vp, _f32, _vp, _fp, _vp, _fp, _vp, _i32, _vp, _vp, _i32, _i32,
                                         _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
     "gsn_gemm1_glu_bf16s": (_i32, [_vp, _vp, _fp, _fp, _vp, _i32, _i32, _i32, _vp, _i32, _vp]),

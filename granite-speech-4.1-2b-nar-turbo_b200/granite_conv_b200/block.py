@@ -69,18 +69,35 @@ def run_conformer_block(x: torch.Tensor, p: PreparedConformerBlock,
 
 
 class ConformerEncoderStack:
-    """Blocks applied in order (``CTCEncoder.forward``'s layer loop, ``conformer.py:317-318``, without the input
-    projection, self-conditioning and heads)."""
+    """Blocks applied in order (``CTCEncoder.forward``'s layer loop, ``conformer.py:317-318``; the input projection
+    is outside).  With ``selfcond`` (a PreparedSelfCond) the middle CTC head feeds back after block
+    ``selfcond_layer`` (1-based, ``conformer.py:320-324``); ``encode`` then also returns its blank probabilities."""
 
-    def __init__(self, blocks: Sequence[PreparedConformerBlock]):
+    def __init__(self, blocks: Sequence[PreparedConformerBlock], selfcond=None, selfcond_layer: Optional[int] = None):
         if not blocks:
             raise ValueError("empty stack")
         self.blocks = list(blocks)
+        self.selfcond = selfcond
+        self.selfcond_layer = selfcond_layer if selfcond_layer is not None else len(self.blocks) // 2
+
+    def encode(self, x: torch.Tensor, lengths: Optional[torch.Tensor] = None):
+        """(hidden, blank probabilities [B, T] fp32 or None)."""
+        blank = None
+        for i, p in enumerate(self.blocks, start=1):
+            x = run_conformer_block(x, p, lengths)
+            if self.selfcond is not None and i == self.selfcond_layer:
+                x, blank = ops.run_ctc_selfcond(x, self.selfcond, lengths)
+        return x, blank
 
     def __call__(self, x: torch.Tensor, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
-        for p in self.blocks:
-            x = run_conformer_block(x, p, lengths)
-        return x
+        return self.encode(x, lengths)[0]
+
+    def transcribe(self, x: torch.Tensor, head, lengths: Optional[torch.Tensor] = None):
+        """Encoder body, self-conditioning and the BPE CTC head: (ids, tokens, counts) as ``bpe_ctc_decode``."""
+        if self.selfcond is None:
+            raise ValueError("transcribe needs the self-conditioning head (its blank probabilities weight the pooling)")
+        h, blank = self.encode(x, lengths)
+        return ops.run_bpe_ctc_decode(h, blank, head, lengths)
 
     def run_chunks(self, chunks: Sequence[Tuple[torch.Tensor, Optional[torch.Tensor]]],
                    streams: Optional[Sequence[torch.cuda.Stream]] = None) -> List[torch.Tensor]:

@@ -17,6 +17,8 @@ plus the ops of the whole module (new):
 * ``granite::layer_norm(x, weight, bias, eps)`` (the block's post LayerNorm)
 * ``granite::attention_block(x, ln_w, ln_b, w_qkv, b_qkv, w_out, b_out, rel, lengths?, heads, context, max_pos,
   ln_eps)`` (x + ConformerAttention(x), block-local with Shaw relative positions)
+* ``granite::ctc_selfcond(x, w_out, b_out, w_mid, b_mid, lengths?, n_cls)`` -> (x', blank) (the middle CTC head)
+* ``granite::bpe_ctc_decode(x, blank, lengths?, w, b, blank_id, window)`` -> (ids, tokens, counts) (BPE head)
 
 All are ``mutates_args=()``, CUDA-only, launch on ``torch.cuda.current_stream()`` (as ``jit.py:180-181``) and
 have ``register_fake`` implementations whose strides equal the real outputs', so ``torch.compile(fullgraph=True)``
@@ -308,6 +310,83 @@ def attention_core(qkv: torch.Tensor, rel: torch.Tensor, heads: int, lengths: Op
               inner, _ptr(lens), B, T, heads, dh, context, max_pos, float(dh ** -0.5 if scale is None else scale),
               _stream(q))
     return ctx
+
+
+# ---- CTC heads: self-conditioning, BPE pooling + head + argmax + collapse --------------------------------------------
+@torch.library.custom_op("granite::ctc_selfcond", mutates_args=(), device_types="cuda")
+def ctc_selfcond(x: torch.Tensor, w_out: torch.Tensor, b_out: torch.Tensor, w_mid: torch.Tensor,
+                 b_mid: torch.Tensor, lengths: Optional[torch.Tensor], n_cls: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """The middle layer's self-conditioning (conformer.py:320-324): returns (x + out_mid(softmax(out(x))), blank
+    probability fp32 [B, T])."""
+    name = "granite::ctc_selfcond"
+    _require_cuda(name, x, w_out, b_out, w_mid, b_mid, lengths)
+    B, T, D = x.shape
+    xc = x.contiguous()
+    lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    out = torch.empty_like(xc)
+    blank = torch.empty((B, T), dtype=torch.float32, device=x.device)
+    nbytes = int(_lib.lib().gsn_ctc_selfcond_workspace_bytes(B, T, n_cls)) if B * T > 0 else 0
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    _lib.call("gsn_ctc_selfcond_bf16", xc.data_ptr(), w_out.data_ptr(), b_out.data_ptr(), n_cls, w_mid.data_ptr(),
+              b_mid.data_ptr(), _ptr(lens), out.data_ptr(), blank.data_ptr(), B, T, D, ws.data_ptr(), nbytes,
+              _stream(xc))
+    return out, blank
+
+
+@ctc_selfcond.register_fake
+def _(x, w_out, b_out, w_mid, b_mid, lengths, n_cls):
+    return torch.empty_like(x, memory_format=torch.contiguous_format), x.new_empty(x.shape[:2], dtype=torch.float32)
+
+
+def pooled_frames(T: int, window: int = 4) -> int:
+    """Rows per utterance of the pooled layout: ceil(T / window) rounded up to the 128-row tile."""
+    p = (T + window - 1) // window
+    return (p + 127) // 128 * 128
+
+
+@torch.library.custom_op("granite::bpe_ctc_decode", mutates_args=(), device_types="cuda")
+def bpe_ctc_decode(x: torch.Tensor, blank: torch.Tensor, lengths: Optional[torch.Tensor], w: torch.Tensor,
+                   b: torch.Tensor, blank_id: int, window: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Posterior-weighted pooling (conformer.py:214-226, :336-341), the BPE head with its argmax (conformer.py:342-355,
+    asr.py:123-134, the logits are never stored) and the CTC collapse (asr.py:76-102).  Returns (ids [B, Pp] int32,
+    -1 past each utterance's pooled frames; tokens [B, Pp] int32, the first counts[b] valid; counts [B] int32)."""
+    name = "granite::bpe_ctc_decode"
+    _require_cuda(name, x, blank, lengths, w, b)
+    B, T, D = x.shape
+    Pp = pooled_frames(T, window)
+    xc = x.contiguous()
+    lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+    pooled = torch.empty((B, Pp, D), dtype=torch.bfloat16, device=x.device)
+    plen = torch.empty((B,), dtype=torch.int32, device=x.device)
+    ids = torch.empty((B, Pp), dtype=torch.int32, device=x.device)
+    tokens = torch.empty((B, Pp), dtype=torch.int32, device=x.device)
+    counts = torch.empty((B,), dtype=torch.int32, device=x.device)
+    if B * T == 0:
+        return ids, tokens, counts.zero_()
+    st = _stream(xc)
+    _lib.call("gsn_bpe_pool_bf16", xc.data_ptr(), blank.contiguous().data_ptr(), _ptr(lens), pooled.data_ptr(),
+              plen.data_ptr(), B, T, D, Pp, window, st)
+    nbytes = int(_lib.lib().gsn_bpe_head_workspace_bytes(B, Pp))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    _lib.call("gsn_bpe_head_ctc_bf16", pooled.data_ptr(), plen.data_ptr(), w.data_ptr(), b.data_ptr(), w.shape[0],
+              blank_id, ids.data_ptr(), tokens.data_ptr(), counts.data_ptr(), B, Pp, D, ws.data_ptr(), nbytes, st)
+    return ids, tokens, counts
+
+
+@bpe_ctc_decode.register_fake
+def _(x, blank, lengths, w, b, blank_id, window):
+    B, T, _ = x.shape
+    Pp = pooled_frames(T, window)
+    i32 = torch.int32
+    return x.new_empty((B, Pp), dtype=i32), x.new_empty((B, Pp), dtype=i32), x.new_empty((B,), dtype=i32)
+
+
+def run_ctc_selfcond(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None):
+    return torch.ops.granite.ctc_selfcond(x, p.w_out, p.b_out, p.w_mid, p.b_mid, lengths, p.n_cls)
+
+
+def run_bpe_ctc_decode(x: torch.Tensor, blank: torch.Tensor, head, lengths: Optional[torch.Tensor] = None):
+    return torch.ops.granite.bpe_ctc_decode(x, blank, lengths, head.w, head.b, head.blank_id, head.window)
 
 
 def run_feed_forward_half(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:

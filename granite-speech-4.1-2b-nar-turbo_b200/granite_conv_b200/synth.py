@@ -171,6 +171,41 @@ def make_block_params(seed: int, w_std: float = 0.02) -> BlockParams:
         post_norm_bias=g.normal(0.0, 0.02, D_MODEL).astype(np.float32))
 
 
+CTC_CLASSES = 348       # EncoderConfig.output_dim
+BPE_VOCAB = 100352      # the BPE head's vocabulary: the LLM vocabulary (config.py:66), blank id 100257 inside it
+BPE_BLANK = 100257      # GraniteSpeechNarConfig.blank_token_id (config.py:103)
+
+
+@dataclass
+class CTCHeadParams:
+    """The encoder's CTC heads (``models/granite_speech_nar/conformer.py:240-252``): ``out`` (D -> C, the middle
+    layer's head), ``out_mid`` (C -> D, its feedback), ``out_bpe`` (D -> V).  All arrays are float32."""
+
+    out_weight: np.ndarray         # (C, D)
+    out_bias: np.ndarray           # (C,)
+    mid_weight: np.ndarray         # (D, C)
+    mid_bias: np.ndarray           # (D,)
+    bpe_weight: np.ndarray         # (V, D)
+    bpe_bias: np.ndarray           # (V,)
+    blank_id: int = BPE_BLANK
+    window: int = 4
+
+
+def make_ctc_params(seed: int, vocab: int = BPE_VOCAB, blank_id: int = BPE_BLANK, n_cls: int = CTC_CLASSES,
+                    d_model: int = D_MODEL, w_std: float = 0.02) -> CTCHeadParams:
+    """Random-init heads; the blank classes get a positive bias (blank is the most frequent CTC output)."""
+    g = np.random.default_rng(seed)
+    f32 = np.float32
+    out_b = g.normal(0.0, 0.02, n_cls).astype(f32)
+    out_b[0] += 1.0
+    bpe_b = g.normal(0.0, 0.02, vocab).astype(f32)
+    bpe_b[blank_id] += 3.5
+    return CTCHeadParams(
+        out_weight=g.normal(0.0, w_std * 3, (n_cls, d_model)).astype(f32), out_bias=out_b,
+        mid_weight=g.normal(0.0, w_std, (d_model, n_cls)).astype(f32), mid_bias=g.normal(0.0, 0.02, d_model).astype(f32),
+        bpe_weight=g.normal(0.0, w_std * 3, (vocab, d_model)).astype(f32), bpe_bias=bpe_b, blank_id=blank_id)
+
+
 def make_activations(seed: int, shape: tuple[int, ...]) -> np.ndarray:
     """x ~ N(0, 1), float32."""
     return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)

@@ -291,3 +291,71 @@ def prepare_attn_from_params(params, device="cuda") -> PreparedAttention:
                                      t(params.kv_weight), t(params.out_weight), t(params.out_bias),
                                      t(params.rel_pos), heads=params.heads, context=params.context,
                                      max_pos=params.max_pos, ln_eps=params.ln_eps, device=device)
+
+
+# ---- CTC heads ------------------------------------------------------------------------------------------------
+def _round_up(v: int, g: int) -> int:
+    return (v + g - 1) // g * g
+
+
+@dataclass
+class PreparedSelfCond:
+    """The middle layer's CTC head and its feedback (``conformer.py:240-241``, ``:320-324``), padded for the GEMMs:
+    ``w_out`` [round_up(C, 256), D] (rows >= C zero), ``w_mid`` [D, round_up(C, 64)] (columns >= C zero)."""
+
+    w_out: torch.Tensor         # bf16
+    b_out: torch.Tensor         # fp32 [round_up(C, 256)]
+    w_mid: torch.Tensor         # bf16
+    b_mid: torch.Tensor         # fp32 [D]
+    n_cls: int = 348
+
+
+@dataclass
+class PreparedBPEHead:
+    """The BPE CTC head ``out_bpe`` (``conformer.py:251-252``, ``:338-355``): ``w`` [round_up(V, 256), D] bf16 (padded
+    rows zero, their bias -inf so they never win the argmax), ``b`` fp32."""
+
+    w: torch.Tensor
+    b: torch.Tensor
+    vocab: int
+    blank_id: int
+    window: int = 4
+
+
+@torch.no_grad()
+def prepare_selfcond_from_tensors(out_w, out_b, mid_w, mid_b, device="cuda") -> PreparedSelfCond:
+    bf = torch.bfloat16
+    dev = torch.device(device)
+    C, D = out_w.shape
+    w_out = torch.zeros((_round_up(C, 256), D), dtype=bf, device=dev)
+    w_out[:C] = out_w.to(dev, bf)
+    b_out = torch.zeros(_round_up(C, 256), dtype=torch.float32, device=dev)
+    b_out[:C] = out_b.to(dev, bf).float()
+    w_mid = torch.zeros((D, _round_up(C, 64)), dtype=bf, device=dev)
+    w_mid[:, :C] = mid_w.to(dev, bf)
+    return PreparedSelfCond(w_out=w_out, b_out=b_out, w_mid=w_mid.contiguous(),
+                            b_mid=mid_b.to(dev, bf).float().contiguous(), n_cls=int(C))
+
+
+@torch.no_grad()
+def prepare_bpe_head_from_tensors(w, b, blank_id: int, window: int = 4, device="cuda") -> PreparedBPEHead:
+    bf = torch.bfloat16
+    dev = torch.device(device)
+    V, D = w.shape
+    Vp = _round_up(V, 256)
+    wp = torch.zeros((Vp, D), dtype=bf, device=dev)
+    wp[:V] = w.to(dev, bf)
+    bp = torch.full((Vp,), float("-inf"), dtype=torch.float32, device=dev)
+    bp[:V] = b.to(dev, bf).float()
+    return PreparedBPEHead(w=wp, b=bp, vocab=int(V), blank_id=int(blank_id), window=int(window))
+
+
+@torch.no_grad()
+def prepare_ctc_heads(encoder: nn.Module, device="cuda") -> tuple:
+    """(PreparedSelfCond, PreparedBPEHead) from a reference CTCEncoder (attributes out, out_mid, out_bpe, config)."""
+    sc = prepare_selfcond_from_tensors(encoder.out.weight, encoder.out.bias, encoder.out_mid.weight,
+                                       encoder.out_mid.bias, device=device)
+    head = prepare_bpe_head_from_tensors(encoder.out_bpe.weight, encoder.out_bpe.bias,
+                                         encoder.config.blank_token_id, encoder.config.bpe_pooling_window,
+                                         device=device)
+    return sc, head

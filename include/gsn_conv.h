@@ -247,6 +247,38 @@ int gsn_attention_block_bf16(const void* x, const void* ln_w, const void* ln_b, 
                              int dim_head, int context, int max_pos_emb, void* workspace, size_t workspace_bytes,
                              gsn_stream_t stream);
 
+/* ---- CTC heads ----------------------------------------------------------------------------------------------
+ * The encoder's heads around the Conformer stack (models/granite_speech_nar/conformer.py:320-355) and the CTC
+ * collapse of asr.py:76-102.  Frames are rows of [B, T, D] bf16; lengths (device int32 [B]) as elsewhere.
+ * gsn_ctc_selfcond_bf16: the self-conditioning of the middle layer (conformer.py:320-324): logits = h W_out^T + b_out
+ * over n_cls classes (bf16), p = softmax(float(logits)), blank[m] = p[m, 0] (fp32 [B*T]), h_out = h + bf16(p) W_mid^T
+ * + b_mid.  w_out [round_up(n_cls, 256), D] bf16 with rows >= n_cls zero, b_out [round_up(n_cls, 256)] fp32; w_mid
+ * [D, round_up(n_cls, 64)] bf16 with columns >= n_cls zero, b_mid [D] fp32; n_cls <= 512, D % 256 == 0.  Padding
+ * frames (t >= lengths[b]) get blank = 1.  Workspace: gsn_ctc_selfcond_workspace_bytes(B, T, n_cls), 256-aligned.
+ * gsn_bpe_pool_bf16: posterior_weighted_pool (conformer.py:214-226) with importance 1 - blank over windows of
+ * `window` frames, frames t >= lengths[b] left out; pooled [B, Pp, D] bf16 (Pp >= ceil(T / window); pooled frames
+ * past ceil(len / window) are zero), pooled_lengths[b] = ceil(len / window) (device int32 [B]).
+ * gsn_bpe_head_ctc_bf16: the BPE head out_bpe (conformer.py:338-355) and its argmax + collapse (asr.py:123-134):
+ * ids[b, p] = argmax_v bf16(pooled W_bpe^T + b_bpe) (lowest v among equal values; -1 past pooled_lengths[b]),
+ * tokens[b, 0:counts[b]] = the collapsed ids (a new id or the utterance's first, and not blank_id), -1 after.  The logits
+ * are never stored: the GEMM's epilogue keeps each row's best value.  w_bpe [V, D] bf16 (pad V to a multiple of
+ * 256 with rows of zeros and b_bpe = -inf), b_bpe [V] fp32; Pp % 128 == 0; ids, tokens [B, Pp] int32, counts [B].
+ * Workspace: gsn_bpe_head_workspace_bytes(B, Pp) bytes (one 64-bit key per pooled frame), 256-aligned. */
+size_t gsn_ctc_selfcond_workspace_bytes(int B, int T, int n_cls);
+
+int gsn_ctc_selfcond_bf16(const void* h, const void* w_out, const float* b_out, int n_cls, const void* w_mid,
+                          const float* b_mid, const int32_t* lengths, void* h_out, float* blank, int B, int T, int D,
+                          void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
+int gsn_bpe_pool_bf16(const void* h, const float* blank, const int32_t* lengths, void* pooled, int32_t* pooled_lengths,
+                      int B, int T, int D, int Pp, int window, gsn_stream_t stream);
+
+size_t gsn_bpe_head_workspace_bytes(int B, int Pp);
+
+int gsn_bpe_head_ctc_bf16(const void* pooled, const int32_t* pooled_lengths, const void* w_bpe, const float* b_bpe,
+                          int V, int blank_id, int32_t* ids, int32_t* tokens, int32_t* counts, int B, int Pp, int D,
+                          void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
 /* ---- whole module without any allocation ------------------------------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device memory where they run the module —
  * a plugin inside a host application that owns the GPU memory budget and its allocator, or a latency-critical

@@ -17,7 +17,9 @@ What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/
   (``conformer.py:205``, ``:208``), in fp32 and bf16 on the test-fire shape;
 * ``ConformerAttention`` (``conformer.py:43-131``) as the block applies it, ``x + attn(x)`` (``conformer.py:206``),
   in fp32 and bf16, whole and with each utterance trimmed to a length;
-* a whole ``ConformerBlock`` (``conformer.py:190-210``, BatchNorm folded by ``fold_conv_bn_``) in fp32 and bf16.
+* a whole ``ConformerBlock`` (``conformer.py:190-210``, BatchNorm folded by ``fold_conv_bn_``) in fp32 and bf16;
+* the encoder's CTC heads: ``CTCEncoder.forward`` (``conformer.py:284-361``) with an identity projection and block,
+  so the self-conditioning, pooling and BPE head run on the test input, then ``_collapse_ids_flat`` (``asr.py``).
 
 Inputs and parameters come from ``granite_conv_b200.synth`` (numpy PCG64 seeds), so the tests regenerate them
 bit-for-bit and only the reference outputs are stored.  bf16 tensors are stored as uint16 bit patterns.
@@ -248,6 +250,57 @@ def main(ref_root: str) -> None:
     np.savez_compressed(os.path.join(HERE, "block_b2_t237_w002.npz"), bf16=_bits(yb), fp32=y32, lengths=lengths,
                         trimmed=np.concatenate([_bits(t) for t in y_trim], axis=0))
     out["block_w002_t237"] = tuple(yb.shape)
+
+    # ---- CTC heads: CTCEncoder.forward's self-conditioning, pooling and BPE head (conformer.py:284-361), and the
+    # CTC collapse (asr.py:76-102).  The encoder gets an identity input projection and one identity block, so its
+    # hidden state is the test input; vocabulary 2048 (blank 7) to keep the fixture small.
+    from models.granite_speech_nar.conformer import CTCEncoder  # noqa: E402
+    from models.granite_speech_nar.asr import _collapse_ids_flat  # noqa: E402
+
+    class _Identity(torch.nn.Module):
+        def forward(self, x, **kwargs):
+            return x
+
+    V, blank = 2048, 7
+    cp = synth.make_ctc_params(1401, vocab=V, blank_id=blank)
+    cfg = EC(input_dim=synth.D_MODEL, num_layers=1, self_conditioning_layer=1, bpe_output_dim=V, blank_token_id=blank)
+    enc = CTCEncoder(cfg)
+    enc.layers = torch.nn.ModuleList([_Identity()])
+    with torch.no_grad():
+        enc.input_linear.weight.copy_(torch.eye(synth.D_MODEL))
+        enc.input_linear.bias.zero_()
+        enc.out.weight.copy_(torch.from_numpy(cp.out_weight))
+        enc.out.bias.copy_(torch.from_numpy(cp.out_bias))
+        enc.out_mid.weight.copy_(torch.from_numpy(cp.mid_weight))
+        enc.out_mid.bias.copy_(torch.from_numpy(cp.mid_bias))
+        enc.out_bpe.weight.copy_(torch.from_numpy(cp.bpe_weight))
+        enc.out_bpe.bias.copy_(torch.from_numpy(cp.bpe_bias))
+    enc.eval()
+    encb = enc.to(torch.bfloat16)
+    T = 37
+    x = synth.make_activations(1901, (2, T, synth.D_MODEL))
+    xb = torch.from_numpy(x).to(torch.bfloat16)
+    res = {}
+    lengths = np.array([T, 23], dtype=np.int32)
+    for tag, batch in (("whole", [(0, T), (1, T)]), ("trimmed", [(b, int(L)) for b, L in enumerate(lengths)])):
+        ids_all, logits_all, hid_all, seg = [], [], [], []
+        for b, L in batch:
+            o = encb(xb[b:b + 1, :L], attention_mask=torch.ones((1, L), dtype=torch.bool),
+                     output_hidden_states=False)
+            ids_all.append(o.logits.argmax(-1))
+            logits_all.append(o.logits)
+            hid_all.append(o.last_hidden_state[0])
+            seg.append(int(o.logits.shape[0]))
+        flat = torch.cat(ids_all)
+        toks, counts, _ = _collapse_ids_flat(flat, seg, blank)
+        res[f"{tag}_ids"] = flat.numpy().astype(np.int32)
+        res[f"{tag}_logits"] = _bits(torch.cat(logits_all))
+        res[f"{tag}_hidden"] = np.concatenate([_bits(h) for h in hid_all], axis=0)
+        res[f"{tag}_tokens"] = (torch.cat(toks).numpy().astype(np.int32) if sum(counts) else np.zeros(0, np.int32))
+        res[f"{tag}_counts"] = np.array(counts, dtype=np.int32)
+        res[f"{tag}_segments"] = np.array(seg, dtype=np.int32)
+    np.savez_compressed(os.path.join(HERE, "ctc_heads_b2_t37_v2048.npz"), lengths=lengths, **res)
+    out["ctc_heads"] = tuple(res["whole_ids"].shape)
 
     for k, v in out.items():
         print(f"{k}: {v}")

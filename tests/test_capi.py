@@ -133,3 +133,22 @@ def test_validation_of_attention_entry_points():
     assert blk(p, p, p, 1e-5, p, p, p, p, p, 1025, None, p, 2, 256, 768, 8, 128, 200, 512, p, ws, None) == 2
     assert blk(*([None] * 3), 1e-5, *([None] * 5), 1025, None, None, 0, 256, 1024, 8, 128, 200, 512, None, 0,
                None) == 0
+
+
+def test_validation_of_ctc_head_entry_points():
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    ws = L.gsn_ctc_selfcond_workspace_bytes(2, 128, 348)
+    assert ws == 2 * 128 * (512 * 2 + 384 * 2)
+    assert L.gsn_ctc_selfcond_bf16(p, p, p, 600, p, p, None, p, p, 2, 128, 1024, p, ws, None) == 2
+    assert L.gsn_ctc_selfcond_bf16(p, p, p, 348, p, p, None, p, p, 2, 128, 1000, p, ws, None) == 2
+    assert L.gsn_ctc_selfcond_bf16(p, p, p, 348, p, p, None, p, p, 2, 128, 1024, p, 100, None) == 5
+    assert L.gsn_ctc_selfcond_bf16(*([None] * 3), 348, None, None, None, None, None, 0, 128, 1024, None, 0, None) == 0
+    assert L.gsn_bpe_pool_bf16(p, p, None, p, p, 2, 128, 1024, 16, 4, None) == 1       # Pp < ceil(T / 4)
+    assert L.gsn_bpe_pool_bf16(p, p, None, p, p, 2, 128, 1024, 32, 9, None) == 1       # window too large
+    assert L.gsn_bpe_head_workspace_bytes(2, 128) == 2 * 128 * 8
+    head = L.gsn_bpe_head_ctc_bf16
+    assert head(p, p, p, p, 1000, 7, p, p, p, 2, 128, 1024, p, 4096, None) == 2         # V % 256
+    assert head(p, p, p, p, 1024, 7, p, p, p, 2, 100, 1024, p, 4096, None) == 2         # Pp % 128
+    assert head(p, p, p, p, 1024, 7, p, p, p, 2, 128, 1024, p, 100, None) == 5
+    assert head(None, None, None, None, 1024, 7, None, None, None, 0, 128, 1024, None, 0, None) == 0

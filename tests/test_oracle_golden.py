@@ -170,3 +170,35 @@ def test_conformer_block_oracle():
     yl = BK.conformer_block(xb, prep, lengths=lens)
     valid = np.concatenate([yl[b, :L] for b, L in enumerate(lens)], axis=0)
     assert_bf16_close(valid, O.from_bf16_bits(g["trimmed"]), "block oracle trimmed")
+
+
+def _margin_ok(logits_ref, ids_out, ids_ref):
+    """ids agree, or the reference's two best logits are within one bf16 ulp of each other (a near-tie that any
+    other summation order may flip)."""
+    top2 = np.sort(logits_ref, axis=-1)[:, -2:]
+    tie = (top2[:, 1] - top2[:, 0]) <= np.maximum(np.abs(top2[:, 1]), 1e-30) * 2.0 ** -7
+    return (ids_out == ids_ref) | tie
+
+
+def test_ctc_heads_oracle():
+    """Self-conditioning, pooling, BPE head argmax and collapse: the oracle against the reference CTCEncoder."""
+    from oracle import ctc_head as CH
+    g = _load("ctc_heads_b2_t37_v2048.npz")
+    p = synth.make_ctc_params(1401, vocab=2048, blank_id=7)
+    prep = CH.prepare_ctc_bf16(p)
+    x = O.bf16_round(synth.make_activations(1901, (2, 37, synth.D_MODEL)))
+    for tag, lens in (("whole", None), ("trimmed", g["lengths"])):
+        h, blank = CH.selfcond(x, prep, lengths=lens)
+        L = [37, 37] if lens is None else list(lens)
+        hv = np.concatenate([h[b, :n] for b, n in enumerate(L)], axis=0)
+        assert_bf16_close(hv, O.from_bf16_bits(g[f"{tag}_hidden"]), f"selfcond {tag}")
+        res, plen = CH.decode(h, blank, prep, lengths=lens)
+        assert list(plen) == list(g[f"{tag}_segments"])
+        ids = np.concatenate([r[0] for r in res])
+        lg_ref = O.from_bf16_bits(g[f"{tag}_logits"])
+        assert_bf16_close(np.concatenate([r[1] for r in res]), lg_ref, f"head logits {tag}")
+        assert _margin_ok(lg_ref, ids, g[f"{tag}_ids"]).all()
+        if (ids == g[f"{tag}_ids"]).all():
+            toks = np.concatenate([r[2] for r in res])
+            np.testing.assert_array_equal(toks, g[f"{tag}_tokens"])
+            np.testing.assert_array_equal([len(r[2]) for r in res], g[f"{tag}_counts"])
