@@ -23,8 +23,9 @@
 // barrel shift), adds, scales by scale * log2(e), masks, and writes the logits back over S.  A second pass turns
 // them into bf16 probabilities (row max subtracted, ex2) stored into TMEM columns 224..327 as packed pairs (over
 // the consumed Pos columns), the A operand of O = P V (V as an MN-major operand straight from its TMA tile, 13
-// MMAs of K = 16), which lands in columns 352..479 and is scaled by 1 / row sum on the way out.  With P in TMEM
-// the Q/K tiles are free as soon as the S / Pos MMAs finish, so the next unit's Q/K loads run under the softmax.
+// MMAs of K = 16), which lands in columns 0..127 (over the consumed S) and is scaled by 1 / row sum on the way out.
+// With P in TMEM the Q/K tiles are free as soon as the S / Pos MMAs finish, so the next unit's Q/K loads run under
+// the softmax, and the next unit's Pos MMAs are issued right behind P V, under this unit's output.
 //
 // Roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + single-thread MMA issuer, warps 2-9 softmax /
 // output: warp w reads TMEM lanes 32 (w % 4) ..; the two warps of a lane quarter take alternate key chunks and the
@@ -46,7 +47,7 @@ constexpr int PCOLS = 304;                 // positional columns c = r - j + 199
 constexpr int PN0 = 160, PN1 = PCOLS - PN0;
 constexpr int S_COL = 0, POS_COL = KEYS;
 constexpr int P_TCOL = 224;                // P: KEYS / 2 columns of packed bf16 pairs, over consumed Pos columns
-constexpr int O_COL = 352;
+constexpr int O_COL = 0;                   // O over the consumed S columns
 constexpr int EPI_WARPS = 8;
 constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int THREADS = 64 + EPI_THREADS;
@@ -59,7 +60,7 @@ constexpr int E_BOX_ROWS = PCOLS / 2;      // 152 (a TMA box has at most 256 row
 constexpr int E_BYTES = PCOLS * ROW_BYTES; // 38 KB per half
 constexpr int P_STEPS = KEYS / 16;         // 13 MMAs of K = 16 for O = P V
 static_assert(POS_COL + PCOLS == (int)TMEM_COLS, "S and the positional columns fill the tensor memory");
-static_assert(P_TCOL >= POS_COL && P_TCOL + KEYS / 2 <= O_COL && O_COL + DH <= (int)TMEM_COLS, "P, O placement");
+static_assert(P_TCOL >= POS_COL && P_TCOL + KEYS / 2 <= (int)TMEM_COLS && O_COL + DH <= POS_COL, "P, O placement");
 
 struct __align__(1024) Smem {
   uint8_t q[2][Q_BYTES];
@@ -68,7 +69,7 @@ struct __align__(1024) Smem {
   uint8_t e[2][E_BYTES];
   float red_max[2][BM];      // the two warps of a lane quarter: partial row max, partial row sum
   float red_sum[2][BM];
-  uint64_t qk_full, v_full, e_full, s_full, qk_free, p_full, o_full, v_free, tmem_free;
+  uint64_t qk_full, v_full, e_full, s_full, qk_free, p_full, o_full, v_free, tmem_free, mma_drain;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -146,6 +147,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&s.o_full, 1);
     mbar_init(&s.v_free, 1);
     mbar_init(&s.tmem_free, EPI_WARPS);
+    mbar_init(&s.mma_drain, 1);
     s.abort_flag = 0;
     fence_mbar_init();
   }
@@ -214,49 +216,55 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (one thread)
+    // Order per unit n: P V(n) -> Pos(n+1) -> [O(n) read out] -> S(n+1).  Pos(n+1) overwrites P(n), which P V(n)
+    // (issued before it by this thread) reads first; O lives over S, so only S(n+1) waits for the output.
     if (lane == 0) {
-      int n = 0, ne = 0, cur_q = -1;
-      uint64_t* last_commit = nullptr;
-      uint32_t last_parity = 0;
+      int ne = 0, cur_q = -1;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
-        const Unit x = decode(u, p);
-        if (!x.active) continue;
-        // P and O of the previous unit (columns 224..479, over Pos) have been read out
-        if (n > 0 && !mbar_wait_bounded(&s.tmem_free, (uint32_t)((n - 1) & 1), abort_flag, kStatusTimeoutMma)) {
-          ok = false;
-          break;
-        }
+      auto next_active = [&](int u) {
+        for (; u < p.n_units; u += gridDim.x)
+          if (decode(u, p).active) return u;
+        return p.n_units;
+      };
+      auto issue_pos = [&](const Unit& x, int n) -> bool {
         if (x.q != cur_q) {
           cur_q = x.q;
-          if (!mbar_wait_bounded(&s.e_full, (uint32_t)(ne & 1), abort_flag, kStatusTimeoutMma)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait_bounded(&s.e_full, (uint32_t)(ne & 1), abort_flag, kStatusTimeoutMma)) return false;
           ++ne;
         }
-        if (!mbar_wait_bounded(&s.qk_full, (uint32_t)(n & 1), abort_flag, kStatusTimeoutMma)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait_bounded(&s.qk_full, (uint32_t)(n & 1), abort_flag, kStatusTimeoutMma)) return false;
         tc_fence_after();
         for (int kh = 0; kh < 2; ++kh) {
           const uint64_t qd = make_sw128_kmajor_desc(smem_u32(s.q[kh]));
           const uint64_t e0 = make_sw128_kmajor_desc(smem_u32(s.e[kh]));
           const uint64_t e1 = make_sw128_kmajor_desc(smem_u32(s.e[kh] + PN0 * ROW_BYTES));
-          const uint64_t kd = make_sw128_kmajor_desc(smem_u32(s.k[kh]));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint32_t acc = (kh | k) != 0 ? 1u : 0u;
             umma_f16(tmem_base + POS_COL, qd + (uint64_t)(2 * k), e0 + (uint64_t)(2 * k), IDESC_P0, acc);
             umma_f16(tmem_base + POS_COL + PN0, qd + (uint64_t)(2 * k), e1 + (uint64_t)(2 * k), IDESC_P1, acc);
-            umma_f16(tmem_base + S_COL, qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), IDESC_S, acc);
           }
+        }
+        return true;
+      };
+      auto issue_s = [&]() {
+        for (int kh = 0; kh < 2; ++kh) {
+          const uint64_t qd = make_sw128_kmajor_desc(smem_u32(s.q[kh]));
+          const uint64_t kd = make_sw128_kmajor_desc(smem_u32(s.k[kh]));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem_base + S_COL, qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), IDESC_S, (kh | k) != 0 ? 1u : 0u);
         }
         umma_commit(&s.s_full);
         umma_commit(&s.qk_free);
-        last_commit = &s.qk_free;
-        last_parity = (uint32_t)(n & 1);
+      };
+      int u = next_active(blockIdx.x);
+      int n = 0;
+      if (u < p.n_units) {
+        ok = issue_pos(decode(u, p), 0);
+        if (ok) issue_s();
+      }
+      while (ok && u < p.n_units) {
         if (!mbar_wait_bounded(&s.p_full, (uint32_t)(n & 1), abort_flag, kStatusTimeoutMma) ||
             !mbar_wait_bounded(&s.v_full, (uint32_t)(n & 1), abort_flag, kStatusTimeoutMma)) {
           ok = false;
@@ -271,12 +279,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         umma_commit(&s.o_full);
         umma_commit(&s.v_free);
-        last_commit = &s.v_free;
+        const int un = next_active(u + gridDim.x);
+        if (un < p.n_units) {
+          if (!issue_pos(decode(un, p), n + 1) ||
+              !mbar_wait_bounded(&s.tmem_free, (uint32_t)(n & 1), abort_flag, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s();
+        }
+        u = un;
         ++n;
       }
-      if (!ok && last_commit != nullptr) {
+      if (!ok) {
         // the MMAs already issued finish before the tensor memory is released
-        mbar_wait_bounded(last_commit, last_parity, nullptr, kStatusTimeoutMma, 100000000ull);
+        umma_commit(&s.mma_drain);
+        mbar_wait_bounded(&s.mma_drain, 0, nullptr, kStatusTimeoutMma, 100000000ull);
       }
     }
   } else {
