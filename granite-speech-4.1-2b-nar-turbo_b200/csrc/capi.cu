@@ -143,7 +143,7 @@ int check_dw(const void* x, const void* w, const void* b, const void* y, int B, 
 int check_gemm(const char* name, const void* a, const void* w, const float* bias, const void* out, int M, int K,
                int N) {
   if (M < 0 || K <= 0 || N <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: bad sizes M=%d K=%d N=%d", name, M, K, N);
-  if (K % 64 != 0) return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d must be a multiple of 64", name, K);
+  if (K % 8 != 0) return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d must be a multiple of 8 (16-byte rows)", name, K);
   if (N % 256 != 0) return fail(GSN_ERR_UNSUPPORTED, "%s: N=%d must be a multiple of 256", name, N);
   if (M == 0) return -1;
   if (!a || !w || !bias || !out) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);

@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = p.N / BN;
-  const int num_kb = p.K / BK;
+  const int num_kb = (p.K + BK - 1) / BK;   // a partial last K-block is completed with zeros by TMA
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -1101,7 +1101,7 @@ int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* 
 
 int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
   if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale && (epilogue == kEpiGlu || epilogue == kEpiResidual) &&
-      a.out_scale == 1.0f) {
+      a.out_scale == 1.0f && a.K % BK == 0) {
     bool launched = false;
     const int rc = epilogue == kEpiGlu ? launch_pair<kEpiGlu>(a, stream, &launched)
                                        : launch_pair<kEpiResidual>(a, stream, &launched);

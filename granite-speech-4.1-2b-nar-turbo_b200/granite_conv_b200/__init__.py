@@ -10,6 +10,7 @@ from .conv_kernel import enable_dwconv_silu  # noqa: F401
 from .dispatch import Chunk, bucket_frames, plan_chunks, shard_chunks  # noqa: F401
 from .block import (ConformerEncoderStack, PreparedConformerBlock, prepare_block_from_params,  # noqa: F401
                     prepare_conformer_block, run_conformer_block)
+from .encoder import GraniteCTCEncoder  # noqa: F401
 from .stack import ConvModuleStack  # noqa: F401
 from .weights import (PreparedConvModule, fold_conv_bn_, glu_interleave, prepare_conv_module,  # noqa: F401
                       prepare_from_params, prepare_from_tensors, quantize_per_channel)

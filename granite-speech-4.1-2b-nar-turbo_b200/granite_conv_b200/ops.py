@@ -19,6 +19,7 @@ plus the ops of the whole module (new):
   ln_eps)`` (x + ConformerAttention(x), block-local with Shaw relative positions)
 * ``granite::ctc_selfcond(x, w_out, b_out, w_mid, b_mid, lengths?, n_cls)`` -> (x', blank) (the middle CTC head)
 * ``granite::bpe_ctc_decode(x, blank, lengths?, w, b, blank_id, window)`` -> (ids, tokens, counts) (BPE head)
+* ``granite::linear(x, w, b)`` (nn.Linear; the encoder's input projection)
 
 All are ``mutates_args=()``, CUDA-only, launch on ``torch.cuda.current_stream()`` (as ``jit.py:180-181``) and
 have ``register_fake`` implementations whose strides equal the real outputs', so ``torch.compile(fullgraph=True)``
@@ -387,6 +388,25 @@ def run_ctc_selfcond(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None)
 
 def run_bpe_ctc_decode(x: torch.Tensor, blank: torch.Tensor, head, lengths: Optional[torch.Tensor] = None):
     return torch.ops.granite.bpe_ctc_decode(x, blank, lengths, head.w, head.b, head.blank_id, head.window)
+
+
+@torch.library.custom_op("granite::linear", mutates_args=(), device_types="cuda")
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """x W^T + b on bf16 x [..., K] (K % 8 == 0), W bf16 [N, K] (N % 256 == 0), b fp32 [N] (nn.Linear, e.g. the
+    encoder's input projection, conformer.py:238, :289)."""
+    _require_cuda("granite::linear", x, w, b)
+    K = x.shape[-1]
+    N = w.shape[0]
+    x2 = x.contiguous().view(-1, K)
+    out = torch.empty((x2.shape[0], N), dtype=torch.bfloat16, device=x.device)
+    _lib.call("gsn_gemm_linear_bf16", x2.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(), N, x2.shape[0], K, N,
+              None, 0, _stream(x2))
+    return out.view(*x.shape[:-1], N)
+
+
+@linear.register_fake
+def _(x, w, b):
+    return x.new_empty((*x.shape[:-1], w.shape[0]))
 
 
 def run_feed_forward_half(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:

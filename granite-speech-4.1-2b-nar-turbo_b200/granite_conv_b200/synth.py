@@ -206,6 +206,16 @@ def make_ctc_params(seed: int, vocab: int = BPE_VOCAB, blank_id: int = BPE_BLANK
         bpe_weight=g.normal(0.0, w_std * 3, (vocab, d_model)).astype(f32), bpe_bias=bpe_b, blank_id=blank_id)
 
 
+INPUT_DIM = 160         # EncoderConfig.input_dim
+
+
+def make_input_params(seed: int, input_dim: int = INPUT_DIM, d_model: int = D_MODEL) -> tuple:
+    """The encoder's input projection (``conformer.py:238``): weight ~N(0, 1/sqrt(input_dim)), bias ~N(0, 0.02)."""
+    g = np.random.default_rng(seed)
+    w = g.normal(0.0, input_dim ** -0.5, (d_model, input_dim)).astype(np.float32)
+    return w, g.normal(0.0, 0.02, d_model).astype(np.float32)
+
+
 def make_activations(seed: int, shape: tuple[int, ...]) -> np.ndarray:
     """x ~ N(0, 1), float32."""
     return np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)

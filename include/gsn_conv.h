@@ -69,7 +69,7 @@ int gsn_layernorm_bf16(const void* x, int64_t ld_x, const void* gamma, const voi
  * v = (a[m,:] . W1[c,:]) + b1[c], g = (a[m,:] . W1[C+c,:]) + b1[C+c], C = N/2.
  * a: [M, K] bf16 contiguous; h: [M, N/2] bf16 contiguous.  w1_glu / b1_glu hold W1 and b1 with their rows
  * interleaved per 256-row block as [128 value rows | the matching 128 gate rows] (gsn_interleave_glu_rows).
- * K % 64 == 0, N % 256 == 0, pointers 16-byte aligned.  b1_glu is fp32.
+ * K % 8 == 0, N % 256 == 0, pointers 16-byte aligned.  b1_glu is fp32.
  * lengths: NULL, or int32[M / T] with T % 128 == 0: the rows are M / T utterances of T frames and 128-row tiles
  * made only of padding frames (t >= lengths[b]) are skipped, their rows of h left unwritten. */
 int gsn_gemm1_glu_bf16(const void* a, const void* w1_glu, const float* b1_glu, void* h, int M, int K, int N,
@@ -82,7 +82,7 @@ int gsn_gemm1_glu_i8w(const void* a, const void* w1q_glu, const float* s1_glu, c
 /* ---- pointwise_conv2 + residual -------------------------------------------------------------------------
  * Replaces down_conv (conformer.py:170, :187) plus the block's residual add (conformer.py:207):
  * out[m, n] = (d[m,:] . W2[n,:]) + b2[n] + residual[m, n].  d: [M, K] bf16; residual, out: [M, N] bf16 with
- * row strides ld_res, ld_out (multiples of 8); residual may be NULL (no add).  K % 64 == 0, N % 256 == 0.
+ * row strides ld_res, ld_out (multiples of 8); residual may be NULL (no add).  K % 8 == 0, N % 256 == 0.
  * b2 is fp32.  lengths / T as for gsn_gemm1_glu_bf16: 128-row tiles of pure padding skip the MMA and are written
  * as residual + b2 (what a zero row of d gives). */
 int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, const void* residual, int64_t ld_res,
@@ -192,7 +192,7 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
  * block's half-step residual x + 0.5 * ff(x) (conformer.py:205, :208).  Dropout is the identity (inference).
  * gsn_gemm_silu_bf16: h = silu(a W^T + b), a [M, K], W [N, K] bf16 (the Linear weight as stored), b [N] fp32;
  * lengths / T as for gsn_gemm1_glu_bf16: rows of pure-padding tiles are left unwritten, other padding rows are
- * written as zero (what a masked input gives).  K % 64, N % 256 == 0.
+ * written as zero (what a masked input gives).  K % 8, N % 256 == 0.
  * gsn_gemm_residual_scaled_bf16: out = out_scale * (d W^T + b) + residual (residual may be NULL), otherwise as
  * gsn_gemm2_residual_bf16.
  * gsn_ff_half_bf16: out = x + 0.5 * down(silu(up(layernorm(x)))) on x [B, T, D] bf16, w_up [F, D], w_down [D, F]
@@ -237,7 +237,8 @@ size_t gsn_attention_block_workspace_bytes(int B, int T, int D, int heads, int d
 
 /* gsn_gemm_linear_bf16: out = a W^T + b (a [M, K] bf16, W [N, K] bf16, b [N] fp32, out rows of stride ld_out); with
  * lengths (T % 128 == 0, M a multiple of T) the 128-row tiles made only of padding frames are skipped and left
- * unwritten.  The q|k|v projection of the attention step.  K % 64, N % 256 == 0. */
+ * unwritten.  The q|k|v projection of the attention step, the encoder's input projection (K = 160).  K % 8,
+ * N % 256 == 0. */
 int gsn_gemm_linear_bf16(const void* a, const void* w, const float* b, void* out, int64_t ld_out, int M, int K, int N,
                          const int32_t* lengths, int T, gsn_stream_t stream);
 

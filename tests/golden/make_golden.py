@@ -19,7 +19,8 @@ What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/
   in fp32 and bf16, whole and with each utterance trimmed to a length;
 * a whole ``ConformerBlock`` (``conformer.py:190-210``, BatchNorm folded by ``fold_conv_bn_``) in fp32 and bf16;
 * the encoder's CTC heads: ``CTCEncoder.forward`` (``conformer.py:284-361``) with an identity projection and block,
-  so the self-conditioning, pooling and BPE head run on the test input, then ``_collapse_ids_flat`` (``asr.py``).
+  so the self-conditioning, pooling and BPE head run on the test input, then ``_collapse_ids_flat`` (``asr.py``);
+* ``CTCEncoder.forward`` end to end with two Conformer blocks, from 160 input features to the BPE logits.
 
 Inputs and parameters come from ``granite_conv_b200.synth`` (numpy PCG64 seeds), so the tests regenerate them
 bit-for-bit and only the reference outputs are stored.  bf16 tensors are stored as uint16 bit patterns.
@@ -197,6 +198,17 @@ def main(ref_root: str) -> None:
     from models.granite_speech_nar.conformer import ConformerBlock  # noqa: E402
     bp = synth.make_block_params(1301, w_std=0.02)
     blk = ConformerBlock(EC())
+    _load_block(blk, bp)
+    blk.eval()
+    _block_golden(blk, bp, fold, out)
+    _ctc_goldens(EC, out)
+    _encoder_golden(EC, fold, out)
+
+    for k, v in out.items():
+        print(f"{k}: {v}")
+
+
+def _load_block(blk, bp):
     with torch.no_grad():
         for name, fp in (("ff1", bp.ff1), ("ff2", bp.ff2)):
             ff = getattr(blk, name)
@@ -229,7 +241,11 @@ def main(ref_root: str) -> None:
         m.down_conv.bias.copy_(torch.from_numpy(cp.down_bias))
         blk.post_norm.weight.copy_(torch.from_numpy(bp.post_norm_weight))
         blk.post_norm.bias.copy_(torch.from_numpy(bp.post_norm_bias))
-    blk.eval()
+
+
+def _block_golden(blk, bp, fold, out):
+    from models.granite_speech_nar.conformer import ConformerBlock  # noqa: E402
+    from models.granite_speech_nar.config import EncoderConfig as EC  # noqa: E402
     cs = blk.attn.context_size
     seq = torch.arange(cs)
     dists = torch.clamp(seq.view(-1, 1) - seq.view(1, -1), -cs, cs) + blk.attn.max_pos_emb
@@ -251,6 +267,8 @@ def main(ref_root: str) -> None:
                         trimmed=np.concatenate([_bits(t) for t in y_trim], axis=0))
     out["block_w002_t237"] = tuple(yb.shape)
 
+
+def _ctc_goldens(EC, out):
     # ---- CTC heads: CTCEncoder.forward's self-conditioning, pooling and BPE head (conformer.py:284-361), and the
     # CTC collapse (asr.py:76-102).  The encoder gets an identity input projection and one identity block, so its
     # hidden state is the test input; vocabulary 2048 (blank 7) to keep the fixture small.
@@ -302,8 +320,54 @@ def main(ref_root: str) -> None:
     np.savez_compressed(os.path.join(HERE, "ctc_heads_b2_t37_v2048.npz"), lengths=lengths, **res)
     out["ctc_heads"] = tuple(res["whole_ids"].shape)
 
-    for k, v in out.items():
-        print(f"{k}: {v}")
+
+def _encoder_golden(EC, fold, out):
+    """CTCEncoder.forward end to end (conformer.py:284-361): input projection from 160 features, two Conformer blocks,
+    the self-conditioning after block 1, the BPE head; BatchNorm folded as the reference loader does; bf16."""
+    from models.granite_speech_nar.conformer import CTCEncoder  # noqa: E402
+    from models.granite_speech_nar.asr import _collapse_ids_flat  # noqa: E402
+    V, blank = 2048, 7
+    cfg = EC(num_layers=2, self_conditioning_layer=1, bpe_output_dim=V, blank_token_id=blank)
+    enc = CTCEncoder(cfg)
+    w_in, b_in = synth.make_input_params(1501)
+    cp = synth.make_ctc_params(1502, vocab=V, blank_id=blank)
+    with torch.no_grad():
+        enc.input_linear.weight.copy_(torch.from_numpy(w_in))
+        enc.input_linear.bias.copy_(torch.from_numpy(b_in))
+        for i, layer in enumerate(enc.layers):
+            _load_block(layer, synth.make_block_params(1503 + i, w_std=0.02))
+        enc.out.weight.copy_(torch.from_numpy(cp.out_weight))
+        enc.out.bias.copy_(torch.from_numpy(cp.out_bias))
+        enc.out_mid.weight.copy_(torch.from_numpy(cp.mid_weight))
+        enc.out_mid.bias.copy_(torch.from_numpy(cp.mid_bias))
+        enc.out_bpe.weight.copy_(torch.from_numpy(cp.bpe_weight))
+        enc.out_bpe.bias.copy_(torch.from_numpy(cp.bpe_bias))
+    enc.eval()
+    enc = enc.to(torch.bfloat16)
+    assert fold(enc) == 2
+    T = 237
+    feats = synth.make_activations(1601, (2, T, synth.INPUT_DIM))
+    fb = torch.from_numpy(feats).to(torch.bfloat16)
+    res = {}
+    lengths = np.array([T, 150], dtype=np.int32)
+    for tag, batch in (("whole", [(0, T), (1, T)]), ("trimmed", [(b, int(L)) for b, L in enumerate(lengths)])):
+        ids_all, logits_all, hid_all, seg = [], [], [], []
+        for b, L in batch:
+            o = enc(fb[b:b + 1, :L], attention_mask=torch.ones((1, L), dtype=torch.bool), output_hidden_states=False)
+            ids_all.append(o.logits.argmax(-1))
+            logits_all.append(o.logits)
+            hid_all.append(o.last_hidden_state[0])
+            seg.append(int(o.logits.shape[0]))
+        flat = torch.cat(ids_all)
+        toks, counts, _ = _collapse_ids_flat(flat, seg, blank)
+        res[f"{tag}_ids"] = flat.numpy().astype(np.int32)
+        res[f"{tag}_logits"] = _bits(torch.cat(logits_all))
+        res[f"{tag}_hidden"] = np.concatenate([_bits(h) for h in hid_all], axis=0)
+        res[f"{tag}_tokens"] = (torch.cat(toks).numpy().astype(np.int32) if sum(counts) else np.zeros(0, np.int32))
+        res[f"{tag}_counts"] = np.array(counts, dtype=np.int32)
+        res[f"{tag}_segments"] = np.array(seg, dtype=np.int32)
+    np.savez_compressed(os.path.join(HERE, "encoder_l2_b2_t237_v2048.npz"), lengths=lengths, **res)
+    out["encoder_l2"] = tuple(res["whole_ids"].shape)
 
 
 if __name__ == "__main__":

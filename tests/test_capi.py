@@ -45,7 +45,7 @@ def test_validation_without_gpu():
     assert rc == 2 and "kernel size 14" in _lib.last_error()
     # GEMM shape constraints
     assert L.gsn_gemm1_glu_bf16(p, p, p, p, 128, 100, 4096, None, 0, None) == 2
-    assert "multiple of 64" in _lib.last_error()
+    assert "multiple of 8" in _lib.last_error()
     assert L.gsn_gemm2_residual_bf16(p, p, p, None, 0, p, 1024, 128, 2048, 1000, None, 0, None) == 2
     assert L.gsn_layernorm_bf16(p, 768, p, p, p, 768, 4, 768, 1e-5, None, 0, None) == 2
     # lengths need T on the 128-frame grid dividing M
@@ -99,7 +99,7 @@ def test_validation_of_fused_and_block_entry_points():
     assert L.gsn_ff_half_bf16(*([p] * 7), None, p, 2, 128, 1024, 4000, 1e-5, p, 1 << 30, None) == 2
     rc = L.gsn_ff_half_bf16(*([p] * 7), None, p, 2, 128, 1024, 4096, 1e-5, p, 100, None)
     assert rc == 5 and "workspace" in _lib.last_error()
-    assert L.gsn_gemm_silu_bf16(p, p, p, p, 128, 1000, 4096, None, 0, None) == 2
+    assert L.gsn_gemm_silu_bf16(p, p, p, p, 128, 1001, 4096, None, 0, None) == 2
     assert L.gsn_gemm_residual_scaled_bf16(p, p, p, None, 0, p, 1024, 128, 4096, 1000, 0.5, None, 0, None) == 2
     # int8 widening: sizes must be multiples of 16
     assert L.gsn_widen_i8_bf16(p, p, 17, None, None, 0, None) == 1

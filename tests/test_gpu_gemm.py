@@ -125,10 +125,10 @@ def test_gemm_int8_weights(M):
 
 
 def test_gemm_shape_errors():
-    a = torch.zeros((128, 100), dtype=torch.bfloat16, device=DEV)      # K not a multiple of 64
+    a = torch.zeros((128, 100), dtype=torch.bfloat16, device=DEV)      # K not a multiple of 8
     w = torch.zeros((256, 100), dtype=torch.bfloat16, device=DEV)
     b = torch.zeros((256,), dtype=torch.float32, device=DEV)
-    with pytest.raises(RuntimeError, match="multiple of 64"):
+    with pytest.raises(RuntimeError, match="multiple of 8"):
         ops.gemm1_glu(a, w, b)
     a = torch.zeros((128, 64), dtype=torch.bfloat16, device=DEV)
     w = torch.zeros((200, 64), dtype=torch.bfloat16, device=DEV)      # N not a multiple of 256
