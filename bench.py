@@ -13,9 +13,9 @@ Other workloads (single-GPU measurements): "module" = one conv module on one B=4
 the 128 grid), "module_i8" = the same with int8 weights, "dw" = the depthwise kernel alone on [48, 1024, 2048],
 "ff" = one feed-forward half on the same chunk, "attn" = one attention step (block-local, Shaw relative
 positions) on the same chunk, "block" = one whole Conformer block (FF/2, attention, conv, FF/2, post norm) on the
-same chunk, "encoder" = 16 Conformer blocks over the stack's 512 utterances with the self-conditioning CTC head after
-block 8 and the BPE CTC head (100352-word vocabulary, argmax fused into the GEMM, CTC collapse) at the end, "ctc" =
-those heads alone on the B=48 chunk.
+same chunk, "encoder" = the whole CTC encoder over the stack's 512 utterances: 160-dim input features projected
+to 1024, 16 Conformer blocks, the self-conditioning CTC head after block 8 and the BPE CTC head (100352-word
+vocabulary, argmax fused into the GEMM, CTC collapse) at the end, "ctc" = those heads alone on the B=48 chunk.
 
 ``--impl reference`` times the CPU oracle (numpy restatement of the reference eager module) on the host cores on a
 bounded sample of the same workload and prints the same JSON line with "impl": "reference".
@@ -253,9 +253,10 @@ def _config(args, world):
                 "chunk, lognormal lengths, T on the 128-frame grid, length mask",
         "block": "one Conformer block (FF/2, block-local Shaw attention, conv module, FF/2, post LayerNorm; 14 "
                  "launches), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
-        "encoder": "16 Conformer blocks (FF/2, attention, conv, FF/2, post norm per block) with the self-conditioning "
-                   "CTC head after block 8 and the BPE CTC head (V=100352, fused argmax, collapse) at the end, 512 "
-                   "utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid",
+        "encoder": "the whole CTC encoder: 160-dim features -> 1024 projection, 16 Conformer blocks (FF/2, attention, "
+                   "conv, FF/2, post norm) with the self-conditioning CTC head after block 8 and the BPE CTC head "
+                   "(V=100352, fused argmax, collapse) at the end; 512 utterances/rank, lognormal lengths, chunks<=48 "
+                   "on the 128-frame grid",
         "ctc": "the encoder's CTC heads alone: self-conditioning (1024->348 GEMM, softmax, 348->1024 GEMM + residual), "
                "posterior-weighted pooling by 4, BPE head 1024->100352 GEMM with the argmax in its epilogue, CTC "
                "collapse; B=48 chunk, lognormal lengths, T on the 128-frame grid"}[w],
@@ -314,6 +315,12 @@ def run_ours(args):
         from granite_conv_b200 import prepare_block_from_params
         layers = [prepare_block_from_params(synth.make_block_params(1008 + l), device=dev) for l in range(n_layers)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+        if workload == "encoder":       # the input features and the projection 160 -> 1024
+            feats = [torch.randn((c.B, c.T, synth.INPUT_DIM), generator=gen, device=dev).to(torch.bfloat16)
+                     for c in chunks]
+            wi, bi = synth.make_input_params(1010)
+            w_in = torch.from_numpy(wi).to(torch.bfloat16).to(dev)
+            b_in = torch.from_numpy(bi).to(torch.bfloat16).float().to(dev)
     elif workload == "ctc":
         layers = []
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
@@ -570,6 +577,12 @@ def run_ours(args):
                 n += 1
                 continue
             src = xs[ci]
+            if workload == "encoder":
+                x0 = xs[ci]
+                timed("input_linear", c, record, lambda: _lib.check(L.gsn_gemm_linear_bf16(
+                    feats[ci].data_ptr(), w_in.data_ptr(), b_in.data_ptr(), x0.data_ptr(), D, c.padded_frames,
+                    synth.INPUT_DIM, D, None, 0, sp), "input_linear"))
+                n += 1
             for li, p in enumerate(layers):
                 dst = act[ci] if li % 2 == 0 else act2[ci]
                 if workload == "ff":
@@ -771,6 +784,8 @@ def _named_work(name, c):
         return "tensor", rows * OUT_FLOP_PER_FRAME
     if kind == "attention":
         return "tensor", _attn_query_keys(c) * ATTN_FLOP_PER_QUERY_KEY
+    if name == "input_linear":
+        return "tensor", c.padded_frames * 2 * synth.INPUT_DIM * D
     if kind == "selfcond":
         return "tensor", rows * (2 * D * 512 + 2 * 384 * D)
     if kind == "pool":
@@ -873,11 +888,14 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
         def stack(x, lengths):
             return ops.run_attention_block(x, layers[0], lengths)
     elif block and heads is not None:
-        from granite_conv_b200 import ConformerEncoderStack
-        enc = ConformerEncoderStack(layers, selfcond=heads[0], selfcond_layer=len(layers) // 2)
+        from granite_conv_b200 import GraniteCTCEncoder
+        wi, bi = synth.make_input_params(1010)
+        genc = GraniteCTCEncoder(torch.from_numpy(wi).to(torch.bfloat16).to(dev),
+                                 torch.from_numpy(bi).to(torch.bfloat16).float().to(dev), layers, heads[0], heads[1],
+                                 selfcond_layer=len(layers) // 2)
 
-        def stack(x, lengths):            # the transcript: collapsed token ids (int32 [B, Pp]) come back
-            return enc.transcribe(x, heads[1], lengths)[1]
+        def stack(x, lengths):            # features in, the transcript (collapsed token ids, int32 [B, Pp]) back
+            return genc(x, lengths)["tokens"]
     elif block:
         from granite_conv_b200 import ConformerEncoderStack
         stack = ConformerEncoderStack(layers)
@@ -888,7 +906,8 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
     else:
         stack = ConvModuleStack(layers, int8=int8)
     g = torch.Generator().manual_seed(4242)
-    hx = [torch.randn((c.B, c.T, D), generator=g).to(torch.bfloat16).pin_memory() for c in chunks]
+    din = synth.INPUT_DIM if (block and heads is not None) else D       # the encoder takes the 160-dim features
+    hx = [torch.randn((c.B, c.T, din), generator=g).to(torch.bfloat16).pin_memory() for c in chunks]
     hl = [torch.from_numpy(c.lengths).pin_memory() for c in chunks]
     # the output of one call: bf16 [B, T, D] frames, or with the heads int32 [B, Pp] tokens
     out_dtype = torch.bfloat16 if heads is None else torch.int32
@@ -904,7 +923,7 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
     copy_in = torch.cuda.Stream(dev)
     copy_out = torch.cuda.Stream(dev)
     comp = [stream, torch.cuda.Stream(dev)]
-    xd = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
+    xd = [torch.empty((c.B, c.T, din), dtype=torch.bfloat16, device=dev) for c in chunks]
     ld = [torch.empty((c.B,), dtype=torch.int32, device=dev) for c in chunks]
     done = [None] * len(chunks)
 
@@ -960,7 +979,7 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
         valid = float(v.item())
     return {"value": valid * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
-            "path": ("ConformerEncoderStack.transcribe (granite:: ops per step, CTC heads; tokens come back)"
+            "path": ("GraniteCTCEncoder (features in, granite:: ops per step, CTC heads; tokens come back)"
                      if block and heads is not None else
                      "granite::ctc_selfcond + granite::bpe_ctc_decode (tokens come back)" if heads is not None else
                      "ConformerEncoderStack (granite:: ops per step of each block)" if block else
