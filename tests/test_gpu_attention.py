@@ -174,3 +174,32 @@ def test_attention_core_ignores_padding_rows():
     for b, L in enumerate(lens):
         assert_bf16_close(ctx[b, :L], ref[b, :L], f"b={b} L={L}")
         assert not ctx[b, L:].any()
+
+
+@pytest.mark.parametrize("heads", [2, 4])
+def test_attention_core_other_head_counts(heads):
+    """The kernel walks (query tile, utterance, block, head) units for any head count: 2 and 4 heads of 128."""
+    B, T = 2, 437
+    inner = heads * DH
+    g = np.random.default_rng(40 + heads)
+    qkv = O.bf16_round(np.concatenate([g.normal(0, 0.3, (B, T, inner)), g.normal(0, 0.3, (B, T, inner)),
+                                       g.normal(0, 1.0, (B, T, inner))], axis=-1).astype(np.float32))
+    rel = _rel(41)
+    lens = np.array([T, 250], dtype=np.int32)
+    ctx = ops.attention_core(_t(qkv), _t(rel), heads, torch.from_numpy(lens).to(DEV)).float().cpu().numpy()
+    for b, L in enumerate(lens):
+        q, k, v = qkv[b, :L, :inner], qkv[b, :L, inner:2 * inner], qkv[b, :L, 2 * inner:]
+        ref = AT.attention_core(q, k, v, rel, heads, synth.CONTEXT, synth.MAX_POS_EMB, mode="fp32")
+        assert_bf16_close(ctx[b, :L], ref, f"heads={heads} b={b}")
+        assert not ctx[b, L:].any()
+
+
+def test_attention_block_d512_four_heads():
+    """The attention step at D = 512 with 4 heads of 128 (the LayerNorm and both GEMMs at that width)."""
+    params = synth.make_attn_params(77, d_model=512, heads=4, w_std=0.03)
+    p = prepare_attn_from_params(params, device=DEV)
+    x = O.bf16_round(synth.make_activations(78, (2, 384, 512)))
+    lens = np.array([384, 190], dtype=np.int32)
+    y = ops.run_attention_block(_t(x), p, torch.from_numpy(lens).to(DEV))
+    ref = AT.attention_block(x, AT.prepare_attn_bf16(params), lengths=lens, mode="reference")
+    assert_bf16_close(y, ref, "attention block D=512 heads=4")
