@@ -14,7 +14,10 @@
 //    zero-filled, through a 3-stage ring: the load of tile i + 3 is issued as soon as tile i has been consumed.  A
 //    warp owns FPW output frames, a lane CPT channels (conflict-free shared-memory rows), with the 15 x CPT weights
 //    in registers and packed fp32x2 FMAs.  Tiles entirely inside the utterance take an unmasked path, tiles past
-//    its end skip their load, and a CTA whose frames are all padding only writes zeros.
+//    its end skip their load, and a CTA whose frames are all padding only writes zeros.  Two tile shapes: without
+//    lengths a lane owns 2 channels x 32 frames (46 staged rows feed 32 outputs, so fewer bf16 unpacks and shared
+//    loads per output); with lengths, and in the GLU form, 4 channels x 8 frames (short tiles waste less work past
+//    an utterance's end).  Both accumulate every output in the same order, so they agree bit for bit.
 //  * channels-first (element stride of T is 1; the layout the reference op receives from up_conv): a CTA owns 32
 //    channels x 128 frames, stages the rows (plus halo) in shared memory as fp32 with plain coalesced loads
 //    (row strides need not be 16-byte multiples there, e.g. T = 37), and transposes the result through shared
@@ -23,27 +26,6 @@
 
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
-
-// Tile shape of the channels-last kernel (compile-time: channels per lane, frames per warp, warps per CTA, time
-// tiles per CTA).
-#ifndef GSN_DW_CPT
-#define GSN_DW_CPT 4
-#endif
-#ifndef GSN_DW_FPW
-#define GSN_DW_FPW 8
-#endif
-#ifndef GSN_DW_WARPS
-#define GSN_DW_WARPS 4
-#endif
-#ifndef GSN_DW_SEG
-#define GSN_DW_SEG 8
-#endif
-#ifndef GSN_DW_STAGES
-#define GSN_DW_STAGES 3
-#endif
-#ifndef GSN_DW_MIN_CTAS            // resident CTAs per SM the register allocation must allow
-#define GSN_DW_MIN_CTAS 4
-#endif
 
 namespace gsn {
 
@@ -54,22 +36,36 @@ constexpr int HALO = 7;
 
 // ----------------------------------------------------------------------------------------------------------------
 // channels-last
-template <int CPT, int FPW, int WARPS, bool GLU>
+
+// Tile shape: channels per lane, frames per warp, warps per CTA, time tiles per CTA, and the resident CTAs per SM
+// the register allocation must allow.
+template <int CPT_, int FPW_, int WARPS_, int SEG_, int MINB_>
+struct ClShape {
+  static constexpr int CPT = CPT_, FPW = FPW_, WARPS = WARPS_, SEG = SEG_, MINB = MINB_;
+};
+using ShapeDense = ClShape<2, 32, 2, 4, 6>;    // no lengths: 64 channels x 64 frames per tile, 146 registers
+using ShapeMasked = ClShape<4, 8, 4, 8, 4>;    // lengths or GLU: 128 channels x 32 frames per tile
+
+template <class S, bool GLU>
 struct ClCfg {
+  static constexpr int CPT = S::CPT;
+  static constexpr int FPW = S::FPW;
+  static constexpr int WARPS = S::WARPS;
   static constexpr int NP = CPT / 2;               // fp32 pairs per lane
   static constexpr int CC = 32 * CPT;              // channels per tile
   static constexpr int TT = FPW * WARPS;           // output frames per tile
   static constexpr int ROWS = TT + 2 * HALO;       // staged rows
   static constexpr int ROW_BYTES = CC * 2;
   static constexpr int TILE_BYTES = ROWS * ROW_BYTES;
-  static constexpr int STAGES = GSN_DW_STAGES;
+  static constexpr int STAGES = 3;
   static constexpr int THREADS = 32 * WARPS;
-  static constexpr int TILES = GSN_DW_SEG;         // consecutive time tiles per CTA
+  static constexpr int TILES = S::SEG;             // consecutive time tiles per CTA
+  static constexpr int MIN_CTAS = GLU ? 3 : S::MINB;
 };
 
-template <int CPT, int FPW, int WARPS, bool GLU>
+template <class S, bool GLU>
 struct __align__(128) ClSmem {
-  using C = ClCfg<CPT, FPW, WARPS, GLU>;
+  using C = ClCfg<S, GLU>;
   uint8_t x[C::STAGES][GLU ? 2 : 1][C::TILE_BYTES];
   uint64_t full[C::STAGES];
   int abort_flag;
@@ -143,16 +139,18 @@ __device__ __forceinline__ void stg_words(__nv_bfloat16* p, const uint32_t (&w)[
   }
 }
 
-template <int CPT, int FPW, int WARPS, bool GLU>
-__global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
+template <class S, bool GLU>
+__global__ void __launch_bounds__(ClCfg<S, GLU>::THREADS, ClCfg<S, GLU>::MIN_CTAS)
     dwconv_cl_kernel(const __grid_constant__ CUtensorMap tmX, ClParams p) {
-  using Cfg = ClCfg<CPT, FPW, WARPS, GLU>;
+  using Cfg = ClCfg<S, GLU>;
+  constexpr int CPT = Cfg::CPT;
+  constexpr int FPW = Cfg::FPW;
+  constexpr int WARPS = Cfg::WARPS;
   constexpr int NP = Cfg::NP;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int TT = Cfg::TT;
   extern __shared__ uint8_t smem_raw[];
-  auto& s = *reinterpret_cast<ClSmem<CPT, FPW, WARPS, GLU>*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                                             ~uintptr_t(127));
+  auto& s = *reinterpret_cast<ClSmem<S, GLU>*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -310,9 +308,9 @@ __global__ void __launch_bounds__(32 * WARPS, GLU ? 3 : GSN_DW_MIN_CTAS)
   }
 }
 
-template <int CPT, int FPW, int WARPS, bool GLU>
+template <class S, bool GLU>
 int launch_cl(const DwArgs& a, cudaStream_t stream) {
-  using Cfg = ClCfg<CPT, FPW, WARPS, GLU>;
+  using Cfg = ClCfg<S, GLU>;
   CUtensorMap tm;
   const uint64_t cx = (uint64_t)a.C * (GLU ? 2 : 1);
   const uint64_t dims[3] = {cx, (uint64_t)a.T, (uint64_t)a.B};
@@ -331,8 +329,8 @@ int launch_cl(const DwArgs& a, cudaStream_t stream) {
   p.C = a.C;
   const int64_t t_chunks = ((int64_t)a.T + Cfg::TT * Cfg::TILES - 1) / (Cfg::TT * Cfg::TILES);
   if (t_chunks > 65535 || a.B > 65535) return (int)cudaErrorInvalidValue;
-  auto kern = dwconv_cl_kernel<CPT, FPW, WARPS, GLU>;
-  const int smem = (int)sizeof(ClSmem<CPT, FPW, WARPS, GLU>) + 128;
+  auto kern = dwconv_cl_kernel<S, GLU>;
+  const int smem = (int)sizeof(ClSmem<S, GLU>) + 128;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   dim3 grid(a.C / Cfg::CC, (unsigned)t_chunks, a.B);
@@ -435,15 +433,17 @@ using namespace dw_impl;
 
 int launch_dwconv(const DwArgs& a, cudaStream_t stream) {
   if (a.B == 0 || a.T == 0 || a.C == 0) return 0;
-  constexpr int CC = ClCfg<GSN_DW_CPT, GSN_DW_FPW, GSN_DW_WARPS, false>::CC;
-  const bool cl = (a.sxC == 1 && a.syC == 1 && (a.C % CC) == 0 && (a.sxT % 8) == 0 && (a.sxB % 8) == 0 &&
-                   (a.syT % GSN_DW_CPT) == 0 && (a.syB % GSN_DW_CPT) == 0 &&
-                   (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
-                   (reinterpret_cast<uintptr_t>(a.y) & (2 * GSN_DW_CPT - 1)) == 0);
-  if (cl) {
-    return a.glu ? launch_cl<GSN_DW_CPT, GSN_DW_FPW, GSN_DW_WARPS, true>(a, stream)
-                 : launch_cl<GSN_DW_CPT, GSN_DW_FPW, GSN_DW_WARPS, false>(a, stream);
-  }
+  // the channels-last kernel of shape S applies when both tensors are channels-last with 16-byte aligned frame rows
+  // in x, C a multiple of the tile's channels and y's lane stores (CPT bf16) aligned
+  auto cl_ok = [&](auto shape) {
+    using Cfg = ClCfg<decltype(shape), false>;
+    return a.sxC == 1 && a.syC == 1 && (a.C % Cfg::CC) == 0 && (a.sxT % 8) == 0 && (a.sxB % 8) == 0 &&
+           (a.syT % Cfg::CPT) == 0 && (a.syB % Cfg::CPT) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(a.y) & (2 * Cfg::CPT - 1)) == 0;
+  };
+  if (!a.glu && !a.lengths && cl_ok(ShapeDense{})) return launch_cl<ShapeDense, false>(a, stream);
+  if (cl_ok(ShapeMasked{}))
+    return a.glu ? launch_cl<ShapeMasked, true>(a, stream) : launch_cl<ShapeMasked, false>(a, stream);
   CfParams p{a.x, a.w, a.bias, a.y, a.lengths, a.sxB, a.sxC, a.sxT, a.syB, a.syC, a.syT, a.C, a.T};
   dim3 grid((a.T + CF_TT - 1) / CF_TT, (a.C + CF_CC - 1) / CF_CC, a.B);
   if (a.glu)

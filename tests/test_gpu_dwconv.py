@@ -103,6 +103,26 @@ def test_dwconv_lengths(layout):
         np.testing.assert_array_equal(yi.transpose(1, 2)[0].float().cpu().numpy(), yb[i, :L])
 
 
+@pytest.mark.parametrize("C,T", [(2048, 1024), (192, 261), (64, 37)])
+def test_dwconv_tile_shapes_agree(C, T):
+    """Without lengths the channels-last kernel runs 64-channel x 64-frame tiles; with lengths (all frames valid here)
+    128-channel x 32-frame tiles.  Both accumulate in the same order: equal bit for bit.  C = 192 and 64 reach the
+    first shape only (not a multiple of 128 channels); they are checked against the oracle."""
+    B = 3
+    w, b = _dw_params(C, seed=80)
+    x_btc = O.bf16_round(synth.make_activations(6161 + C, (B, T, C)))
+    xt = _bf(x_btc).to(DEV)
+    wt, bt = _bf(w)[:, None, :].to(DEV), _bf(b).to(DEV)
+    y = torch.ops.granite.dwconv_silu(xt.transpose(1, 2), wt, bt)
+    assert y.stride() == (T * C, 1, C)
+    if C % 128 == 0:
+        full = torch.full((B,), T, dtype=torch.int32, device=DEV)
+        ym = torch.ops.granite.dwconv_silu_masked(xt.transpose(1, 2), wt, bt, full)
+        assert torch.equal(y, ym)
+    else:
+        assert_bf16_close(y.transpose(1, 2), O.dwconv_silu(x_btc, w, b), f"dw C={C} T={T}")
+
+
 def test_dwconv_generic_strides_and_odd_channels():
     """C not a multiple of the channels-last tile and a non-dense view take the generic path."""
     C, T, B = 96, 50, 2
