@@ -43,7 +43,7 @@ template <int CPT_, int FPW_, int WARPS_, int SEG_, int MINB_>
 struct ClShape {
   static constexpr int CPT = CPT_, FPW = FPW_, WARPS = WARPS_, SEG = SEG_, MINB = MINB_;
 };
-using ShapeDense = ClShape<2, 32, 2, 4, 6>;    // no lengths: 64 channels x 64 frames per tile, 146 registers
+using ShapeDense = ClShape<2, 32, 2, 4, 8>;    // no lengths: 64 channels x 64 frames per tile, 128 registers
 using ShapeMasked = ClShape<4, 8, 4, 8, 4>;    // lengths or GLU: 128 channels x 32 frames per tile
 
 template <class S, bool GLU>
