@@ -1,6 +1,6 @@
 """Benchmark of the B200 Conformer conv-module kernels.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload stack|module|module_i8|dw|ff|attn]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload stack|module|module_i8|module_w8a8|dw|ff|attn|block|encoder|ctc]
                     [--impl ours|reference]
 
 Default workload ("stack"): 16 conv-module layers (independent seeds) over 512 synthetic utterances per rank with
@@ -140,7 +140,7 @@ def _workload_plan(rank: int, workload: str):
         lens = synth.sample_lengths(1005 + 7919 * rank, N_UTTS)
         return dispatch.plan_chunks(lens, exec_batch=dispatch.EXEC_BATCH, logical_batch=dispatch.LOGICAL_BATCH,
                                     frame_grid=dispatch.FRAME_GRID)
-    if workload in ("module", "module_i8", "ff", "attn", "block", "ctc"):
+    if workload in ("module", "module_i8", "module_w8a8", "ff", "attn", "block", "ctc"):
         lens = synth.sample_lengths(1003 + 7919 * rank, 48)
         T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
         return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
@@ -245,6 +245,8 @@ def _config(args, world):
                  "residual), 512 utterances/rank, lognormal lengths, chunks<=48 on the 128-frame grid",
         "module": "one conv module, B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
         "module_i8": "one conv module with int8 per-channel weights, B=48 chunk, lognormal lengths, length mask",
+        "module_w8a8": "one conv module with int8 per-channel weights and per-row int8 activations (kind::i8 MMAs, "
+                       "s32 accumulate), B=48 chunk, lognormal lengths, length mask",
         "dw": "depthwise k15 + bias + SiLU alone, bf16 [48, 1024, 2048] channels-last, all frames valid",
         "ff": "one feed-forward half of the Conformer block (LN, 1024->4096 GEMM+SiLU, 4096->1024 GEMM + 0.5x "
               "residual), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
@@ -288,6 +290,7 @@ def run_ours(args):
     sp = stream.cuda_stream
     workload = args.workload
     int8 = workload == "module_i8"
+    w8a8 = workload == "module_w8a8"
     n_layers = _layers_for(workload)
 
     chunks = _workload_plan(rank, workload)
@@ -326,7 +329,8 @@ def run_ours(args):
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     else:
         # bf16: the LayerNorm folded into the up_conv GEMM (the module op's path for T on the 128 grid)
-        layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8, ln_fold=not int8)
+        layers = [prepare_from_params(synth.make_params(1005 + l), device=dev, int8=int8 or w8a8,
+                                      ln_fold=not (int8 or w8a8))
                   for l in range(n_layers)]
         xs = [torch.randn((c.B, c.T, D), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
     heads = None
@@ -341,6 +345,8 @@ def run_ours(args):
     lens_dev = [torch.from_numpy(c.lengths).to(dev) for c in chunks]
     max_m = max(c.padded_frames for c in chunks)
     ws_bytes = int(L.gsn_conv_module_workspace_bytes(1, max_m, D, I))
+    if w8a8:
+        ws_bytes = max(ws_bytes, int(L.gsn_conv_module_w8a8_workspace_bytes(1, max_m, D, I)))
     if workload == "ff":
         ws_bytes = max(ws_bytes, int(L.gsn_ff_half_workspace_bytes(1, max_m, D, 4 * D)))
     if workload in ("ff", "block", "encoder"):
@@ -371,6 +377,7 @@ def run_ours(args):
 
     layer_events = []      # per recorded layer: (events[4], chunk) around layernorm, gemm1 + dwconv, gemm2
     widen_events = []      # int8: per recorded layer, the events around the weight widening
+    w8_events = []         # W8A8: per recorded module call, (start, end, chunk)
 
     def layer_kernels(x, out, c, p, lens, record):
         """The kernels of one conv module (the same launches the module op makes for T on the 128 grid): bf16
@@ -378,6 +385,21 @@ def run_ours(args):
         in, down_conv + residual (gsn_conv_module_lnfold_bf16); int8 weights: their widening, LayerNorm, the fused
         up_conv kernel on the LayerNorm output, down_conv + residual.  CUDA events between them when `record`."""
         M = c.padded_frames
+        if w8a8:
+            # the six launches of gsn_conv_module_w8a8 (LayerNorm, quantise, kind::i8 up_conv + GLU, depthwise,
+            # quantise, kind::i8 down_conv + residual), timed as one call
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None
+            if record:
+                e[0].record(stream)
+            _lib.check(L.gsn_conv_module_w8a8(x.data_ptr(), p.ln_w.data_ptr(), p.ln_b.data_ptr(), p.w1q_glu.data_ptr(),
+                                              p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), p.dw_w.data_ptr(),
+                                              p.dw_b.data_ptr(), p.w2q.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
+                                              lens.data_ptr(), 1, out.data_ptr(), c.B, c.T, D, I, p.ln_eps,
+                                              ws.data_ptr(), ws.numel(), sp), "w8a8 module")
+            if record:
+                e[1].record(stream)
+                w8_events.append((e[0], e[1], c))
+            return
         dp = h_buf.data_ptr()                   # depthwise output [M, I]
         tp = h_buf.data_ptr() + t_off           # LayerNorm output [M, D]
         lp, T = lens.data_ptr(), c.T
@@ -601,7 +623,7 @@ def run_ours(args):
                         n += 3
                 else:
                     layer_kernels(src, dst, c, p, lens_dev[ci], record)
-                    n += 4 if int8 else 3
+                    n += 6 if w8a8 else (4 if int8 else 3)
                 src = dst
             if workload == "ctc":
                 selfcond_kernels(xs[ci], act[ci], c, lens_dev[ci], record)
@@ -656,6 +678,19 @@ def run_ours(args):
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
+    elif w8a8:
+        dur = sum(a.elapsed_time(b) for a, b, _ in w8_events) / len(w8_events)
+        rows = sum(sum(-(-int(L_) // 128) * 128 for L_ in c.lengths) for _, _, c in w8_events) / len(w8_events)
+        peak = 2 * peaks["bf16_tflops_sustained"]
+        achieved = rows * (GEMM1_FLOP_PER_FRAME + GEMM2_FLOP_PER_FRAME) / (dur / 1e3) / 1e12
+        roof = {"kernel": "whole W8A8 module call (LayerNorm, 2 row quantisations, kind::i8 up_conv + GLU, depthwise, "
+                          "kind::i8 down_conv + residual), timed as one unit: a lower bound for the GEMMs",
+                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+                "traffic": None, "per_launch_ms": dur,
+                "algorithmic_ops_per_frame": GEMM1_FLOP_PER_FRAME + GEMM2_FLOP_PER_FRAME,
+                "frames_counted": "rows of the 128-row tiles holding valid frames",
+                "peak_source": f"int8 dense peak not measured: 2 x bf16_tflops_sustained of {peaks['source']} "
+                               "(the nominal int8 / bf16 ratio)"}
     elif workload == "ff":
         kernels = _ff_breakdown(layer_events, peaks)
         g1 = kernels["ff_up_silu"]
@@ -700,7 +735,7 @@ def run_ours(args):
 
     # ---- end to end through the public op with pinned host buffers
     e2e = None
-    if workload != "dw" and not args.no_e2e:
+    if workload not in ("dw", "module_w8a8") and not args.no_e2e:
         e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff",
                    attn=workload == "attn", block=workload in ("block", "encoder"), heads=heads)
 
@@ -713,7 +748,7 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if not int8 else "bf16 x int8-weight", "data": "synthetic",
+            "vs_baseline": None, "dtype": "int8 x int8 (s32 accumulate), bf16 in/out" if w8a8 else ("bf16" if not int8 else "bf16 x int8-weight"), "data": "synthetic",
             "config": dict(_config(args, world), padded_frames_per_s=padded_all * args.steps / (ms / 1e3)),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
             "gpu_launches": launches,
@@ -993,7 +1028,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "dw", "ff", "attn", "block", "encoder",
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "module_w8a8", "dw", "ff", "attn", "block", "encoder",
                                            "ctc"], default="stack")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")

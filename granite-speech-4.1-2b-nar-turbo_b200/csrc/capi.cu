@@ -740,6 +740,83 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                      T, D, inner, ln_eps, workspace, workspace_bytes, 1, stream, "gsn_conv_module_i8w");
 }
 
+int gsn_quant_rows_bf16(const void* x, int64_t ldx, void* q, float* scale, int M, int K, const int32_t* lengths,
+                        int T, gsn_stream_t stream) {
+  const char* name = "gsn_quant_rows_bf16";
+  if (M < 0 || K <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: M=%d K=%d", name, M, K);
+  if (M == 0) return ok();
+  if (!x || !q || !scale) return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (K % 8 || ldx < K || ldx % 8 || !aligned(x, 16) || !aligned(q, 8))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d ldx=%lld (K %% 8 == 0, 16-byte aligned rows)", name, K, (long long)ldx);
+  if (lengths && (T <= 0 || M % T)) return fail(GSN_ERR_INVALID_ARG, "%s: lengths need M %% T == 0 (T=%d)", name, T);
+  return finish(launch_quant_rows((const __nv_bfloat16*)x, ldx, (int8_t*)q, scale, M, K, lengths, T,
+                                  (cudaStream_t)stream), name);
+}
+
+size_t gsn_conv_module_w8a8_workspace_bytes(int B, int T, int D, int inner) {
+  const size_t base = gsn_conv_module_workspace_bytes(B, T, D, inner);
+  if (base == 0) return 0;
+  const size_t M = (size_t)B * (size_t)T;
+  const size_t wide = (size_t)(inner > D ? inner : D);
+  return base + align256(M * wide) + align256(M * 4);
+}
+
+int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, const void* w1q_glu,
+                         const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,
+                         const void* w2q, const float* s2, const float* b2, const int32_t* lengths, int add_residual,
+                         void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
+                         size_t workspace_bytes, gsn_stream_t stream) {
+  const char* name = "gsn_conv_module_w8a8";
+  if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
+  if ((int64_t)B * T == 0) return ok();
+  if (!x || !ln_w || !ln_b || !w1q_glu || !s1_glu || !b1_glu || !dw_w || !dw_b || !w2q || !s2 || !b2 || !out)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (!ln_dim_ok(D) || (2 * inner) % 256 != 0 || inner % 128 != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d inner=%d (D in {256..2048}, inner %% 128 == 0)", name, D, inner);
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  const int M = B * T;
+  const size_t need = gsn_conv_module_w8a8_workspace_bytes(B, T, D, inner);
+  if (!workspace || workspace_bytes < need)
+    return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w1q_glu, 16) || !aligned(w2q, 16))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: x, out and the int8 weights must be 16-byte aligned", name);
+
+  // workspace: h = GLU output [M, inner] bf16; t = LayerNorm output [M, D] bf16, later the depthwise output
+  // [M, inner]; q = int8 activations [M, max(D, inner)]; rs = their per-row scales [M]
+  const size_t wide = (size_t)(inner > D ? inner : D);
+  __nv_bfloat16* h = (__nv_bfloat16*)workspace;
+  __nv_bfloat16* t = (__nv_bfloat16*)((char*)workspace + align256((size_t)M * inner * 2));
+  int8_t* q = (int8_t*)((char*)t + align256((size_t)M * wide * 2));
+  float* rs = (float*)((char*)q + align256((size_t)M * wide));
+  const cudaStream_t st = (cudaStream_t)stream;
+  const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
+
+  int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
+                            M, D, ln_eps, skip, T, st);
+  if (rc) return finish(rc, name);
+  rc = launch_quant_rows(t, D, q, rs, M, D, lengths, T, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g1{(const __nv_bfloat16*)q, w1q_glu, b1_glu, s1_glu, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, 1,
+              skip, T};
+  g1.a_int8 = 1;
+  g1.row_scale = rs;
+  rc = launch_gemm(g1, kEpiGlu, st);
+  if (rc) return finish(rc, name);
+  DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
+            (int64_t)T * inner, 1, inner, (int64_t)T * inner, 1, inner, B, inner, T, 0};
+  rc = launch_dwconv(dw, st);
+  if (rc) return finish(rc, name);
+  rc = launch_quant_rows(t, inner, q, rs, M, inner, lengths, T, st);
+  if (rc) return finish(rc, name);
+  GemmArgs g2{(const __nv_bfloat16*)q, w2q, b2, s2, add_residual ? (const __nv_bfloat16*)x : nullptr,
+              (__nv_bfloat16*)out, D, D, M, D, inner, 1, skip, T};
+  g2.a_int8 = 1;
+  g2.row_scale = rs;
+  rc = launch_gemm(g2, kEpiResidual, st);
+  return finish(rc, name);
+}
+
 }  // extern "C"
 
 // ---- whole module with library-owned scratch -------------------------------------------------------------------

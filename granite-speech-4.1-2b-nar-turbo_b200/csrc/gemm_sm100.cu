@@ -52,6 +52,7 @@ constexpr uint32_t TMEM_COLS = 512;
 struct KParams {
   const float* bias;
   const float* col_scale;
+  const float* row_scale;                 // W8A8: per-row scale of the int8 activations, else null
   const __nv_bfloat16* residual;
   __nv_bfloat16* out;
   const int* lengths;                     // per-utterance valid frames, or null (every row computed)
@@ -217,8 +218,9 @@ struct __align__(1024) EpiSmem {
 
 // ------------------------------------------------------------------------------------------------------------
 // Epilogue of one warp (state lives in registers; one object per epilogue warp).  SCALED: the accumulator is
-// multiplied by a per-output-column scale (int8 weights, staged as int8 or already widened to bf16).
-template <int EPI, bool SCALED>
+// multiplied by a per-output-column scale (int8 weights, staged as int8 or already widened to bf16).  A8: the
+// accumulator is an s32 sum of int8 products (W8A8), converted to fp32 and multiplied by its row's scale first.
+template <int EPI, bool SCALED, bool A8 = false>
 struct Epilogue {
   static constexpr int NU = (EPI == kEpiGlu ? BN / 2 : BN) / BOX;   // 32-column output sub-tiles per tile
   float alpha;                            // residual epilogue: scale of acc * scale + bias
@@ -232,6 +234,8 @@ struct Epilogue {
   const CUtensorMap* tmR;
   unsigned long long* argmax_keys;
   int M;
+  const float* row_scale;
+  float rs;                               // A8: this lane's row scale for the current tile
   bool has_res;
   int lane, swz;
   uint32_t su;                            // sub-tiles handled so far: buffer su & 1, its use count su >> 1
@@ -245,6 +249,8 @@ struct Epilogue {
     tmR = r;
     argmax_keys = p.argmax_keys;
     M = p.M;
+    row_scale = p.row_scale;
+    rs = 1.0f;
     has_res = EPI == kEpiResidual && p.residual != nullptr;
     alpha = EPI == kEpiResidual ? p.out_scale : 1.0f;
     lengths = p.lengths;
@@ -274,6 +280,12 @@ struct Epilogue {
       }
     }
     __syncwarp();
+  }
+
+  // accumulator word -> fp32 (A8: exact s32 sum, converted, times the row scale)
+  __device__ __forceinline__ float accf(uint32_t bits) const {
+    if constexpr (A8) return (float)(int32_t)bits * rs;
+    return __uint_as_float(bits);
   }
 
   __device__ void load_residual(uint32_t buf, int col, int row0) {
@@ -322,6 +334,10 @@ struct Epilogue {
       }
       return true;
     }
+    if constexpr (A8) {
+      const int row = row0 + lane;
+      rs = row < M ? __ldg(row_scale + row) : 0.f;
+    }
     // SiLU: this lane's row is a padding frame -> zero, so the next GEMM sees what a masked input gives
     bool row_valid = true;
     if (EPI == kEpiSilu && lengths != nullptr) {
@@ -365,8 +381,8 @@ struct Epilogue {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const int k = c4 + c;
-            const float a = fmaf(__uint_as_float(va[k >> 4][k & 15]), sav[c], bav[c]);   // value / 2
-            const float g = fmaf(__uint_as_float(vg[k >> 4][k & 15]), sgv[c], bgv[c]);   // gate / 2
+            const float a = fmaf(accf(va[k >> 4][k & 15]), sav[c], bav[c]);   // value / 2
+            const float g = fmaf(accf(vg[k >> 4][k & 15]), sgv[c], bgv[c]);   // gate / 2
             o[k] = fmaf(a, tanh_approx(g), a);
           }
         }
@@ -390,7 +406,7 @@ struct Epilogue {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const int k = c4 + c;
-            o[k] = fmaf(__uint_as_float(v[k >> 4][k & 15]), sv[c], bv[c]);
+            o[k] = fmaf(accf(v[k >> 4][k & 15]), sv[c], bv[c]);
             if (EPI == kEpiSilu) {
               // the Linear output is a bf16 tensor before the SiLU (conformer.py:35-36): round it, then
               // silu(y) = h + h tanh(h) with h = y / 2
@@ -482,12 +498,16 @@ static_assert(offsetof(Smem<false>, b) % 1024 == 0 && offsetof(Smem<true>, b8) %
 static_assert(offsetof(Smem<false>, epi) % 1024 == 0 && offsetof(Smem<true>, epi) % 1024 == 0, "box alignment");
 static_assert(sizeof(Smem<false>) + 1024 <= 232448 && sizeof(Smem<true>) + 1024 <= 232448, "shared memory size");
 
-template <int EPI, bool W_I8, bool SCALED>
+// A8 (W8A8): A and W are int8 with 128 elements (128 bytes) per K-block, the same bytes per stage and the same
+// swizzled layout as 64 bf16; four kind::i8 MMAs of K = 32 per K-block, s32 accumulators.
+template <int EPI, bool W_I8, bool SCALED, bool A8 = false>
 __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, KParams p) {
+  static_assert(!(A8 && W_I8), "W8A8 tiles are loaded as int8 and used as int8");
   constexpr int STAGES = Cfg<W_I8>::STAGES;
-  constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
+  constexpr uint32_t IDESC = A8 ? make_idesc_s8_s32(BM, BN) : make_idesc_bf16_f32(BM, BN);
+  constexpr int KBE = A8 ? 2 * BK : BK;      // elements per K-block
   extern __shared__ uint8_t smem_raw[];
   Smem<W_I8>& s =
       *reinterpret_cast<Smem<W_I8>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -496,7 +516,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = p.N / BN;
-  const int num_kb = (p.K + BK - 1) / BK;   // a partial last K-block is completed with zeros by TMA
+  const int num_kb = (p.K + KBE - 1) / KBE;   // a partial last K-block is completed with zeros by TMA
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -556,8 +576,8 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
             tma_load_2d_hint(s.b8[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
           } else {
             mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES);
-            tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, m_blk * BM);
-            tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
+            tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * KBE, m_blk * BM);
+            tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * KBE, n_blk * BN, pol_w);
           }
         }
         __syncwarp();
@@ -610,9 +630,13 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
           const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.b[stage]));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // +32 bytes per K=16 slice inside the 128-byte swizzled row: +2 in the (addr >> 4) field
-            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC,
-                     (kb | k) != 0 ? 1u : 0u);
+            // +32 bytes per K=16 (bf16) or K=32 (int8) slice inside the 128-byte swizzled row: +2 in the
+            // (addr >> 4) field
+            if constexpr (A8)
+              umma_i8(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC,
+                       (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&s.empty[stage]);
         }
@@ -633,7 +657,7 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int q = warp & 3;           // a warp may only read its own 32-lane quarter of TMEM
-    Epilogue<EPI, SCALED> epi;
+    Epilogue<EPI, SCALED, A8> epi;
     epi.init(s.epi, warp - 2, &tmO, &tmR, p);
     int local = 0;
     const int epi_tiles = EPI == kEpiResidual ? tmap.num_tiles : tmap.active_tiles;
@@ -947,21 +971,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 // host side
 int encode_operands(const GemmArgs& a, int epilogue, int a_rows, int w_rows, CUtensorMap* tmA, CUtensorMap* tmW,
                     CUtensorMap* tmO, CUtensorMap* tmR) {
-  {
-    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
-    const uint64_t strides[1] = {(uint64_t)a.K * 2};
-    const uint32_t box[2] = {BK, (uint32_t)a_rows};
-    int rc = encode_tmap(tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
+  if (a.a_int8) {
+    // W8A8: int8 A and W, 128 elements (128 bytes) per box row, 128-byte swizzle like the bf16 tiles
+    const uint64_t adims[2] = {(uint64_t)a.K, (uint64_t)a.M};
+    const uint64_t astrides[1] = {(uint64_t)a.K};
+    const uint32_t abox[2] = {2 * BK, (uint32_t)a_rows};
+    int rc = encode_tmap(tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.a, adims, astrides, abox,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
-    const uint64_t strides[1] = {(uint64_t)a.K * (a.w_int8 ? 1 : 2)};
-    const uint32_t box[2] = {BK, (uint32_t)w_rows};
-    int rc = encode_tmap(tmW, a.w_int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w,
-                         dims, strides, box, a.w_int8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint64_t wdims[2] = {(uint64_t)a.K, (uint64_t)a.N};
+    const uint32_t wbox[2] = {2 * BK, (uint32_t)w_rows};
+    rc = encode_tmap(tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.w, wdims, astrides, wbox, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+  } else {
+    {
+      const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
+      const uint64_t strides[1] = {(uint64_t)a.K * 2};
+      const uint32_t box[2] = {BK, (uint32_t)a_rows};
+      int rc = encode_tmap(tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
+    {
+      const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
+      const uint64_t strides[1] = {(uint64_t)a.K * (a.w_int8 ? 1 : 2)};
+      const uint32_t box[2] = {BK, (uint32_t)w_rows};
+      int rc = encode_tmap(tmW, a.w_int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w,
+                           dims, strides, box, a.w_int8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
   }
   if (tmO == nullptr) return 0;   // no output tensor (argmax epilogue)
   {
@@ -990,6 +1028,7 @@ KParams make_params(const GemmArgs& a) {
   KParams p;
   p.bias = a.bias;
   p.col_scale = a.col_scale;
+  p.row_scale = a.row_scale;
   p.residual = a.residual;
   p.out = a.out;
   p.lengths = a.lengths;
@@ -1005,7 +1044,7 @@ KParams make_params(const GemmArgs& a) {
   return p;
 }
 
-template <int EPI, bool W_I8, bool SCALED>
+template <int EPI, bool W_I8, bool SCALED, bool A8 = false>
 int launch_single(const GemmArgs& a, cudaStream_t stream) {
   CUtensorMap tmA, tmW, tmO, tmR;
   if (EPI == kEpiArgmax) {
@@ -1018,7 +1057,7 @@ int launch_single(const GemmArgs& a, cudaStream_t stream) {
   }
   const KParams p = make_params(a);
   const int smem = (int)sizeof(Smem<W_I8>) + 1024;
-  auto kern = gemm_kernel<EPI, W_I8, SCALED>;
+  auto kern = gemm_kernel<EPI, W_I8, SCALED, A8>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
@@ -1100,6 +1139,14 @@ int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* 
 }
 
 int launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream) {
+  if (a.a_int8) {
+    // W8A8: int8 activations with per-row scales, int8 weights with per-column scales
+    if (!a.w_int8 || !a.col_scale || !a.row_scale || a.K % 16 || a.out_scale != 1.0f ||
+        (epilogue != kEpiGlu && epilogue != kEpiResidual))
+      return (int)cudaErrorInvalidValue;
+    return epilogue == kEpiGlu ? launch_single<kEpiGlu, false, true, true>(a, stream)
+                               : launch_single<kEpiResidual, false, true, true>(a, stream);
+  }
   if (GSN_GEMM_PAIR && !a.w_int8 && !a.col_scale && (epilogue == kEpiGlu || epilogue == kEpiResidual) &&
       a.out_scale == 1.0f && a.K % BK == 0) {
     bool launched = false;

@@ -3,6 +3,7 @@
 #include "layernorm.cu"
 #include "dwconv.cu"
 #include "gemm_sm100.cu"
+#include "quant_rows.cu"
 #include "gemm_glu_dw_sm100.cu"
 #include "attention_sm100.cu"
 #include "ctc_head.cu"

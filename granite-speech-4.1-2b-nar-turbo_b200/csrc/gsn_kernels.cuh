@@ -39,6 +39,8 @@ struct GemmArgs {
   float out_scale = 1.0f;        // RESIDUAL: out = out_scale * (acc * col_scale + bias) + residual
   unsigned long long* argmax_keys = nullptr;   // ARGMAX: [M] keys, zeroed by the caller
   int n_major = 0;               // walk the tiles column block by column block (each W tile read once)
+  int a_int8 = 0;                // W8A8: a is int8 [M, K] and w int8 [N, K] (kind::i8 MMAs, s32 accumulate);
+  const float* row_scale = nullptr;   //   acc is scaled by row_scale[m] * col_scale[n] (GLU and RESIDUAL only)
 };
 
 // LINEAR: out = acc + b, 128-row tiles of pure padding skipped (nothing written there)
@@ -46,6 +48,11 @@ struct GemmArgs {
 enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2, kEpiLinear = 3, kEpiArgmax = 4 };
 
 int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
+// Per-row symmetric int8 quantisation: scale[m] = max_k |x[m, k]| / 127, q[m, k] = rint(x[m, k] / scale[m]) (q = 0
+// and scale = 0 for an all-zero row; with lengths, rows of padding frames likewise).  x bf16 [M, K] (row stride
+// ldx), q int8 [M, K] dense.  K % 8 == 0, 16-byte aligned rows.
+int launch_quant_rows(const __nv_bfloat16* x, int64_t ldx, int8_t* q, float* scale, int M, int K,
+                      const int* lengths, int T, cudaStream_t stream);
 // int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).
 int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* o1, int64_t n1, cudaStream_t stream);
 

@@ -202,6 +202,17 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// D(tmem) (+)= A(smem desc) * B(smem desc)^T, kind::i8 (signed 8-bit inputs, s32 accumulate; K = 32 per
+// instruction, the same 32 bytes of a 128-byte swizzled row as one kind::f16 step), issued by one thread.
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D(tmem) (+)= A(tmem) * B(smem desc)^T, kind::f16: A is M lanes x K/2 columns of packed bf16 pairs (element k of
 // row m in the low half of column k / 2 when k is even), issued by one thread.
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -311,6 +322,12 @@ __device__ __forceinline__ uint64_t make_sw128_mnmajor_desc(uint32_t smem_addr, 
   d |= (uint64_t)1u << 46;
   d |= (uint64_t)2u << 61;
   return d;
+}
+
+// Instruction descriptor, kind::i8: D s32 (bits 4-5 = 2), A signed 8-bit (bits 7-9 = 1), B signed 8-bit
+// (bits 10-12 = 1), no saturation (bit 3), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t make_idesc_s8_s32(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 // Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16 (bits 10-12 = 1),

@@ -71,6 +71,10 @@ SIGNATURES = {
                                     _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
     "gsn_conv_module_i8w": (_i32, [_vp, _vp, _vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _fp, _vp, _i32, _vp,
                                    _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
+    "gsn_conv_module_w8a8_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "gsn_conv_module_w8a8": (_i32, [_vp, _vp, _vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _fp, _vp, _i32, _vp,
+                                    _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
+    "gsn_quant_rows_bf16": (_i32, [_vp, _i64, _vp, _fp, _i32, _i32, _vp, _i32, _vp]),
     "gsn_conv_module_bf16_noalloc": (_i32, [_vp, _vp, _vp, _vp, _fp, _vp, _vp, _vp, _fp, _vp, _i32, _vp, _i32,
                                             _i32, _i32, _i32, _f32, _vp]),
     "gsn_interleave_glu_rows": (_i32, [_vp, _vp, _i32, _i64, _vp]),

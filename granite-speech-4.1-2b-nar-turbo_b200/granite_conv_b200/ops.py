@@ -217,6 +217,30 @@ def _(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, 
     return torch.empty_like(x, memory_format=torch.contiguous_format)
 
 
+@torch.library.custom_op("granite::conv_module_w8a8", mutates_args=(), device_types="cuda")
+def conv_module_w8a8(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w1q_glu: torch.Tensor,
+                     s1_glu: torch.Tensor, b1_glu: torch.Tensor, dw_w: torch.Tensor, dw_b: torch.Tensor,
+                     w2q: torch.Tensor, s2: torch.Tensor, b2: torch.Tensor, lengths: Optional[torch.Tensor],
+                     ln_eps: float, add_residual: bool) -> torch.Tensor:
+    """conv_module with int8 weights and int8 activations: the LayerNorm and depthwise outputs are quantised per
+    row (symmetric, absmax / 127) and both pointwise GEMMs run int8 x int8 tensor-core MMAs with s32 accumulation,
+    scaled by the row and column scales in the epilogue.  Same weights as ``conv_module_i8w``."""
+    name = "granite::conv_module_w8a8"
+    _require_cuda(name, x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths)
+    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(name, x, ln_w, dw_w, lengths,
+                                                               "gsn_conv_module_w8a8_workspace_bytes")
+    _lib.call("gsn_conv_module_w8a8", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w1q_glu.data_ptr(),
+              s1_glu.data_ptr(), b1_glu.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), w2q.data_ptr(), s2.data_ptr(),
+              b2.data_ptr(), _ptr(lens), 1 if add_residual else 0, out.data_ptr(), B, T, D, inner, float(ln_eps),
+              ws.data_ptr(), nbytes, _stream(xc))
+    return out
+
+
+@conv_module_w8a8.register_fake
+def _(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, ln_eps, add_residual):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # ---- the rest of the Conformer block: feed-forward halves and the post LayerNorm -------------------------------
 @torch.library.custom_op("granite::feed_forward_half", mutates_args=(), device_types="cuda")
@@ -416,9 +440,15 @@ def run_feed_forward_half(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = 
 
 
 def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, add_residual: bool = True,
-                    int8: bool = False, ln_fold: Optional[bool] = None) -> torch.Tensor:
+                    int8: bool = False, ln_fold: Optional[bool] = None, w8a8: bool = False) -> torch.Tensor:
     """Call the fused module op with a :class:`~granite_conv_b200.weights.PreparedConvModule`.  ``ln_fold``: use
-    the LayerNorm-folded op (default: when the weights carry the folded operands and T % 128 == 0)."""
+    the LayerNorm-folded op (default: when the weights carry the folded operands and T % 128 == 0).  ``w8a8``: the
+    int8-weight, int8-activation op (needs weights prepared with int8)."""
+    if w8a8:
+        if not p.has_int8:
+            raise RuntimeError("run_conv_module(w8a8=True): weights were prepared without int8")
+        return torch.ops.granite.conv_module_w8a8(x, p.ln_w, p.ln_b, p.w1q_glu, p.s1_glu, p.b1_glu, p.dw_w, p.dw_b,
+                                                  p.w2q, p.s2, p.b2, lengths, p.ln_eps, add_residual)
     if ln_fold is None:
         ln_fold = (not int8) and p.has_ln_fold and x.dim() == 3 and x.shape[1] % 128 == 0
     if ln_fold:
@@ -436,6 +466,18 @@ def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, 
 
 
 # ---- single-kernel wrappers (tests, benchmarks) ---------------------------------------------------------------
+def quant_rows(x2d: torch.Tensor, lengths: Optional[torch.Tensor] = None, T: int = 0):
+    """Per-row symmetric int8 quantisation of bf16 rows: returns (q int8 [M, K], scale fp32 [M])."""
+    _require_cuda("quant_rows", x2d, lengths)
+    if x2d.dtype != torch.bfloat16 or x2d.dim() != 2 or x2d.stride(1) != 1:
+        raise RuntimeError("quant_rows: expects a bf16 [M, K] tensor with unit column stride")
+    M, K = x2d.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x2d.device)
+    sc = torch.empty((M,), dtype=torch.float32, device=x2d.device)
+    _lib.call("gsn_quant_rows_bf16", x2d.data_ptr(), x2d.stride(0), q.data_ptr(), sc.data_ptr(), M, K,
+              _ptr(lengths), T, _stream(x2d))
+    return q, sc
+
 def layernorm(x2d: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5,
               lengths: Optional[torch.Tensor] = None, T: int = 0) -> torch.Tensor:
     """LayerNorm of bf16 rows [M, D]; with lengths (int32 [M / T]) padding rows are left unwritten."""

@@ -187,6 +187,27 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                         int add_residual, void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
                         size_t workspace_bytes, gsn_stream_t stream);
 
+/* W8A8 module: int8 weights (as for gsn_conv_module_i8w: w1q_glu [2*inner, D] GLU-interleaved, w2q [D, inner],
+ * fp32 per-output-channel scales s1_glu, s2) and int8 activations: the LayerNorm output and the depthwise output
+ * are quantised per row (gsn_quant_rows_bf16) and both pointwise GEMMs run kind::i8 tensor-core MMAs with s32
+ * accumulation, scaled by row_scale[m] * col_scale[n] in the epilogue.  No reference code: the nearest is torchao's
+ * W8A8 dynamic quantisation in bench_asr.py:92-105 (not vendored).  Workspace: at least
+ * gsn_conv_module_w8a8_workspace_bytes(B, T, D, inner), 256-byte aligned. */
+size_t gsn_conv_module_w8a8_workspace_bytes(int B, int T, int D, int inner);
+
+int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, const void* w1q_glu,
+                         const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,
+                         const void* w2q, const float* s2, const float* b2, const int32_t* lengths, int add_residual,
+                         void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
+                         size_t workspace_bytes, gsn_stream_t stream);
+
+/* Per-row symmetric int8 quantisation used by gsn_conv_module_w8a8 (no reference counterpart): for each row m of
+ * x (bf16 [M, K], row stride ldx), scale[m] = max_k |x[m, k]| / 127 and q[m, k] = rint(x[m, k] / scale[m]) (IEEE
+ * fp32 division, ties to even; q = 0 and scale = 0 for an all-zero row).  With lengths (M = B * T), rows of
+ * padding frames get q = 0 and scale = 0.  q is int8 [M, K] dense.  K % 8 == 0, x rows 16-byte aligned. */
+int gsn_quant_rows_bf16(const void* x, int64_t ldx, void* q, float* scale, int M, int K, const int32_t* lengths,
+                        int T, gsn_stream_t stream);
+
 /* ---- feed-forward halves of the Conformer block ---------------------------------------------------------------
  * Replace ConformerFeedForward (conformer.py:23-40: pre_norm -> up_proj -> SiLU -> down_proj) together with the
  * block's half-step residual x + 0.5 * ff(x) (conformer.py:205, :208).  Dropout is the identity (inference).

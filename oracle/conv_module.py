@@ -207,6 +207,51 @@ def conv_module(x, prep, lengths=None, mode="fused", residual=True, dtype=np.flo
 
 
 # --------------------------------------------------------------------------------------------------------------
+# W8A8: int8 weights and int8 activations (no reference code; torchao's W8A8 dynamic quantisation in
+# ``script/bench_asr.py:92-105`` is the nearest analogue and is not vendored)
+def quantize_rows(x):
+    """Per-row symmetric int8 of activations: ``s = absmax / 127`` and ``q = rint(x / s)`` in fp32 (IEEE division,
+    ties to even), clipped to [-127, 127]; ``q = 0`` and ``s = 0`` for an all-zero row.  Returns (q int8, s fp32)."""
+    x = np.asarray(x, dtype=np.float32)
+    s = (np.abs(x).max(axis=1) / np.float32(127.0)).astype(np.float32)
+    safe = np.where(s == 0, np.float32(1.0), s).astype(np.float32)
+    q = np.clip(np.rint(x / safe[:, None]), -127, 127)
+    q = np.where(s[:, None] == 0, 0, q).astype(np.int8)
+    return q, s
+
+
+def conv_module_w8a8(x, prep, q1, s1, q2, s2, lengths=None, residual=True):
+    """The conv module with int8 weights ``q1 [2I, D]``, ``q2 [D, I]`` (per-row scales ``s1``, ``s2``) and int8
+    activations: the LayerNorm output and the depthwise output are quantised per row (:func:`quantize_rows`; rows
+    of padding frames quantise to zero), each GEMM is an exact integer sum scaled by ``s_row * s_col``.  bf16
+    rounding points as the B200 path: LayerNorm out, GLU out, depthwise + SiLU out, final sum."""
+    B, T, D = x.shape
+    m = _row_mask(B, T, lengths)
+    mrow = None if m is None else m.reshape(-1, 1)
+    xin = x.astype(np.float32)
+    xn = bf16_round(layer_norm(xin, prep["ln_w"], prep["ln_b"], prep["ln_eps"]).astype(np.float32)).reshape(B * T, D)
+    if mrow is not None:
+        xn = xn * mrow
+    qa, sa = quantize_rows(xn)
+    acc = qa.astype(np.int64) @ q1.astype(np.int64).T
+    h = acc.astype(np.float64) * sa.astype(np.float64)[:, None] * s1.astype(np.float64)[None, :] + prep["b1"]
+    gl = bf16_round(glu(h).astype(np.float32)).reshape(B, T, -1)
+    if m is not None:
+        gl = gl * m[..., None]
+    d = bf16_round(_silu(depthwise(gl.astype(np.float64), prep["dw_w"], prep["dw_b"])).astype(np.float32))
+    d = d.reshape(B * T, -1)
+    if mrow is not None:
+        d = d * mrow
+    qd, sd = quantize_rows(d)
+    acc2 = qd.astype(np.int64) @ q2.astype(np.int64).T
+    y = acc2.astype(np.float64) * sd.astype(np.float64)[:, None] * s2.astype(np.float64)[None, :] + prep["b2"]
+    y = y.reshape(B, T, D)
+    if residual:
+        y = y + xin.astype(np.float64)
+    return bf16_round(y.astype(np.float32))
+
+
+# --------------------------------------------------------------------------------------------------------------
 # parity metrics (``script/cuda_kernels/bench.py:31-44`` reports max-abs; rel-L2 is the second gate)
 def max_abs(a, b) -> float:
     return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64)))) if np.size(a) else 0.0

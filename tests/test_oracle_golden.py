@@ -202,3 +202,18 @@ def test_ctc_heads_oracle():
             toks = np.concatenate([r[2] for r in res])
             np.testing.assert_array_equal(toks, g[f"{tag}_tokens"])
             np.testing.assert_array_equal([len(r[2]) for r in res], g[f"{tag}_counts"])
+
+
+def test_oracle_quantize_rows_properties():
+    """Per-row int8 of activations (the W8A8 path): |x - q * s| <= s / 2 on every element, the largest |x| of each
+    row maps to +-127, and an all-zero row gives q = 0, s = 0."""
+    g = np.random.default_rng(5)
+    x = O.bf16_round(g.normal(0, 2.0, (64, 256)).astype(np.float32))
+    x[7] = 0.0
+    q, s = O.quantize_rows(x)
+    assert q.dtype == np.int8 and s.dtype == np.float32
+    assert s[7] == 0 and not q[7].any()
+    err = np.abs(x.astype(np.float64) - q.astype(np.float64) * s.astype(np.float64)[:, None])
+    assert np.all(err <= s.astype(np.float64)[:, None] / 2 * (1 + 1e-5))   # fp32 division rounds x / s
+    rows = [r for r in range(64) if r != 7]
+    assert np.all(np.abs(q[rows]).max(axis=1) == 127)
