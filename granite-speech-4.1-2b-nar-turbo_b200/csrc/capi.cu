@@ -782,8 +782,9 @@ int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, cons
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w1q_glu, 16) || !aligned(w2q, 16))
     return fail(GSN_ERR_UNSUPPORTED, "%s: x, out and the int8 weights must be 16-byte aligned", name);
 
-  // workspace: h = GLU output [M, inner] bf16; t = LayerNorm output [M, D] bf16, later the depthwise output
-  // [M, inner]; q = int8 activations [M, max(D, inner)]; rs = their per-row scales [M]
+  // workspace: h = GLU output [M, inner] bf16; t = the depthwise output [M, inner] bf16; q = int8 activations
+  // [M, max(D, inner)] (the LayerNorm output quantised in the LayerNorm pass, then the depthwise output); rs = their
+  // per-row scales [M]
   const size_t wide = (size_t)(inner > D ? inner : D);
   __nv_bfloat16* h = (__nv_bfloat16*)workspace;
   __nv_bfloat16* t = (__nv_bfloat16*)((char*)workspace + align256((size_t)M * inner * 2));
@@ -792,10 +793,8 @@ int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, cons
   const cudaStream_t st = (cudaStream_t)stream;
   const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
 
-  int rc = launch_layernorm((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b, t, D,
-                            M, D, ln_eps, skip, T, st);
-  if (rc) return finish(rc, name);
-  rc = launch_quant_rows(t, D, q, rs, M, D, lengths, T, st);
+  int rc = launch_layernorm_quant((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b,
+                                  q, rs, M, D, ln_eps, lengths, T, st);
   if (rc) return finish(rc, name);
   GemmArgs g1{(const __nv_bfloat16*)q, w1q_glu, b1_glu, s1_glu, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, 1,
               skip, T};
