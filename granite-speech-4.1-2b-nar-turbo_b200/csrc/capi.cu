@@ -796,16 +796,27 @@ int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, cons
   int rc = launch_layernorm_quant((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b,
                                   q, rs, M, D, ln_eps, lengths, T, st);
   if (rc) return finish(rc, name);
-  GemmArgs g1{(const __nv_bfloat16*)q, w1q_glu, b1_glu, s1_glu, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, 1,
-              skip, T};
-  g1.a_int8 = 1;
-  g1.row_scale = rs;
-  rc = launch_gemm(g1, kEpiGlu, st);
-  if (rc) return finish(rc, name);
-  DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
-            (int64_t)T * inner, 1, inner, (int64_t)T * inner, 1, inner, B, inner, T, 0};
-  rc = launch_dwconv(dw, st);
-  if (rc) return finish(rc, name);
+  if (T % 128 == 0 && D % 128 == 0) {
+    // frames on the 128 grid: GLU, depthwise and SiLU run inside the kind::i8 up_conv GEMM (the GLU tensor is never
+    // written); t receives the depthwise output
+    GemmDwArgs gd{(const __nv_bfloat16*)q, (const __nv_bfloat16*)w1q_glu, b1_glu, s1_glu, (const __nv_bfloat16*)dw_w,
+                  (const __nv_bfloat16*)dw_b, t, lengths, B, T, D, 2 * inner};
+    gd.a_int8 = 1;
+    gd.row_scale = rs;
+    rc = launch_gemm_glu_dw(gd, st);
+    if (rc) return finish(rc, name);
+  } else {
+    GemmArgs g1{(const __nv_bfloat16*)q, w1q_glu, b1_glu, s1_glu, nullptr, h, (int64_t)inner, 0, M, 2 * inner, D, 1,
+                skip, T};
+    g1.a_int8 = 1;
+    g1.row_scale = rs;
+    rc = launch_gemm(g1, kEpiGlu, st);
+    if (rc) return finish(rc, name);
+    DwArgs dw{h, (const __nv_bfloat16*)dw_w, (const __nv_bfloat16*)dw_b, t, lengths,
+              (int64_t)T * inner, 1, inner, (int64_t)T * inner, 1, inner, B, inner, T, 0};
+    rc = launch_dwconv(dw, st);
+    if (rc) return finish(rc, name);
+  }
   rc = launch_quant_rows(t, inner, q, rs, M, inner, lengths, T, st);
   if (rc) return finish(rc, name);
   GemmArgs g2{(const __nv_bfloat16*)q, w2q, b2, s2, add_residual ? (const __nv_bfloat16*)x : nullptr,

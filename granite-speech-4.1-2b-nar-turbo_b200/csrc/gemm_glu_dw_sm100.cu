@@ -60,6 +60,7 @@ struct Params {
   const int* lengths;         // [B] or null
   const float2* row_stats;    // LayerNorm folded in: per-row (rstd, rstd * mean), rows b * T + t
   const float* colsum;        // LayerNorm folded in: [N] column sums of W'
+  const float* row_scale;     // A8: per-row scale of the int8 activations, rows b * T + t
   int B, T, K, N;
 };
 
@@ -152,18 +153,22 @@ struct Units {
 
 // SCALED: per-column scale on the accumulator (int8 weights widened to bf16).  LNF: LayerNorm folded in -- A holds
 // the raw frames, W the weights times gamma, and the accumulator becomes rstd * (acc - mean * colsum) + bias.
-template <bool SCALED, bool LNF>
+// A8 (W8A8): A and W are int8 (128 per K-block, the same bytes per stage as 64 bf16), kind::i8 MMAs with s32
+// accumulators; the epilogue takes fp32(acc) * row_scale * col_scale + bias, as the standalone int8 GEMM does.
+template <bool SCALED, bool LNF, bool A8 = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmW64, const __grid_constant__ CUtensorMap tmD, Params p) {
-  constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN);
-  constexpr uint32_t IDESC_HALF = make_idesc_bf16_f32(BM, BN / 2);
+  static_assert(!(A8 && (LNF || !SCALED)), "W8A8 takes per-column scales and no folded LayerNorm");
+  constexpr uint32_t IDESC = A8 ? make_idesc_s8_s32(BM, BN) : make_idesc_bf16_f32(BM, BN);
+  constexpr uint32_t IDESC_HALF = A8 ? make_idesc_s8_s32(BM, BN / 2) : make_idesc_bf16_f32(BM, BN / 2);
+  constexpr int KBE = A8 ? 2 * BK : BK;       // elements per K-block
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   const int warp = warp_id();
   const int lane = threadIdx.x & 31;
-  const int num_kb = p.K / BK;
+  const int num_kb = p.K / KBE;
   const int inner = p.N / 2;
   const bool sorted = p.B <= MAX_SORT_B;
 
@@ -236,16 +241,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (lane == 0) {
             if (u.half < 0) {
               mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES);
-              tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, row0);
-              tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * BK, u.n_blk * BN, pol_w);
+              tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * KBE, row0);
+              tma_load_2d_hint(s.b[stage], &tmW, &s.full[stage], kb * KBE, u.n_blk * BN, pol_w);
             } else {
               // half unit: W rows of its 64 value channels, then of their 64 gate channels (8-row swizzle atoms,
               // so the two 64-row boxes form one 128-row tile)
               const int w0 = u.n_blk * BN + 64 * u.half;
               mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B_BYTES / 2);
-              tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, row0);
-              tma_load_2d_hint(s.b[stage], &tmW64, &s.full[stage], kb * BK, w0, pol_w);
-              tma_load_2d_hint(s.b[stage] + B_BYTES / 4, &tmW64, &s.full[stage], kb * BK, w0 + CH, pol_w);
+              tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * KBE, row0);
+              tma_load_2d_hint(s.b[stage], &tmW64, &s.full[stage], kb * KBE, w0, pol_w);
+              tma_load_2d_hint(s.b[stage] + B_BYTES / 4, &tmW64, &s.full[stage], kb * KBE, w0 + CH, pol_w);
             }
           }
           __syncwarp();
@@ -299,9 +304,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(s.a[stage]));
             const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.b[stage]));
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk)
-              umma_f16(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
-                       (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              if constexpr (A8)
+                umma_i8(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
+                        (kb | kk) != 0 ? 1u : 0u);
+              else
+                umma_f16(d_tmem, adesc + (uint64_t)(2 * kk), bdesc + (uint64_t)(2 * kk), idesc,
+                         (kb | kk) != 0 ? 1u : 0u);
+            }
             umma_commit(&s.empty[stage]);
           }
           __syncwarp();
@@ -398,6 +408,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               rs = st.x;
               rsm = st.y;
             }
+            if (A8 && valid) rs = __ldg(p.row_scale + (int64_t)b * p.T + t0 + r);
             const int nsub = whole ? 2 : 1;              // 32-channel sub-tiles of this warp
             for (int uu = 0; uu < nsub; ++uu) {
               const int cb = whole ? grp * 64 + uu * 32 : grp * 32;   // first of the sub-tile's 32 GLU channels
@@ -421,6 +432,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rs * s.vs[cb + kk],
                              fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
                     g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rs * s.vs[ga], fmaf(-rsm, s.vc[ga], s.vb[ga]));
+                  } else if (A8) {
+                    a = fmaf((float)(int32_t)va[kk >> 4][kk & 15] * rs, s.vs[cb + kk], s.vb[cb + kk]);
+                    g = fmaf((float)(int32_t)vg[kk >> 4][kk & 15] * rs, s.vs[ga], s.vb[ga]);
                   } else {
                     a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
                     g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[ga], s.vb[ga]);
@@ -535,29 +549,28 @@ __global__ void __launch_bounds__(THREADS, 1)
 int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   namespace G = gdw_impl;
   if (a.B <= 0 || a.T <= 0) return 0;
-  if (a.T % G::BM || a.K % G::BK || a.N % G::BN) return (int)cudaErrorInvalidValue;
+  // W8A8: int8 operands, 128 elements (128 bytes) per box row
+  const int kbe = a.a_int8 ? 2 * G::BK : G::BK;
+  const int esz = a.a_int8 ? 1 : 2;
+  const CUtensorMapDataType dt = a.a_int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (a.T % G::BM || a.K % kbe || a.N % G::BN) return (int)cudaErrorInvalidValue;
+  if (a.a_int8 && (!a.col_scale || !a.row_scale || a.row_stats)) return (int)cudaErrorInvalidValue;
   CUtensorMap tmA, tmW;
   const int64_t M = (int64_t)a.B * a.T;
   {
     const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)a.K * 2};
-    const uint32_t box[2] = {G::BK, G::BM};
-    if (int rc = encode_tmap(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.a, dims, strides, box,
-                             CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
+    const uint64_t strides[1] = {(uint64_t)a.K * esz};
+    const uint32_t box[2] = {(uint32_t)kbe, G::BM};
+    if (int rc = encode_tmap(&tmA, dt, 2, a.a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   CUtensorMap tmW64;
   {
     const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
-    const uint64_t strides[1] = {(uint64_t)a.K * 2};
-    const uint32_t box[2] = {G::BK, G::BN};
-    if (int rc = encode_tmap(&tmW, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w, dims, strides, box,
-                             CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
-    const uint32_t box64[2] = {G::BK, G::BN / 4};
-    if (int rc = encode_tmap(&tmW64, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.w, dims, strides, box64,
-                             CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
+    const uint64_t strides[1] = {(uint64_t)a.K * esz};
+    const uint32_t box[2] = {(uint32_t)kbe, G::BN};
+    if (int rc = encode_tmap(&tmW, dt, 2, a.w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    const uint32_t box64[2] = {(uint32_t)kbe, G::BN / 4};
+    if (int rc = encode_tmap(&tmW64, dt, 2, a.w, dims, strides, box64, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   }
   CUtensorMap tmD;
   {
@@ -577,14 +590,16 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   p.lengths = a.lengths;
   p.row_stats = a.row_stats;
   p.colsum = a.colsum;
+  p.row_scale = a.row_scale;
   p.B = a.B;
   p.T = a.T;
   p.K = a.K;
   p.N = a.N;
   const int smem = (int)sizeof(G::Smem) + 1024;
   if (a.row_stats && !a.colsum) return (int)cudaErrorInvalidValue;
-  auto kern = a.col_scale ? (a.row_stats ? G::gemm_glu_dw_kernel<true, true> : G::gemm_glu_dw_kernel<true, false>)
-                          : (a.row_stats ? G::gemm_glu_dw_kernel<false, true> : G::gemm_glu_dw_kernel<false, false>);
+  auto kern = a.a_int8 ? G::gemm_glu_dw_kernel<true, false, true>
+             : a.col_scale ? (a.row_stats ? G::gemm_glu_dw_kernel<true, true> : G::gemm_glu_dw_kernel<true, false>)
+                           : (a.row_stats ? G::gemm_glu_dw_kernel<false, true> : G::gemm_glu_dw_kernel<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int64_t units = (int64_t)a.B * (a.N / G::BN);

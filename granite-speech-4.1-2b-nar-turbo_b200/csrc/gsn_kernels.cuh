@@ -75,6 +75,8 @@ struct GemmDwArgs {
   int B, T, K, N;
   const float2* row_stats;       // LayerNorm folded in: a = raw frames, per-row (rstd, rstd * mean) [B*T]; or null
   const float* colsum;           // with row_stats: [N] column sums of w
+  int a_int8 = 0;                // W8A8: a int8 [B*T, K], w int8 [N, K] (kind::i8), needs col_scale and row_scale
+  const float* row_scale = nullptr;
 };
 int launch_gemm_glu_dw(const GemmDwArgs& args, cudaStream_t stream);
 

@@ -86,3 +86,17 @@ def test_module_w8a8_compile_fullgraph():
     x = torch.randn((2, 128, synth.D_MODEL), device=DEV).bfloat16()
     f = lambda x: ops.run_conv_module(x, p, w8a8=True)  # noqa: E731
     assert torch.equal(torch.compile(f, fullgraph=True)(x), f(x))
+
+
+def test_module_w8a8_fused_equals_unfused():
+    """T on the 128 grid runs GLU, depthwise and SiLU inside the kind::i8 up_conv kernel; T off the grid runs the
+    int8 GEMM, then the depthwise kernel.  The same utterances through both (T = 256 and the same frames padded to
+    T = 257, equal lengths) give bit-identical valid frames."""
+    params = synth.make_params(3001)
+    p = prepare_from_params(params, device=DEV, int8=True)
+    x = O.bf16_round(synth.make_activations(3501, (3, 257, synth.D_MODEL)))
+    lens = torch.tensor([256, 201, 77], dtype=torch.int32, device=DEV)
+    y_grid = ops.run_conv_module(_t(x[:, :256]), p, lengths=lens, w8a8=True).float().cpu().numpy()
+    y_off = ops.run_conv_module(_t(x), p, lengths=lens, w8a8=True).float().cpu().numpy()
+    for b, L in enumerate(lens.tolist()):
+        np.testing.assert_array_equal(y_grid[b, :L], y_off[b, :L])
