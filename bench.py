@@ -54,6 +54,8 @@ ATTN_FLOP_PER_QUERY_KEY = 3 * 2 * DIM_HEAD * HEADS      # 6144
 # rows); the traffic of a launch scales with the rows it computes.
 GEMM1DW_DRAM_BYTES_PER_ROW = 5019
 DW_BYTES_PER_FRAME = 2 * I * 2                # read + write bf16: 8192 B
+DW_GLU_BYTES_PER_FRAME = 3 * I * 2            # GLU form: read value + gate, write: 12288 B
+DW_WORKLOADS = ("dw", "dw_cf", "dw_cf_glu")
 METRIC = "conv-module frames/s at 1/2/4/8 B200; % of HBM / tensor-pipe roofline"
 
 
@@ -144,7 +146,7 @@ def _workload_plan(rank: int, workload: str):
         lens = synth.sample_lengths(1003 + 7919 * rank, 48)
         T = synth.round_up(int(lens.max()), synth.FRAME_GRID)
         return [dispatch.Chunk(index=np.arange(48), lengths=lens, T=T)]
-    if workload == "dw":
+    if workload in DW_WORKLOADS:
         return [dispatch.Chunk(index=np.arange(48), lengths=np.full(48, 1024, np.int32), T=1024)]
     raise ValueError(workload)
 
@@ -161,7 +163,7 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
     from oracle import attention as ATO
     from oracle import feed_forward as FFO
     chunks = _workload_plan(rank, workload)
-    if workload == "dw":
+    if workload in DW_WORKLOADS:
         w, b = synth.make_dw_weights(1002)
         wb, bb = O.bf16_round(w), O.bf16_round(b)
     elif workload == "ff":
@@ -186,9 +188,12 @@ def cpu_oracle_rate(workload: str, budget_s: float, rank: int = 0):
         c = chunks[i % len(chunks)]
         B = min(c.B, 4)
         T = int(c.lengths[:B].max())
-        x = synth.make_activations(77 + i, (B, T, I if workload == "dw" else D))
+        x = synth.make_activations(77 + i, (B, T, (2 * I if workload == "dw_cf_glu" else I)
+                                               if workload in DW_WORKLOADS else D))
         lens = c.lengths[:B]
-        if workload == "dw":
+        if workload == "dw_cf_glu":
+            O.dwconv_silu_glu(x, wb, bb, lengths=lens)
+        elif workload in DW_WORKLOADS:
             O.dwconv_silu(x, wb, bb, lengths=lens, round_out=False)
         elif workload == "ff":
             FFO.feed_forward_half(x, ffprep, lengths=lens, mode="fp32", dtype=np.float32)
@@ -248,6 +253,10 @@ def _config(args, world):
         "module_w8a8": "one conv module with int8 per-channel weights and per-row int8 activations (kind::i8 MMAs, "
                        "s32 accumulate), B=48 chunk, lognormal lengths, length mask",
         "dw": "depthwise k15 + bias + SiLU alone, bf16 [48, 1024, 2048] channels-last, all frames valid",
+        "dw_cf": "depthwise k15 + bias + SiLU alone at the reference op's call site: bf16 (48, 2048, 1024) "
+                 "channels-first (T innermost, contiguous), all frames valid",
+        "dw_cf_glu": "GLU + depthwise k15 + bias + SiLU alone (granite::dwconv_silu_glu at the reference's call site): "
+                     "bf16 (48, 4096, 1024) channels-first up_conv output -> (48, 2048, 1024), all frames valid",
         "ff": "one feed-forward half of the Conformer block (LN, 1024->4096 GEMM+SiLU, 4096->1024 GEMM + 0.5x "
               "residual), B=48 chunk, lognormal lengths, T on the 128-frame grid, length mask",
         "attn": "one attention step of the Conformer block (LN, 1024->3072 q|k|v GEMM, block-local attention over "
@@ -299,12 +308,17 @@ def run_ours(args):
 
     # ---- resident inputs and weights
     gen = torch.Generator(device=dev).manual_seed(1005 + rank)
-    if workload == "dw":
+    if workload in DW_WORKLOADS:
         w, b = synth.make_dw_weights(1002)
         dw_w = torch.from_numpy(w).to(torch.bfloat16).to(dev)
         dw_b = torch.from_numpy(b).to(torch.bfloat16).to(dev)
-        xs = [torch.randn((c.B, c.T, I), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
-        ys = [torch.empty_like(x) for x in xs]
+        if workload == "dw":          # [B, T, C] rows
+            xs = [torch.randn((c.B, c.T, I), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+            ys = [torch.empty_like(x) for x in xs]
+        else:                         # (B, C_in, T) contiguous, T innermost
+            cin = 2 * I if workload == "dw_cf_glu" else I
+            xs = [torch.randn((c.B, cin, c.T), generator=gen, device=dev).to(torch.bfloat16) for c in chunks]
+            ys = [torch.empty((c.B, I, c.T), dtype=torch.bfloat16, device=dev) for c in chunks]
         layers = []
     elif workload == "ff":
         from granite_conv_b200.weights import prepare_ff_from_params
@@ -585,14 +599,19 @@ def run_ours(args):
     def step(record=False):
         n = 0
         for ci, c in enumerate(chunks):
-            if workload == "dw":
+            if workload in DW_WORKLOADS:
                 x, y = xs[ci], ys[ci]
                 if record:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e1 = torch.cuda.Event(enable_timing=True)
                     e0.record(stream)
-                _lib.check(L.gsn_dwconv_silu_bf16(x.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), y.data_ptr(),
-                                                  c.B, I, c.T, 15, c.T * I, 1, I, c.T * I, 1, I, 0, sp), "dwconv")
+                if workload == "dw":
+                    _lib.check(L.gsn_dwconv_silu_bf16(x.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), y.data_ptr(),
+                                                      c.B, I, c.T, 15, c.T * I, 1, I, c.T * I, 1, I, 0, sp), "dwconv")
+                else:
+                    entry = L.gsn_dwconv_silu_glu_bf16 if workload == "dw_cf_glu" else L.gsn_dwconv_silu_bf16
+                    _lib.check(entry(x.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), y.data_ptr(), c.B, I, c.T, 15,
+                                     *x.stride(), *y.stride(), 0, sp), "dwconv")
                 if record:
                     e1.record(stream)
                     dw_events.append((e0, e1, c.padded_frames))
@@ -670,13 +689,16 @@ def run_ours(args):
     value = valid_all * args.steps / (ms / 1e3)
 
     peaks = _peaks()
-    if workload == "dw":
+    if workload in DW_WORKLOADS:
         dur = sum(a.elapsed_time(b) for a, b, _ in dw_events) / len(dw_events)
         frames = sum(m for _, _, m in dw_events) / len(dw_events)
-        achieved = frames * DW_BYTES_PER_FRAME / (dur / 1e3) / 1e9
-        roof = {"kernel": "dwconv_cl_kernel", "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+        bpf = DW_GLU_BYTES_PER_FRAME if workload == "dw_cf_glu" else DW_BYTES_PER_FRAME
+        achieved = frames * bpf / (dur / 1e3) / 1e9
+        roof = {"kernel": "dwconv_cl_kernel" if workload == "dw" else
+                          "dwconv_cf_tma_kernel<GLU>" if workload == "dw_cf_glu" else "dwconv_cf_tma_kernel",
+                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                "per_launch_ms": dur, "algorithmic_bytes_per_frame": DW_BYTES_PER_FRAME,
+                "per_launch_ms": dur, "algorithmic_bytes_per_frame": bpf,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
     elif w8a8:
         dur = sum(a.elapsed_time(b) for a, b, _ in w8_events) / len(w8_events)
@@ -736,7 +758,9 @@ def run_ours(args):
 
     # ---- end to end through the public op with pinned host buffers
     e2e = None
-    if workload not in ("dw", "module_w8a8") and not args.no_e2e:
+    if workload in ("dw_cf", "dw_cf_glu") and not args.no_e2e:
+        e2e = _e2e_dw(args, chunks, xs[0].shape, workload == "dw_cf_glu", dw_w, dw_b, dev, stream, world)
+    elif workload not in ("dw", "module_w8a8") and not args.no_e2e:
         e2e = _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=workload == "ff",
                    attn=workload == "attn", block=workload in ("block", "encoder"), heads=heads)
 
@@ -1023,14 +1047,50 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
                                              "conv_module per layer")) + ", pinned host in/out on two copy streams"}
 
 
+def _e2e_dw(args, chunks, shape, glu, dw_w, dw_b, dev, stream, world):
+    """The depthwise op at the reference's call site end to end: torch.ops.granite.dwconv_silu[_glu] on a (B, C, T)
+    tensor copied from pinned host memory, its output copied back, every step inside the timed region."""
+    import torch
+
+    from granite_conv_b200 import ops  # noqa: F401  (registers the ops)
+    op = torch.ops.granite.dwconv_silu_glu if glu else torch.ops.granite.dwconv_silu
+    g = torch.Generator().manual_seed(4243)
+    hx = torch.randn(shape, generator=g).to(torch.bfloat16).pin_memory()
+    ho = torch.empty((shape[0], I, shape[2]), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    w3 = dw_w[:, None, :]
+
+    def step():
+        xd.copy_(hx, non_blocking=True)
+        y = op(xd, w3, dw_b)
+        ho.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    frames = sum(c.valid_frames for c in chunks)
+    return {"value": frames * args.steps / (ms / 1e3), "unit": "frames/s", "h2d_bytes_per_step": hx.numel() * 2,
+            "d2h_bytes_per_step": ho.numel() * 2, "ms_per_step": ms / args.steps,
+            "path": "torch.ops.granite." + ("dwconv_silu_glu" if glu else "dwconv_silu") +
+                    " on (B, C, T) contiguous, pinned host in/out"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "module_w8a8", "dw", "ff", "attn", "block", "encoder",
-                                           "ctc"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "module", "module_i8", "module_w8a8", "dw", "dw_cf", "dw_cf_glu", "ff",
+                                           "attn", "block", "encoder", "ctc"], default="stack")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
