@@ -873,6 +873,10 @@ int gsn_conv_module_bf16_noalloc(const void* x, const void* ln_w, const void* ln
   const char* name = "gsn_conv_module_bf16_noalloc";
   if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
   if ((int64_t)B * T == 0) return ok();
+  // the same shape rule as the workspace entry point, checked first so an unsupported D or inner is reported as
+  // such rather than as a scratch-size problem
+  if (!ln_dim_ok(D) || (2 * inner) % 256 != 0 || inner % 128 != 0)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: D=%d inner=%d (D in {256..2048}, inner %% 128 == 0)", name, D, inner);
   const size_t need = gsn_conv_module_workspace_bytes(B, T, D, inner);
   if (need > (size_t)GSN_NOALLOC_SCRATCH_BYTES)
     return fail(GSN_ERR_WORKSPACE,
@@ -924,6 +928,29 @@ int gsn_selftest_bounded_wait(uint64_t limit_ns, gsn_stream_t stream) {
   if (limit_ns == 0 || limit_ns > 2000000000ull)
     return fail(GSN_ERR_INVALID_ARG, "selftest: limit_ns must be in (0, 2e9]");
   return finish(launch_wait_selftest(limit_ns, (cudaStream_t)stream), "gsn_selftest_bounded_wait");
+}
+
+int gsn_selftest_gemm_withheld_bf16(const void* d, const void* w, const float* b, const void* residual, void* out,
+                                    int M, int K, int N, gsn_stream_t stream) {
+  const char* name = "gsn_selftest_gemm_withheld_bf16";
+  if (int rc = check_gemm(name, d, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
+  if (residual && !aligned(residual, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: residual must be 16-byte aligned", name);
+  if (K < 128) return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d must span at least two 64-wide K-blocks", name, K);
+  GemmArgs g{(const __nv_bfloat16*)d, w, b, nullptr, (const __nv_bfloat16*)residual, (__nv_bfloat16*)out,
+             (int64_t)N, (int64_t)N, M, N, K, 0, nullptr, 0};
+  g.withhold_load = 1;    // every CTA's second operand load: one K-block of MMAs has run when the wait runs out
+  return finish(launch_gemm(g, kEpiResidual, (cudaStream_t)stream), name);
+}
+
+int gsn_selftest_dwconv_withheld_bf16(const void* x, const void* w, const void* b, void* y, int B, int C, int T,
+                                      int64_t sxB, int64_t sxC, int64_t sxT, int64_t syB, int64_t syC, int64_t syT,
+                                      gsn_stream_t stream) {
+  const char* name = "gsn_selftest_dwconv_withheld_bf16";
+  if (int rc = check_dw(x, w, b, y, B, C, T, 15)) return rc < 0 ? ok() : rc;
+  DwArgs a{(const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, (__nv_bfloat16*)y, nullptr,
+           sxB, sxC, sxT, syB, syC, syT, B, C, T, 0};
+  a.withhold_tile = 0;    // every CTA's first tile
+  return finish(launch_dwconv(a, (cudaStream_t)stream), name);
 }
 
 }  // extern "C"

@@ -80,6 +80,7 @@ struct ClParams {
   const int* lengths;
   int64_t syB, syT;
   int T, C;
+  int withhold;        // test only: tile #k of every CTA armed but never loaded (-1: none)
 };
 
 __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t v) { return make_float2(bf16lo_to_f32(v), bf16hi_to_f32(v)); }
@@ -193,6 +194,7 @@ __global__ void __launch_bounds__(ClCfg<S, GLU>::THREADS, ClCfg<S, GLU>::MIN_CTA
       return;
     }
     mbar_arrive_expect_tx(&s.full[st], kTxBytes);
+    if (i == p.withhold) return;                     // test only: armed, no copy, so the bounded wait runs out
     tma_load_3d(s.x[st][0], &tmX, &s.full[st], c0, t0 - HALO, b);
     if (GLU) tma_load_3d(s.x[st][GLU ? 1 : 0], &tmX, &s.full[st], c0 + p.C, t0 - HALO, b);
   };
@@ -329,6 +331,7 @@ int launch_cl(const DwArgs& a, cudaStream_t stream) {
   p.syT = a.syT;
   p.T = a.T;
   p.C = a.C;
+  p.withhold = a.withhold_tile;
   const int64_t t_chunks = ((int64_t)a.T + Cfg::TT * Cfg::TILES - 1) / (Cfg::TT * Cfg::TILES);
   if (t_chunks > 65535 || a.B > 65535) return (int)cudaErrorInvalidValue;
   auto kern = dwconv_cl_kernel<S, GLU>;
@@ -355,9 +358,13 @@ int launch_cl(const DwArgs& a, cudaStream_t stream) {
 // bit.  Results leave through a per-warp shared box (64 channels x 32 frames, 64-byte swizzle: conflict-free
 // 16-byte writes) and a TMA store, which clips frames past T.
 //
-// The grid is persistent per channel block: CTA (cb, y) keeps the weights of channel block cb in registers and
-// walks the (utterance, time tile) items y, y + Y, y + 2Y, ... through a STAGES-deep ring of TMA boxes.  Tiles
-// past an utterance's end are not loaded and are written as zeros.
+// The grid is persistent: one CTA per resident slot (SMs x CTAs per SM, so there is no partial second wave), each
+// walking its items (channel block, utterance, time tile; time fastest) through a STAGES-deep ring of TMA boxes and
+// loading a channel block's weights into registers when its channel block changes.  Without lengths a CTA takes a
+// contiguous range of items: every CTA has the same work, consecutive time tiles of one row block follow each other
+// (the 16-frame halo the next tile shares is still in L2) and the weights change at most a few times.  With lengths
+// the items are dealt round robin (item k, k + G, ...), so the tiles past utterance ends, which are not loaded and
+// are only written as zeros, spread evenly.
 template <int WARPS_, int STAGES_, int MINB_, int FPW_ = 32>
 struct CfShape {
   static constexpr int WARPS = WARPS_, STAGES = STAGES_, MINB = MINB_, FPW = FPW_;
@@ -403,7 +410,9 @@ struct CfTmaParams {
   const int* lengths;
   int B, C, T;
   int n_tt;            // time tiles per utterance
-  int n_items;         // B * n_tt
+  int per_cb;          // items per channel block: B * n_tt
+  int n_items;         // (C / 64) * per_cb
+  int withhold;        // test only: item #k of every CTA armed but never loaded (-1: none)
 };
 
 // fp32 pairs (lo, hi) from the low / high bf16 halves of two words
@@ -450,15 +459,27 @@ __global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int T = p.T;
-  const int c0 = blockIdx.x * Cfg::CC;
-  const int Y = gridDim.y;
-  const int n_items = p.n_items > (int)blockIdx.y ? (p.n_items - (int)blockIdx.y + Y - 1) / Y : 0;
+  const int G = gridDim.x;
+  const int k = blockIdx.x;
+  int first, step, n_items;
+  if (p.lengths) {                                    // round robin
+    first = k;
+    step = G;
+    n_items = p.n_items > k ? (p.n_items - k + G - 1) / G : 0;
+  } else {                                            // contiguous range
+    first = (int)((int64_t)k * p.n_items / G);
+    step = 1;
+    n_items = (int)((int64_t)(k + 1) * p.n_items / G) - first;
+  }
   constexpr uint32_t kTxBytes = Cfg::NBOX * Cfg::BOX_BYTES;
 
-  auto item = [&](int i, int& b, int& t0) {
-    const int g = (int)blockIdx.y + i * Y;
-    b = g / p.n_tt;
-    t0 = (g - b * p.n_tt) * TT;
+  auto item = [&](int i, int& c0, int& b, int& t0) {
+    const int g = first + i * step;
+    const int cb = g / p.per_cb;
+    const int r = g - cb * p.per_cb;
+    c0 = cb * Cfg::CC;
+    b = r / p.n_tt;
+    t0 = (r - b * p.n_tt) * TT;
   };
   auto len_of = [&](int b) { return p.lengths ? min(max(__ldg(p.lengths + b), 0), T) : T; };
 
@@ -475,13 +496,14 @@ __global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
   // phase without a copy
   auto issue = [&](int i) {
     const int st = i % STAGES;
-    int b, t0;
-    item(i, b, t0);
+    int c0, b, t0;
+    item(i, c0, b, t0);
     if (t0 >= len_of(b)) {
       mbar_arrive(&s.full[st]);
       return;
     }
     mbar_arrive_expect_tx(&s.full[st], kTxBytes);
+    if (i == p.withhold) return;                     // test only: armed, no copy, so the bounded wait runs out
     tma_load_3d(s.x[st][0], &tmX, &s.full[st], t0 - 8, c0, b);
     if (GLU) tma_load_3d(s.x[st][GLU ? 1 : 0], &tmX, &s.full[st], t0 - 8, c0 + p.C, b);
   };
@@ -493,14 +515,16 @@ __global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
   // weights of channels c0 + lane and c0 + lane + 32 as fp32 pairs, halved (exact): the accumulator holds x / 2
   // and silu(x) = h + h * tanh(h)
   pk2 wr[KW];
-  pk2 bias;
-  {
+  pk2 bias = 0ull;
+  int w_c0 = -1;
+  auto load_weights = [&](int c0) {
     const __nv_bfloat16* wa = p.w + (int64_t)(c0 + lane) * KW;
     const __nv_bfloat16* wb = wa + 32 * KW;
 #pragma unroll
     for (int j = 0; j < KW; ++j) wr[j] = pk_make(0.5f * __bfloat162float(wa[j]), 0.5f * __bfloat162float(wb[j]));
     bias = pk_make(0.5f * __bfloat162float(p.bias[c0 + lane]), 0.5f * __bfloat162float(p.bias[c0 + lane + 32]));
-  }
+    w_c0 = c0;
+  };
 
   // this lane's two rows in the warp's output box: rows of OUT_ROW bytes swizzled as the TMA store reads them
   // (16-byte chunk q of row r at q ^ ((r * OUT_ROW / 128) mod (OUT_ROW / 16)); rows l and l + 32 share the mask)
@@ -512,8 +536,9 @@ __global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
   bool alive = true;
   for (int i = 0; i < n_items; ++i) {
     const int st = i % STAGES;
-    int b, t0;
-    item(i, b, t0);
+    int c0, b, t0;
+    item(i, c0, b, t0);
+    if (c0 != w_c0) load_weights(c0);                 // uniform over the CTA
     const int len = len_of(b);
     const int tw = t0 + warp * FPW;                   // first output frame of this warp
     if (alive)
@@ -628,9 +653,12 @@ int launch_cf_tma(const DwArgs& a, cudaStream_t stream) {
   p.C = a.C;
   p.T = a.T;
   p.n_tt = (a.T + Cfg::TT - 1) / Cfg::TT;
-  const int64_t items = (int64_t)a.B * p.n_tt;
+  const int64_t per_cb = (int64_t)a.B * p.n_tt;
+  const int64_t items = per_cb * (a.C / Cfg::CC);
   if (items > (1 << 30)) return (int)cudaErrorInvalidValue;
+  p.per_cb = (int)per_cb;
   p.n_items = (int)items;
+  p.withhold = a.withhold_tile;
   auto kern = dwconv_cf_tma_kernel<S, GLU>;
   const int smem = (int)sizeof(CfSmem<S, GLU>) + 1024;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -645,11 +673,7 @@ int launch_cf_tma(const DwArgs& a, cudaStream_t stream) {
       per_sm = 1;
     if (dev < 8) resident[dev].store(per_sm, std::memory_order_relaxed);
   }
-  const int n_cb = a.C / Cfg::CC;
-  const int slots = device_sm_count() * per_sm;
-  const int64_t ymax = std::min<int64_t>(items, 65535);
-  const int y = (int)std::max<int64_t>(1, std::min<int64_t>(ymax, (slots + n_cb - 1) / n_cb));
-  dim3 grid(n_cb, y);
+  const int grid = (int)std::min<int64_t>(items, (int64_t)device_sm_count() * per_sm);
   kern<<<grid, Cfg::THREADS, smem, stream>>>(tx, ty, p);
   return (int)cudaGetLastError();
 }

@@ -62,6 +62,7 @@ struct KParams {
   float out_scale;                        // residual epilogue: out = out_scale * (acc * scale + bias) + residual
   unsigned long long* argmax_keys;        // ARGMAX: per row, the best (bf16 logit, lowest column) as one key
   int n_major;                            // walk tiles column block by column block (W read once)
+  int withhold_load;                      // test only: operand load #k of every CTA armed but never issued (-1: none)
 };
 
 // 128-row block `blk` of the M range holds at least one valid frame (a block lies inside one utterance)
@@ -239,6 +240,8 @@ struct Epilogue {
   bool has_res;
   int lane, swz;
   uint32_t su;                            // sub-tiles handled so far: buffer su & 1, its use count su >> 1
+  uint32_t res_pend;                      // lane 0: buffers whose residual copy is issued and not yet waited for
+  uint32_t res_par[2];                    //   and the phase parity that copy completes
 
   __device__ void init(EpiSmem& e, int ew, const CUtensorMap* o, const CUtensorMap* r, const KParams& p) {
     vb = e.vec[ew][0];
@@ -258,6 +261,8 @@ struct Epilogue {
     lane = threadIdx.x & 31;
     swz = (lane >> 1) & 3;
     su = 0;
+    res_pend = 0;
+    res_par[0] = res_par[1] = 0;
   }
 
   // The tile's 256 bias (and scale) values into the warp's slice.  For the GLU they are halved:
@@ -288,7 +293,11 @@ struct Epilogue {
     return __uint_as_float(bits);
   }
 
-  __device__ void load_residual(uint32_t buf, int col, int row0) {
+  // residual of sub-tile `sub` (buffer sub & 1, completing that buffer's phase of parity (sub >> 1) & 1)
+  __device__ void load_residual(uint32_t sub, int col, int row0) {
+    const uint32_t buf = sub & 1;
+    res_pend |= 1u << buf;
+    res_par[buf] = (sub >> 1) & 1;
     mbar_arrive_expect_tx(res0 + buf, BOX_BYTES);
     tma_load_2d(stage0 + buf * BOX_BYTES, tmR, res0 + buf, col, row0);
   }
@@ -297,7 +306,7 @@ struct Epilogue {
   __device__ void prefetch_first(int ocol0, int row0) {
     if (has_res && lane == 0) {
       bulk_wait_group_read<0>();          // the buffer's previous store has read it
-      load_residual(su & 1, ocol0, row0);
+      load_residual(su, ocol0, row0);
     }
   }
 
@@ -351,7 +360,7 @@ struct Epilogue {
       if (has_res) {
         if (lane == 0 && u + 1 < NU) {    // prefetch the next residual sub-tile into the other buffer
           bulk_wait_group_read<0>();
-          load_residual(buf ^ 1, ocol0 + (u + 1) * BOX, row0);
+          load_residual(su + 1, ocol0 + (u + 1) * BOX, row0);
         }
       } else {
         if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
@@ -423,6 +432,7 @@ struct Epilogue {
           bool got = mbar_wait_bounded(res0 + buf, (su >> 1) & 1, abort_flag, kStatusTimeoutEpilogue);
           got = __shfl_sync(0xffffffffu, got, 0);
           if (!got) return false;
+          res_pend &= ~(1u << buf);
         }
       }
       // lane = row of the 32 x 32 box; 16-byte chunk c of the row sits at chunk c ^ ((row >> 1) & 3)
@@ -457,7 +467,13 @@ struct Epilogue {
   }
 
   __device__ void finish() {
-    if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed before the CTA ends
+    if (lane == 0) {
+      bulk_wait_group<0>();               // every store of this warp has landed before the CTA ends
+      // after an unwind, residual copies still in flight land before the shared memory is released (bounded)
+      for (uint32_t b = 0; b < 2; ++b)
+        if (res_pend & (1u << b))
+          mbar_wait_bounded(res0 + b, res_par[b], nullptr, kStatusTimeoutEpilogue, 100000000ull);
+    }
     __syncwarp();
   }
 };
@@ -570,7 +586,10 @@ __global__ void __launch_bounds__(Cfg<W_I8>::THREADS, 1)
           break;
         }
         if (lane == 0) {
-          if (W_I8) {
+          if (issued == p.withhold_load) {
+            // test only: the stage is armed for its bytes but no copy is issued, so its phase never completes
+            mbar_arrive_expect_tx(&s.full[stage], W_I8 ? A_BYTES + B8_BYTES : A_BYTES + B_BYTES);
+          } else if (W_I8) {
             mbar_arrive_expect_tx(&s.full[stage], A_BYTES + B8_BYTES);
             tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, m_blk * BM);
             tma_load_2d_hint(s.b8[stage], &tmW, &s.full[stage], kb * BK, n_blk * BN, pol_w);
@@ -1041,6 +1060,7 @@ KParams make_params(const GemmArgs& a) {
   p.out_scale = a.out_scale;
   p.argmax_keys = a.argmax_keys;
   p.n_major = a.n_major;
+  p.withhold_load = a.withhold_load;
   return p;
 }
 

@@ -41,6 +41,8 @@ struct GemmArgs {
   int n_major = 0;               // walk the tiles column block by column block (each W tile read once)
   int a_int8 = 0;                // W8A8: a is int8 [M, K] and w int8 [N, K] (kind::i8 MMAs, s32 accumulate);
   const float* row_scale = nullptr;   //   acc is scaled by row_scale[m] * col_scale[n] (GLU and RESIDUAL only)
+  int withhold_load = -1;        // test only (>= 0): every CTA's producer arms the barrier of its operand load #k
+                                 //   without issuing the copies, so the MMA warp's bounded wait runs out
 };
 
 // LINEAR: out = acc + b, 128-row tiles of pure padding skipped (nothing written there)
@@ -91,6 +93,7 @@ struct DwArgs {
   int64_t sxB, sxC, sxT, syB, syC, syT;
   int B, C, T;
   int glu;
+  int withhold_tile = -1;        // test only (>= 0): every CTA arms the barrier of its tile #k without the copy
 };
 
 int launch_dwconv(const DwArgs& args, cudaStream_t stream);

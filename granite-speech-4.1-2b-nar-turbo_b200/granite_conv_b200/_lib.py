@@ -80,6 +80,9 @@ SIGNATURES = {
     "gsn_interleave_glu_rows": (_i32, [_vp, _vp, _i32, _i64, _vp]),
     "gsn_device_status": (_i32, [ctypes.POINTER(_i32), _i32, _vp]),
     "gsn_selftest_bounded_wait": (_i32, [_u64, _vp]),
+    "gsn_selftest_gemm_withheld_bf16": (_i32, [_vp, _vp, _fp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "gsn_selftest_dwconv_withheld_bf16": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _i64, _i64,
+                                                 _i64, _vp]),
 }
 
 _LIB = None

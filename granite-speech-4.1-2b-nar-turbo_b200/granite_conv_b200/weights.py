@@ -28,7 +28,8 @@ def fold_conv_bn_(model: nn.Module) -> int:
     """In-place fold of BatchNorm1d into the depthwise Conv1d of every conv module; returns how many were
     folded.  Mirrors ``fold_bn.fold_conv_bn_`` (``script/models/granite_speech_nar/fold_bn.py:33-68``)."""
     if model.training:
-        raise RuntimeError("fold_conv_bn_ requires eval mode (call model.eval() first)")
+        raise RuntimeError("fold_conv_bn_: the model is in training mode; switch it with model.eval() so the "
+                           "BatchNorm running statistics are what gets folded")
     folded = 0
     for m in model.modules():
         if not _is_conv_module(m) or isinstance(m.batch_norm, nn.Identity):
@@ -36,7 +37,8 @@ def fold_conv_bn_(model: nn.Module) -> int:
         conv = m.depth_conv.conv
         bn = m.batch_norm
         if bn.running_mean is None or bn.running_var is None:
-            raise RuntimeError("BatchNorm has no running stats; cannot fold")
+            raise RuntimeError("fold_conv_bn_: this BatchNorm1d keeps no running mean/variance "
+                               "(track_running_stats=False), so there is nothing to fold")
         w_dtype = conv.weight.dtype
         scale = bn.weight.detach().float() * torch.rsqrt(bn.running_var.detach().float() + float(bn.eps))
         new_w = conv.weight.detach().float() * scale.reshape(-1, 1, 1)

@@ -310,7 +310,8 @@ int gsn_bpe_head_ctc_bf16(const void* pooled, const int32_t* pooled_lengths, con
  * gsn_conv_module_workspace_bytes(B, T, D, inner) <= 32 MiB (at D = 1024, inner = 2048: B * T <= 4096 frames)
  * and larger problems are rejected with GSN_ERR_WORKSPACE.  Nothing is allocated, neither here nor per call.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
- * current, so make the first call on each device before any stream capture.  Every call shares the one array:
+ * current, so make the first call on each device before any stream capture; that address is kept for the life of
+ * the process, so resetting a device (cudaDeviceReset) after its first call is not supported.  Every call shares the one array:
  * calls that may overlap on the GPU (other streams, other host threads) race on it and must be serialised by the
  * caller.  The array keeps the previous call's contents; the module writes every scratch byte it reads, so
  * nothing needs clearing between calls. */
@@ -333,6 +334,23 @@ int gsn_interleave_glu_rows(const void* src, void* dst, int rows, int64_t row_by
  * nothing will complete, with a limit of limit_ns (<= 2e9); the status word then reads 0x1FF. */
 int gsn_device_status(int* status, int clear, gsn_stream_t stream);
 int gsn_selftest_bounded_wait(uint64_t limit_ns, gsn_stream_t stream);
+
+/* Test entry points for the unwind path of the production kernels (no reference counterpart).  Each launches the
+ * kernel on the caller's operands with one TMA copy per CTA armed on its barrier but never issued, so a bounded
+ * wait runs out (after 2 s) as it would if a copy never arrived:
+ *   gsn_selftest_gemm_withheld_bf16: the down_conv + residual GEMM (operands as gsn_gemm2_residual_bf16, dense
+ *     row strides, K >= 128), withholding each CTA's second operand load, so one K-block of MMAs has run into the
+ *     TMEM accumulator when the MMA warp gives up;
+ *   gsn_selftest_dwconv_withheld_bf16: the depthwise kernel (operands as gsn_dwconv_silu_bf16, without lengths),
+ *     withholding each CTA's first tile; the layouts the TMA kernels take (channels-last rows, or T innermost with
+ *     16-byte aligned rows and C % 64 == 0) exercise it.
+ * Every role then unwinds: copies in flight land, TMEM is freed, the kernel returns, and gsn_device_status reads a
+ * timeout code (0x101-0x104).  The output is left partly written; the context stays usable. */
+int gsn_selftest_gemm_withheld_bf16(const void* d, const void* w, const float* b, const void* residual, void* out,
+                                    int M, int K, int N, gsn_stream_t stream);
+int gsn_selftest_dwconv_withheld_bf16(const void* x, const void* w, const void* b, void* y, int B, int C, int T,
+                                      int64_t sxB, int64_t sxC, int64_t sxT, int64_t syB, int64_t syC, int64_t syT,
+                                      gsn_stream_t stream);
 
 #ifdef __cplusplus
 }

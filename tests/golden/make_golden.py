@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this folder by running the reference's own eager PyTorch code on the CPU.
 
-Run from the repository root in a container where the reference is mounted read-only at /root/reference:
+Run from the repository root, naming the reference checkout (read-only is fine) as the argument or in
+``GRANITE_REFERENCE_ROOT``:
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py <reference root>
 
 What it runs (all on CPU, PyTorch eager, imported unmodified from ``<reference>/script``):
 
@@ -371,4 +372,7 @@ def _encoder_golden(EC, fold, out):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GRANITE_REFERENCE_ROOT", "")
+    if not root:
+        sys.exit("usage: make_golden.py <reference root>  (or set GRANITE_REFERENCE_ROOT)")
+    main(root)

@@ -152,3 +152,14 @@ def test_validation_of_ctc_head_entry_points():
     assert head(p, p, p, p, 1024, 7, p, p, p, 2, 100, 1024, p, 4096, None) == 2         # Pp % 128
     assert head(p, p, p, p, 1024, 7, p, p, p, 2, 128, 1024, p, 100, None) == 5
     assert head(None, None, None, None, 1024, 7, None, None, None, 0, 128, 1024, None, 0, None) == 0
+
+
+def test_selftest_withheld_validation_without_gpu():
+    """The unwind-path test entry points check their operands like the entry points they mirror."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)
+    assert L.gsn_selftest_gemm_withheld_bf16(p, p, p, p, p, 128, 64, 256, None) == 2
+    assert "K=64" in _lib.last_error()
+    assert L.gsn_selftest_gemm_withheld_bf16(p, p, p, p, p, 128, 1024, 100, None) == 2     # N % 256
+    assert L.gsn_selftest_dwconv_withheld_bf16(p, p, p, p, -1, 8, 8, 64, 8, 1, 64, 8, 1, None) == 1
+    assert L.gsn_selftest_gemm_withheld_bf16(None, None, None, None, None, 0, 1024, 1024, None) == 0   # empty

@@ -217,3 +217,39 @@ def test_oracle_quantize_rows_properties():
     assert np.all(err <= s.astype(np.float64)[:, None] / 2 * (1 + 1e-5))   # fp32 division rounds x / s
     rows = [r for r in range(64) if r != 7]
     assert np.all(np.abs(q[rows]).max(axis=1) == 127)
+
+
+def test_torch_eager_restatement_matches_reference():
+    """oracle/torch_eager.py (the CPU baseline's timed code) makes the reference's eager op calls: it reproduces the
+    reference's own outputs bit for bit, fp32 (B=1, T=256) and bf16 (B=2, T=37, two weight scales), and its BN fold
+    equals the reference's folded weights."""
+    import torch
+
+    from oracle.torch_eager import EagerConvModule
+    g = _load("module_fp32_b1t256.npz")
+    m = EagerConvModule(synth.make_params(1001), torch.float32)
+    np.testing.assert_array_equal(m.dw_w[:, 0, :].numpy(), g["dw_weight_folded"])
+    np.testing.assert_array_equal(m.dw_b.numpy(), g["dw_bias_folded"])
+    y = m(torch.from_numpy(synth.make_activations(1501, (1, 256, synth.D_MODEL)))).numpy().reshape(-1)
+    np.testing.assert_array_equal(y[g["sample_idx"]], g["sample"])
+    for tag, seed, w_std in (("w002", 1003, 0.02), ("w006", 2003, 0.06)):
+        g = _load(f"module_bf16_b2t37_{tag}.npz")
+        m = EagerConvModule(synth.make_params(seed, w_std=w_std), torch.bfloat16)
+        np.testing.assert_array_equal(O.bf16_bits(m.dw_w[:, 0, :].float().numpy()), g["dw_weight_folded"])
+        x = torch.from_numpy(O.bf16_round(synth.make_activations(seed + 500, (2, 37, synth.D_MODEL))))
+        y = m(x.to(torch.bfloat16)).float().numpy()
+        np.testing.assert_array_equal(O.bf16_bits(y), g["full"])
+
+
+def test_torch_eager_dwconv_matches_reference():
+    import torch
+
+    from oracle import torch_eager as TE
+    g = _load("dwconv_silu_b1c2048t37.npz")
+    w, b = synth.make_dw_weights(1002)
+    wt = torch.from_numpy(w).to(torch.bfloat16)
+    bt = torch.from_numpy(b).to(torch.bfloat16)
+    x = torch.from_numpy(O.bf16_round(synth.make_activations(1502, (1, 2048, 37)))).to(torch.bfloat16)
+    np.testing.assert_array_equal(O.bf16_bits(TE.dwconv_silu(x, wt, bt).float().numpy()), g["eager"])
+    x2 = torch.from_numpy(O.bf16_round(synth.make_activations(1602, (1, 4096, 37)))).to(torch.bfloat16)
+    np.testing.assert_array_equal(O.bf16_bits(TE.dwconv_silu_glu(x2, wt, bt).float().numpy()), g["eager_glu"])

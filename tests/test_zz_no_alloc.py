@@ -46,12 +46,13 @@ def _no_alloc(p, x, lens):
 
 
 def test_no_alloc_matches_workspace_entry_point_twice():
-    """Two calls in a row with different shapes and masks: each equals the workspace entry point (the second
-    call starts from the first call's leftovers in the shared scratch)."""
+    """Two calls in a row: a dense call that fills the whole scratch (4096 frames), then a smaller masked one that
+    starts from the first call's leftovers in the shared array.  The two entry points run the same kernels on the
+    same inputs, so each output must equal the workspace entry point's bit for bit."""
     p = prepare_from_params(synth.make_params(4242, w_std=0.05), device=DEV)
     cases = [
+        ((4, 1024), None),
         ((3, 256), np.array([256, 200, 37], dtype=np.int32)),
-        ((2, 384), None),
     ]
     for i, ((B, T), lens) in enumerate(cases):
         x = torch.from_numpy(O.bf16_round(synth.make_activations(777 + i, (B, T, synth.D_MODEL)))).to(
@@ -60,6 +61,7 @@ def test_no_alloc_matches_workspace_entry_point_twice():
         y = _no_alloc(p, x, lt)
         ref = _with_workspace(p, x, lt)
         torch.cuda.synchronize()
+        assert torch.equal(y, ref), f"no-alloc call {i} differs from the workspace entry point"
         assert_bf16_close(y, ref, f"no-alloc call {i} vs workspace entry point")
     assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
 
@@ -72,3 +74,7 @@ def test_no_alloc_refuses_problems_above_its_scratch():
     rc = L.gsn_conv_module_bf16_noalloc(*_args(p, x, None, out), 2, 4096, synth.D_MODEL, p.d_inner, p.ln_eps,
                                         torch.cuda.current_stream().cuda_stream)
     assert rc == 5 and "33554432" in _lib.last_error()
+    # an unsupported width is reported as unsupported (GSN_ERR_UNSUPPORTED = 2), not as a scratch-size problem
+    rc = L.gsn_conv_module_bf16_noalloc(*_args(p, x, None, out), 2, 4096, 768, p.d_inner, p.ln_eps,
+                                        torch.cuda.current_stream().cuda_stream)
+    assert rc == 2, (rc, _lib.last_error())
