@@ -534,10 +534,6 @@ def run_ours(args):
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     h_buf = ws                                                         # [M, I] GLU output
     t_off = ((max_m * I * 2 + 255) // 256) * 256
-    # int8: both weight matrices widened to bf16 once per layer call, as gsn_conv_module_i8w does when its
-    # workspace has room for them
-    w1b = torch.empty((2 * I, D), dtype=torch.bfloat16, device=dev) if int8 else None
-    w2b = torch.empty((D, I), dtype=torch.bfloat16, device=dev) if int8 else None
     if heads is not None:
         from granite_conv_b200.ops import pooled_frames
         hsc, hbpe = heads
@@ -560,8 +556,9 @@ def run_ours(args):
     def layer_kernels(x, out, c, p, lens, record):
         """The kernels of one conv module (the same launches the module op makes for T on the 128 grid): bf16
         weights: LayerNorm statistics, up_conv + GLU + depthwise + SiLU on the raw frames with the LayerNorm folded
-        in, down_conv + residual (gsn_conv_module_lnfold_bf16); int8 weights: their widening, LayerNorm, the fused
-        up_conv kernel on the LayerNorm output, down_conv + residual.  CUDA events between them when `record`."""
+        in, down_conv + residual (gsn_conv_module_lnfold_bf16); int8 weights (widened to bf16 once, when the layer was
+        prepared): LayerNorm, the fused up_conv kernel on the LayerNorm output with the column scales, down_conv +
+        residual (gsn_conv_module_i8w_widened).  CUDA events between them when `record`."""
         M = c.padded_frames
         if w8a8:
             # the four launches of gsn_conv_module_w8a8 for T on the 128 grid (LayerNorm + quantise, kind::i8 up_conv
@@ -582,15 +579,6 @@ def run_ours(args):
         tp = h_buf.data_ptr() + t_off           # LayerNorm output [M, D]
         lp, T = lens.data_ptr(), c.T
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
-        if int8:
-            wev = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if record else None
-            if record:
-                wev[0].record(stream)
-            _lib.check(L.gsn_widen_i8_bf16(p.w1q_glu.data_ptr(), w1b.data_ptr(), 2 * I * D, p.w2q.data_ptr(),
-                                           w2b.data_ptr(), D * I, sp), "widen")
-            if record:
-                wev[1].record(stream)
-                widen_events.append(wev)
         if record:
             ev[0].record(stream)
         if int8:
@@ -601,7 +589,7 @@ def run_ours(args):
         if record:
             ev[1].record(stream)
         if int8:
-            _lib.check(L.gsn_gemm1_glu_dwconv_bf16(tp, w1b.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(),
+            _lib.check(L.gsn_gemm1_glu_dwconv_bf16(tp, p.w1w_glu.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(),
                                                    p.dw_w.data_ptr(), p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp,
                                                    sp), "gemm1_dw")
         else:
@@ -612,7 +600,7 @@ def run_ours(args):
         if record:
             ev[2].record(stream)
         if int8:
-            _lib.check(L.gsn_gemm2_residual_bf16s(dp, w2b.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
+            _lib.check(L.gsn_gemm2_residual_bf16s(dp, p.w2w.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
                                                   x.data_ptr(), D, out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
         else:
             _lib.check(L.gsn_gemm2_residual_bf16(dp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
@@ -806,7 +794,7 @@ def run_ours(args):
                         n += 3
                 else:
                     layer_kernels(src, dst, c, p, lens_dev[ci], record)
-                    n += 4 if w8a8 else (4 if int8 else 3)
+                    n += 4 if w8a8 else 3
                 src = dst
             if workload == "ctc":
                 selfcond_kernels(xs[ci], act[ci], c, lens_dev[ci], record)
@@ -859,7 +847,7 @@ def run_ours(args):
         bpf = DW_GLU_BYTES_PER_FRAME if workload == "dw_cf_glu" else DW_BYTES_PER_FRAME
         achieved = frames * bpf / (dur / 1e3) / 1e9
         roof = {"kernel": "dwconv_cl_kernel" if workload == "dw" else
-                          "dwconv_cf_tma_kernel<GLU>" if workload == "dw_cf_glu" else "dwconv_cf_tma_kernel",
+                          "dwconv_cf_tma_kernel<GLU>" if workload == "dw_cf_glu" else "dwconv_cf_mma_kernel",
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": bpf,

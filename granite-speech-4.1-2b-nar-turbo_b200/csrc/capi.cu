@@ -647,8 +647,9 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   __nv_bfloat16* h = (__nv_bfloat16*)ws;
   __nv_bfloat16* t = (__nv_bfloat16*)((char*)ws + align256((size_t)M * inner * 2));
   const cudaStream_t st = (cudaStream_t)stream;
-  int w_i8 = i8;
-  if (i8 && ws_bytes >= gsn_conv_module_i8w_workspace_bytes(B, T, D, inner)) {
+  // i8: 0 bf16 weights, 1 int8 weights, 2 int8 weights widened to bf16 once by the caller (scales still apply)
+  int w_i8 = i8 == 1;
+  if (i8 == 1 && ws_bytes >= gsn_conv_module_i8w_workspace_bytes(B, T, D, inner)) {
     if (!aligned(w1, 16) || !aligned(w2, 16))
       return fail(GSN_ERR_UNSUPPORTED, "%s: int8 weights must be 16-byte aligned", name);
     void* w1b = (char*)ws + need;
@@ -738,6 +739,15 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                         size_t workspace_bytes, gsn_stream_t stream) {
   return conv_module(x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths, add_residual, out, B,
                      T, D, inner, ln_eps, workspace, workspace_bytes, 1, stream, "gsn_conv_module_i8w");
+}
+
+int gsn_conv_module_i8w_widened(const void* x, const void* ln_w, const void* ln_b, const void* w1w_glu,
+                                const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,
+                                const void* w2w, const float* s2, const float* b2, const int32_t* lengths,
+                                int add_residual, void* out, int B, int T, int D, int inner, float ln_eps,
+                                void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  return conv_module(x, ln_w, ln_b, w1w_glu, s1_glu, b1_glu, dw_w, dw_b, w2w, s2, b2, lengths, add_residual, out, B,
+                     T, D, inner, ln_eps, workspace, workspace_bytes, 2, stream, "gsn_conv_module_i8w_widened");
 }
 
 int gsn_quant_rows_bf16(const void* x, int64_t ldx, void* q, float* scale, int M, int K, const int32_t* lengths,

@@ -244,6 +244,16 @@ __global__ void __launch_bounds__(ClCfg<S, GLU>::THREADS, ClCfg<S, GLU>::MIN_CTA
       auto tile = [&](auto masked_tag) {
         constexpr bool MASKED = decltype(masked_tag)::value;
         pk2 acc[FPW][NP];  // frame f starts from the bias at its first tap (row r = f), as bias + w0 x0 + w1 x1 ...
+        uint32_t o[FPW][NP];                           // the packed outputs
+        auto silu_frame = [&](int f) {
+          const bool valid = !MASKED || t0 + row0 + f < len;
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            const float2 h = pk_split(acc[f][q]);
+            const float2 s2 = pk_split(pk_fma(acc[f][q], pk_make(tanh_approx(h.x), tanh_approx(h.y)), acc[f][q]));
+            o[f][q] = valid ? pack_bf16x2(s2.x, s2.y) : 0u;
+          }
+        };
         const int t_row0 = t0 - HALO + row0;
         const uint8_t* xa = s.x[st][0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
         const uint8_t* xg = s.x[st][GLU ? 1 : 0] + row0 * Cfg::ROW_BYTES + lane * (CPT * 2);
@@ -277,19 +287,12 @@ __global__ void __launch_bounds__(ClCfg<S, GLU>::THREADS, ClCfg<S, GLU>::MIN_CTA
             }
           }
         }
+#pragma unroll
+        for (int f = 0; f < FPW; ++f) silu_frame(f);
         __nv_bfloat16* yt = yb + (int64_t)(t0 + row0) * p.syT;
 #pragma unroll
         for (int f = 0; f < FPW; ++f, yt += p.syT) {
-          const int t = t0 + row0 + f;
-          uint32_t o[NP];
-          const bool valid = !MASKED || t < len;
-#pragma unroll
-          for (int q = 0; q < NP; ++q) {
-            const float2 h = pk_split(acc[f][q]);
-            const float2 s2 = pk_split(pk_fma(acc[f][q], pk_make(tanh_approx(h.x), tanh_approx(h.y)), acc[f][q]));
-            o[q] = valid ? pack_bf16x2(s2.x, s2.y) : 0u;
-          }
-          if (!MASKED || t < T) stg_words<NP>(yt, o);
+          if (!MASKED || t0 + row0 + f < T) stg_words<NP>(yt, o[f]);
         }
       };
       if (t0 + TT + HALO <= len)
@@ -554,6 +557,16 @@ __global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
       } else {
         auto body = [&](auto masked_tag) {
           constexpr bool MASKED = decltype(masked_tag)::value;
+          // SiLU of frames f and f + 1 (halved accumulators: silu(x) = h + h tanh(h)), packed per row
+          auto silu_pair = [&](const pk2 (&acc)[FPW], int f) {
+            const float2 h0 = pk_split(acc[f]);
+            const float2 h1 = pk_split(acc[f + 1]);
+            const float2 s0 = pk_split(pk_fma(acc[f], pk_make(tanh_approx(h0.x), tanh_approx(h0.y)), acc[f]));
+            const float2 s1 = pk_split(pk_fma(acc[f + 1], pk_make(tanh_approx(h1.x), tanh_approx(h1.y)), acc[f + 1]));
+            const bool v0 = !MASKED || tw + f < len, v1 = !MASKED || tw + f + 1 < len;
+            wa[f / 2] = pack_bf16x2(v0 ? s0.x : 0.f, v1 ? s1.x : 0.f);
+            wb[f / 2] = pack_bf16x2(v0 ? s0.y : 0.f, v1 ? s1.y : 0.f);
+          };
           pk2 acc[FPW];
           const uint8_t* ra = s.x[st][0] + lane * Cfg::ROW_BYTES + warp * (FPW * 2);
           const uint8_t* rb = ra + 32 * Cfg::ROW_BYTES;
@@ -585,15 +598,7 @@ __global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
             }
           }
 #pragma unroll
-          for (int f = 0; f < FPW; f += 2) {
-            const float2 h0 = pk_split(acc[f]);
-            const float2 h1 = pk_split(acc[f + 1]);
-            const float2 s0 = pk_split(pk_fma(acc[f], pk_make(tanh_approx(h0.x), tanh_approx(h0.y)), acc[f]));
-            const float2 s1 = pk_split(pk_fma(acc[f + 1], pk_make(tanh_approx(h1.x), tanh_approx(h1.y)), acc[f + 1]));
-            const bool v0 = !MASKED || tw + f < len, v1 = !MASKED || tw + f + 1 < len;
-            wa[f / 2] = pack_bf16x2(v0 ? s0.x : 0.f, v1 ? s1.x : 0.f);
-            wb[f / 2] = pack_bf16x2(v0 ? s0.y : 0.f, v1 ? s1.y : 0.f);
-          }
+          for (int f = 0; f < FPW; f += 2) silu_pair(acc, f);
         };
         if (len < T && tw + FPW + HALO > len)
           body(std::true_type{});
@@ -791,6 +796,11 @@ int launch_dwconv(const DwArgs& a, cudaStream_t stream) {
                      (a.syC % 8) == 0 && (a.syB % 8) == 0 && a.sxC >= a.T && a.syC >= a.T && a.sxB >= cx * a.sxC &&
                      a.syB >= (int64_t)a.C * a.syC && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+  // the plain form on the tensor cores (dwconv_mma_sm100.cu), the GLU form on the CUDA cores
+  const bool mma_ok = a.sxT == 1 && a.syT == 1 && !a.glu && (a.C % 16) == 0 && (a.sxC % 8) == 0 &&
+                      (a.sxB % 8) == 0 && (a.syC % 8) == 0 && (a.syB % 8) == 0 && a.sxC >= a.T && a.syC >= a.T &&
+                      (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+  if (mma_ok) return launch_dwconv_cf_mma(a, stream);
   if (cf_ok)
     return a.glu ? launch_cf_tma<CfShapeGlu, true>(a, stream) : launch_cf_tma<CfShapePlain, false>(a, stream);
   CfParams p{a.x, a.w, a.bias, a.y, a.lengths, a.sxB, a.sxC, a.sxT, a.syB, a.syC, a.syT, a.C, a.T};

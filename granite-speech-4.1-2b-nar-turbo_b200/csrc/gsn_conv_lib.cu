@@ -2,6 +2,7 @@
 // definition visible to every kernel without relocatable device code.
 #include "layernorm.cu"
 #include "dwconv.cu"
+#include "dwconv_mma_sm100.cu"
 #include "gemm_sm100.cu"
 #include "quant_rows.cu"
 #include "gemm_glu_dw_sm100.cu"

@@ -97,6 +97,9 @@ struct DwArgs {
 };
 
 int launch_dwconv(const DwArgs& args, cudaStream_t stream);
+// the channels-first form on the tensor cores (dwconv_mma_sm100.cu): T innermost in x and y, no GLU, C % 16 == 0,
+// 16-byte aligned rows (element strides of C and B multiples of 8)
+int launch_dwconv_cf_mma(const DwArgs& args, cudaStream_t stream);
 
 // ---- LayerNorm over the last dim (layernorm.cu) -------------------------------------------------------------
 // lengths (optional): rows r with r % T >= lengths[r / T] are padding and are skipped.

@@ -71,6 +71,8 @@ SIGNATURES = {
                                     _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
     "gsn_conv_module_i8w": (_i32, [_vp, _vp, _vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _fp, _vp, _i32, _vp,
                                    _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
+    "gsn_conv_module_i8w_widened": (_i32, [_vp, _vp, _vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _fp, _vp, _i32, _vp,
+                                           _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),
     "gsn_conv_module_w8a8_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "gsn_conv_module_w8a8": (_i32, [_vp, _vp, _vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _fp, _vp, _i32, _vp,
                                     _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp]),

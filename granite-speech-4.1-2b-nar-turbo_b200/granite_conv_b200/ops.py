@@ -199,13 +199,21 @@ def conv_module_i8w(x: torch.Tensor, ln_w: torch.Tensor, ln_b: torch.Tensor, w1q
                     w2q: torch.Tensor, s2: torch.Tensor, b2: torch.Tensor, lengths: Optional[torch.Tensor],
                     ln_eps: float, add_residual: bool) -> torch.Tensor:
     """conv_module with int8 per-output-channel weights on both pointwise GEMMs (bf16 activations, fp32
-    accumulate, the scale applied in the epilogue)."""
+    accumulate, the scale applied in the epilogue).  ``w1q_glu`` / ``w2q`` are the int8 weights, or their exact
+    bf16 copies widened once beforehand (``PreparedConvModule.w1w_glu`` / ``w2w``), which skips the per-call
+    widening."""
     name = "granite::conv_module_i8w"
     _require_cuda(name, x, ln_w, ln_b, w1q_glu, s1_glu, b1_glu, dw_w, dw_b, w2q, s2, b2, lengths)
-    # workspace with room for both weight matrices widened to bf16: the GEMMs then run on bf16 tiles
-    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(name, x, ln_w, dw_w, lengths,
-                                                               "gsn_conv_module_i8w_workspace_bytes")
-    _lib.call("gsn_conv_module_i8w", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w1q_glu.data_ptr(),
+    widened = w1q_glu.dtype == torch.bfloat16
+    if widened != (w2q.dtype == torch.bfloat16) or (not widened and (w1q_glu.dtype != torch.int8 or
+                                                                      w2q.dtype != torch.int8)):
+        raise RuntimeError(f"{name}: weights must be both int8 or both their bf16 copies "
+                           f"(got {w1q_glu.dtype}, {w2q.dtype})")
+    # workspace with room for both weight matrices widened to bf16 (int8 weights): the GEMMs then run on bf16 tiles
+    xc, lens, out, ws, nbytes, B, T, D, inner = _module_common(
+        name, x, ln_w, dw_w, lengths,
+        "gsn_conv_module_workspace_bytes" if widened else "gsn_conv_module_i8w_workspace_bytes")
+    _lib.call("gsn_conv_module_i8w_widened" if widened else "gsn_conv_module_i8w", xc.data_ptr(), ln_w.data_ptr(), ln_b.data_ptr(), w1q_glu.data_ptr(),
               s1_glu.data_ptr(), b1_glu.data_ptr(), dw_w.data_ptr(), dw_b.data_ptr(), w2q.data_ptr(), s2.data_ptr(),
               b2.data_ptr(), _ptr(lens), 1 if add_residual else 0, out.data_ptr(), B, T, D, inner, float(ln_eps),
               ws.data_ptr(), nbytes, _stream(xc))
@@ -459,8 +467,9 @@ def run_conv_module(x: torch.Tensor, p, lengths: Optional[torch.Tensor] = None, 
     if int8:
         if not p.has_int8:
             raise RuntimeError("run_conv_module(int8=True): weights were prepared without int8")
-        return torch.ops.granite.conv_module_i8w(x, p.ln_w, p.ln_b, p.w1q_glu, p.s1_glu, p.b1_glu, p.dw_w, p.dw_b,
-                                                 p.w2q, p.s2, p.b2, lengths, p.ln_eps, add_residual)
+        w1, w2 = (p.w1w_glu, p.w2w) if p.w1w_glu is not None else (p.w1q_glu, p.w2q)
+        return torch.ops.granite.conv_module_i8w(x, p.ln_w, p.ln_b, w1, p.s1_glu, p.b1_glu, p.dw_w, p.dw_b,
+                                                 w2, p.s2, p.b2, lengths, p.ln_eps, add_residual)
     return torch.ops.granite.conv_module(x, p.ln_w, p.ln_b, p.w1_glu, p.b1_glu, p.dw_w, p.dw_b, p.w2, p.b2, lengths,
                                          p.ln_eps, add_residual)
 

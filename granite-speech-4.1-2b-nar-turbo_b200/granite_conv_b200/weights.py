@@ -98,6 +98,10 @@ class PreparedConvModule:
     s1_glu: Optional[torch.Tensor] = None    # [2I] fp32
     w2q: Optional[torch.Tensor] = None       # [D, I] int8
     s2: Optional[torch.Tensor] = None        # [D] fp32
+    # the int8 weights widened once to bf16 (exact: |q| <= 127), so the int8-weight module runs its GEMMs on bf16
+    # tiles with the column scales without widening the constant weights on every call
+    w1w_glu: Optional[torch.Tensor] = None   # [2I, D] bf16 = bf16(w1q_glu)
+    w2w: Optional[torch.Tensor] = None       # [D, I] bf16 = bf16(w2q)
     # LayerNorm folded into the up_conv GEMM (gsn_fold_layernorm_bf16): W1 * gamma, b1 + W1 beta, column sums
     w1g_glu: Optional[torch.Tensor] = None   # [2I, D] bf16, GLU-interleaved
     b1g_glu: Optional[torch.Tensor] = None   # [2I] fp32
@@ -162,6 +166,8 @@ def prepare_from_tensors(ln_w, ln_b, up_w, up_b, dw_w, dw_b, down_w, down_b, ln_
         p.s1_glu = glu_interleave(s1.to(dev))
         p.w2q = q2.to(dev).contiguous()
         p.s2 = s2.to(dev).contiguous()
+        p.w1w_glu = p.w1q_glu.to(bf).contiguous()
+        p.w2w = p.w2q.to(bf).contiguous()
     if ln_fold:
         fold_layernorm_(p)
     return p

@@ -187,6 +187,16 @@ int gsn_conv_module_i8w(const void* x, const void* ln_w, const void* ln_b, const
                         int add_residual, void* out, int B, int T, int D, int inner, float ln_eps, void* workspace,
                         size_t workspace_bytes, gsn_stream_t stream);
 
+/* The int8-weight module with the weights already widened to bf16 by the caller, once (w1w_glu, w2w: bf16 copies of
+ * w1q_glu, w2q, exact since |q| <= 127); the GEMMs run on bf16 tiles with the per-output-channel scales, and the
+ * constant weights are not widened again on every call.  Workspace: gsn_conv_module_workspace_bytes(B, T, D,
+ * inner).  Bit-identical to gsn_conv_module_i8w.  No reference counterpart (see gsn_conv_module_i8w). */
+int gsn_conv_module_i8w_widened(const void* x, const void* ln_w, const void* ln_b, const void* w1w_glu,
+                                const float* s1_glu, const float* b1_glu, const void* dw_w, const void* dw_b,
+                                const void* w2w, const float* s2, const float* b2, const int32_t* lengths,
+                                int add_residual, void* out, int B, int T, int D, int inner, float ln_eps,
+                                void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
 /* W8A8 module: int8 weights (as for gsn_conv_module_i8w: w1q_glu [2*inner, D] GLU-interleaved, w2q [D, inner],
  * fp32 per-output-channel scales s1_glu, s2) and int8 activations: the LayerNorm output and the depthwise output
  * are quantised per row (gsn_quant_rows_bf16) and both pointwise GEMMs run kind::i8 tensor-core MMAs with s32

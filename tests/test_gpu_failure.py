@@ -61,8 +61,9 @@ def _after_abort_module_still_correct():
 
 @pytest.mark.parametrize("layout", ["channels_last", "channels_first"])
 def test_depthwise_unwinds_after_withheld_copy(layout):
-    """The depthwise kernel with every CTA's first tile armed but never loaded: the bounded wait runs out, the
-    kernel records 0x104 and returns, and the context then runs the whole module correctly."""
+    """The depthwise kernels with every CTA's first tile armed but never loaded: the bounded wait runs out, the
+    kernel records a timeout and returns (the tensor-core kernel also frees its TMEM), and the context then runs the
+    whole module correctly."""
     s = torch.cuda.current_stream().cuda_stream
     B, C, T = 4, 256, 512
     g = torch.Generator(device="cuda").manual_seed(3)
@@ -78,7 +79,9 @@ def test_depthwise_unwinds_after_withheld_copy(layout):
     _lib.device_status(s, clear=True)
     _lib.call("gsn_selftest_dwconv_withheld_bf16", xin.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), B, C, T,
               *xin.stride(), *y.stride(), s)
-    assert _lib.device_status(s, clear=True) == 0x104
+    # the channels-last kernel's wait (0x104); the channels-first one runs on the tensor cores, where the producer,
+    # the MMA issuer or the epilogue may give up first (0x101 - 0x103)
+    assert _lib.device_status(s, clear=True) in ((0x104,) if layout == "channels_last" else (0x101, 0x102, 0x103))
     ref = torch.ops.granite.dwconv_silu(xin, w[:, None, :], b)      # the same launch without the withheld copy
     want = F.silu(F.conv1d(xin.float(), w[:, None, :].float(), b.float(), padding=7, groups=C))
     assert_bf16_close(ref.float(), want, f"dw {layout} after the unwind")

@@ -115,8 +115,18 @@ def test_module_int8_widened_weights_equal_staged(masked):
                   p.s2.data_ptr(), p.b2.data_ptr(), None if lens is None else lens.data_ptr(), 1, out.data_ptr(),
                   B, T, D, inner, float(p.ln_eps), ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
         outs.append(out)
+    # the weights widened once at prepare time (PreparedConvModule.w1w_glu / w2w): no widening per call, the same bits
+    ws = torch.empty(small, dtype=torch.uint8, device=DEV)
+    out = torch.empty_like(x)
+    _lib.call("gsn_conv_module_i8w_widened", x.data_ptr(), p.ln_w.data_ptr(), p.ln_b.data_ptr(), p.w1w_glu.data_ptr(),
+              p.s1_glu.data_ptr(), p.b1_glu.data_ptr(), p.dw_w.data_ptr(), p.dw_b.data_ptr(), p.w2w.data_ptr(),
+              p.s2.data_ptr(), p.b2.data_ptr(), None if lens is None else lens.data_ptr(), 1, out.data_ptr(),
+              B, T, D, inner, float(p.ln_eps), ws.data_ptr(), small, torch.cuda.current_stream().cuda_stream)
+    outs.append(out)
+    outs.append(ops.run_conv_module(x, p, lengths=lens, int8=True))      # the op takes the widened copies
     torch.cuda.synchronize()
-    assert torch.equal(outs[0], outs[1])
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
 
 
 def test_module_full_size_batch_independence():
