@@ -43,6 +43,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "granite-speech-4.1-2b-nar-turbo_b200"))
 
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    # the communicator's INIT lines (rank count, devices) go to stderr, so the ranks in use can be checked; NCCL reads
+    # these when the library loads, i.e. before torch is imported below
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+
 from granite_conv_b200 import dispatch, synth  # noqa: E402
 
 N_LAYERS = 16
@@ -448,9 +454,6 @@ def run_ours(args):
 
     world, rank, local = _dist_env()
     if world > 1:
-        # the communicator's INIT lines (rank count, devices) go to stderr, so the ranks in use can be checked
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
