@@ -759,7 +759,7 @@ int gsn_quant_rows_bf16(const void* x, int64_t ldx, void* q, float* scale, int M
   if (K % 8 || ldx < K || ldx % 8 || !aligned(x, 16) || !aligned(q, 8))
     return fail(GSN_ERR_UNSUPPORTED, "%s: K=%d ldx=%lld (K %% 8 == 0, 16-byte aligned rows)", name, K, (long long)ldx);
   if (lengths && (T <= 0 || M % T)) return fail(GSN_ERR_INVALID_ARG, "%s: lengths need M %% T == 0 (T=%d)", name, T);
-  return finish(launch_quant_rows((const __nv_bfloat16*)x, ldx, (int8_t*)q, scale, M, K, lengths, T,
+  return finish(launch_quant_rows((const __nv_bfloat16*)x, ldx, (int8_t*)q, scale, M, K, lengths, T, 1,
                                   (cudaStream_t)stream), name);
 }
 
@@ -804,7 +804,7 @@ int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, cons
   const int32_t* skip = (lengths && T % 128 == 0) ? lengths : nullptr;
 
   int rc = launch_layernorm_quant((const __nv_bfloat16*)x, D, (const __nv_bfloat16*)ln_w, (const __nv_bfloat16*)ln_b,
-                                  q, rs, M, D, ln_eps, lengths, T, st);
+                                  q, rs, M, D, ln_eps, lengths, T, 0, st);
   if (rc) return finish(rc, name);
   if (T % 128 == 0 && D % 128 == 0) {
     // frames on the 128 grid: GLU, depthwise and SiLU run inside the kind::i8 up_conv GEMM (the GLU tensor is never
@@ -827,7 +827,8 @@ int gsn_conv_module_w8a8(const void* x, const void* ln_w, const void* ln_b, cons
     rc = launch_dwconv(dw, st);
     if (rc) return finish(rc, name);
   }
-  rc = launch_quant_rows(t, inner, q, rs, M, inner, lengths, T, st);
+  // padding rows: only their zero scale (the GEMMs multiply those rows' sums by it or mask them)
+  rc = launch_quant_rows(t, inner, q, rs, M, inner, lengths, T, 0, st);
   if (rc) return finish(rc, name);
   GemmArgs g2{(const __nv_bfloat16*)q, w2q, b2, s2, add_residual ? (const __nv_bfloat16*)x : nullptr,
               (__nv_bfloat16*)out, D, D, M, D, inner, 1, skip, T};

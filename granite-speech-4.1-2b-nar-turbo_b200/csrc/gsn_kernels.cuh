@@ -51,15 +51,15 @@ enum GemmEpilogue { kEpiGlu = 0, kEpiResidual = 1, kEpiSilu = 2, kEpiLinear = 3,
 
 int launch_gemm(const GemmArgs& args, int epilogue, cudaStream_t stream);
 // Per-row symmetric int8 quantisation: scale[m] = max_k |x[m, k]| / 127, q[m, k] = rint(x[m, k] / scale[m]) (q = 0
-// and scale = 0 for an all-zero row; with lengths, rows of padding frames likewise).  x bf16 [M, K] (row stride
-// ldx), q int8 [M, K] dense.  K % 8 == 0, 16-byte aligned rows.
+// and scale = 0 for an all-zero row; with lengths, rows of padding frames get scale = 0, and q = 0 only with
+// zero_padding).  x bf16 [M, K] (row stride ldx), q int8 [M, K] dense.  K % 8 == 0, 16-byte aligned rows.
 int launch_quant_rows(const __nv_bfloat16* x, int64_t ldx, int8_t* q, float* scale, int M, int K,
-                      const int* lengths, int T, cudaStream_t stream);
+                      const int* lengths, int T, int zero_padding, cudaStream_t stream);
 // LayerNorm (launch_layernorm's arithmetic, rounded to bf16) and launch_quant_rows' quantisation in one pass: q int8
 // [M, D] dense, scale[M]; D in {256, 512, 1024, 2048}.
 int launch_layernorm_quant(const __nv_bfloat16* x, int64_t ld_x, const __nv_bfloat16* gamma,
                            const __nv_bfloat16* beta, int8_t* q, float* scale, int M, int D, float eps,
-                           const int* lengths, int T, cudaStream_t stream);
+                           const int* lengths, int T, int zero_padding, cudaStream_t stream);
 // int8 -> bf16 widening of two weight arrays (n0, n1 bytes, multiples of 16; 16-byte aligned pointers).
 int launch_widen_i8(const void* q0, void* o0, int64_t n0, const void* q1, void* o1, int64_t n1, cudaStream_t stream);
 

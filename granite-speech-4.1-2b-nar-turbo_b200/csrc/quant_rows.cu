@@ -4,7 +4,10 @@
 //   scale[m] = max_k |x[m, k]| / 127        (fp32, IEEE division)
 //   q[m, k]  = rint(x[m, k] / scale[m])     (round half to even, IEEE division; 0 where scale[m] == 0)
 // One warp per row: 16-byte loads of 8 bf16, a shuffle max, then the same loads again for the quantisation (the row
-// is 2-4 KB and sits in L1 / L2 between the two passes).  Rows of padding frames (lengths) get q = 0, scale = 0.
+// is 2-4 KB and sits in L1 / L2 between the two passes).  Rows of padding frames (lengths) get scale = 0, and q = 0
+// when `zero_padding` is set; inside the W8A8 module they keep whatever q they held, since every GEMM that reads
+// them either multiplies the row's s32 sum by its zero scale or masks the row (any int8 values give a finite sum:
+// at most 127^2 x K < 2^31), which saves writing a K-byte row of zeros per padding frame.
 #include "gsn_kernels.cuh"
 #include "gsn_ptx.cuh"
 
@@ -14,25 +17,27 @@ namespace quant_impl {
 
 __global__ void __launch_bounds__(256)
     quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int8_t* __restrict__ q,
-                      float* __restrict__ scale, int M, int K, const int* lengths, int T) {
+                      float* __restrict__ scale, int M, int K, const int* lengths, int T, int zero_padding) {
   const int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  bool valid = true;
+  int8_t* qr = q + (int64_t)row * K;
   if (lengths) {
     const int b = row / T;
-    valid = row - b * T < __ldg(lengths + b);
+    if (row - b * T >= __ldg(lengths + b)) {           // a padding frame
+      if (lane == 0) scale[row] = 0.f;
+      if (zero_padding)
+        for (int d = lane * 8; d < K; d += 256) *reinterpret_cast<uint2*>(qr + d) = make_uint2(0u, 0u);
+      return;
+    }
   }
   const __nv_bfloat16* xr = x + (int64_t)row * ldx;
-  int8_t* qr = q + (int64_t)row * K;
   float amax = 0.f;
-  if (valid) {
-    for (int d = lane * 8; d < K; d += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(xr + d);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  for (int d = lane * 8; d < K; d += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + d);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fmaxf(fabsf(bf16lo_to_f32(w[i])), fabsf(bf16hi_to_f32(w[i]))));
-    }
+    for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fmaxf(fabsf(bf16lo_to_f32(w[i])), fabsf(bf16hi_to_f32(w[i]))));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -62,17 +67,19 @@ template <int V>  // V = D / 256 16-byte vectors per lane
 __global__ void __launch_bounds__(256)
     layernorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, const __nv_bfloat16* __restrict__ gamma,
                            const __nv_bfloat16* __restrict__ beta, int8_t* __restrict__ q, float* __restrict__ scale,
-                           int M, float eps, const int* __restrict__ lengths, int T) {
+                           int M, float eps, const int* __restrict__ lengths, int T, int zero_padding) {
   constexpr int D = V * 256;
   const int lane = threadIdx.x & 31;
   const int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   if (row >= M) return;
   int8_t* qr = q + (int64_t)row * D;
-  if (lengths != nullptr) {               // padding frames: q = 0, scale = 0
+  if (lengths != nullptr) {               // padding frames: scale = 0 (and q = 0 with zero_padding)
     const int b = row / T;
     if (row - b * T >= __ldg(lengths + b)) {
+      if (zero_padding) {
 #pragma unroll
-      for (int i = 0; i < V; ++i) *reinterpret_cast<uint2*>(qr + i * 256 + lane * 8) = make_uint2(0u, 0u);
+        for (int i = 0; i < V; ++i) *reinterpret_cast<uint2*>(qr + i * 256 + lane * 8) = make_uint2(0u, 0u);
+      }
       if (lane == 0) scale[row] = 0.f;
       return;
     }
@@ -147,26 +154,27 @@ __global__ void __launch_bounds__(256)
 
 int launch_layernorm_quant(const __nv_bfloat16* x, int64_t ld_x, const __nv_bfloat16* gamma,
                            const __nv_bfloat16* beta, int8_t* q, float* scale, int M, int D, float eps,
-                           const int* lengths, int T, cudaStream_t stream) {
+                           const int* lengths, int T, int zero_padding, cudaStream_t stream) {
   if (M <= 0) return 0;
   if (lengths && T <= 0) return (int)cudaErrorInvalidValue;
   const int grid = (int)(((int64_t)M * 32 + 255) / 256);
+  const int zp = zero_padding;
   switch (D) {
-    case 256: quant_impl::layernorm_quant_kernel<1><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T); break;
-    case 512: quant_impl::layernorm_quant_kernel<2><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T); break;
-    case 1024: quant_impl::layernorm_quant_kernel<4><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T); break;
-    case 2048: quant_impl::layernorm_quant_kernel<8><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T); break;
+    case 256: quant_impl::layernorm_quant_kernel<1><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T, zp); break;
+    case 512: quant_impl::layernorm_quant_kernel<2><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T, zp); break;
+    case 1024: quant_impl::layernorm_quant_kernel<4><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T, zp); break;
+    case 2048: quant_impl::layernorm_quant_kernel<8><<<grid, 256, 0, stream>>>(x, ld_x, gamma, beta, q, scale, M, eps, lengths, T, zp); break;
     default: return (int)cudaErrorInvalidValue;
   }
   return (int)cudaGetLastError();
 }
 
 int launch_quant_rows(const __nv_bfloat16* x, int64_t ldx, int8_t* q, float* scale, int M, int K,
-                      const int* lengths, int T, cudaStream_t stream) {
+                      const int* lengths, int T, int zero_padding, cudaStream_t stream) {
   if (M <= 0) return 0;
   if (K <= 0 || K % 8 || ldx % 8 || (lengths && T <= 0)) return (int)cudaErrorInvalidValue;
   const int blocks = (int)(((int64_t)M * 32 + 255) / 256);
-  quant_impl::quant_rows_kernel<<<blocks, 256, 0, stream>>>(x, ldx, q, scale, M, K, lengths, T);
+  quant_impl::quant_rows_kernel<<<blocks, 256, 0, stream>>>(x, ldx, q, scale, M, K, lengths, T, zero_padding);
   return (int)cudaGetLastError();
 }
 
