@@ -851,7 +851,7 @@ def run_ours(args):
         bpf = DW_GLU_BYTES_PER_FRAME if workload == "dw_cf_glu" else DW_BYTES_PER_FRAME
         achieved = frames * bpf / (dur / 1e3) / 1e9
         roof = {"kernel": "dwconv_cl_kernel" if workload == "dw" else
-                          "dwconv_cf_tma_kernel<GLU>" if workload == "dw_cf_glu" else "dwconv_cf_mma_kernel",
+                          "dwconv_cf_mma_kernel<GLU>" if workload == "dw_cf_glu" else "dwconv_cf_mma_kernel",
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": bpf,

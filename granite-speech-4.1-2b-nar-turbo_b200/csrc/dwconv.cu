@@ -18,12 +18,12 @@
 //    lengths a lane owns 2 channels x 32 frames (46 staged rows feed 32 outputs, so fewer bf16 unpacks and shared
 //    loads per output); with lengths, and in the GLU form, 4 channels x 8 frames (short tiles waste less work past
 //    an utterance's end).  Both accumulate every output in the same order, so they agree bit for bit.
-//  * channels-first (element stride of T is 1; the layout the reference op receives from up_conv): a CTA owns 32
-//    channels x 128 frames, stages the rows (plus halo) in shared memory as fp32 with plain coalesced loads
-//    (row strides need not be 16-byte multiples there, e.g. T = 37), and transposes the result through shared
-//    memory for coalesced stores.  Any other stride pattern also takes this path.
+//  * channels-first (element stride of T is 1; the layout the reference op receives from up_conv): with 16-byte
+//    aligned rows, T % 8 == 0 and C % 16 == 0 the taps run on the tensor cores (dwconv_mma_sm100.cu).  Otherwise
+//    (a ragged T such as 37, unaligned rows, any other stride pattern) a CTA owns 32 channels x 128 frames, stages
+//    the rows (plus halo) in shared memory as fp32 with plain coalesced loads, and transposes the result through
+//    shared memory for coalesced stores of exactly the frames below T.
 #include <algorithm>
-#include <atomic>
 #include <type_traits>
 
 #include "gsn_kernels.cuh"
@@ -347,90 +347,7 @@ int launch_cl(const DwArgs& a, cudaStream_t stream) {
 }
 
 // ----------------------------------------------------------------------------------------------------------------
-// channels-first through TMA (the layout granite::dwconv_silu receives from up_conv: T innermost)
-//
-// A tile is 64 channels x TT = 32 * WARPS output frames of one utterance.  Its input, frames [t0 - 8, t0 + TT + 16)
-// of the 64 channel rows (or of the 64 value rows and the 64 gate rows in the GLU form), is one 3-D TMA box per
-// row block: BOX_T = TT + 24 frames, so a staged row is 16 bytes times an odd number and the 16-byte shared reads
-// of 8 consecutive lanes (8 consecutive rows) fall in 8 different bank groups.  Lane l of every warp owns the
-// channel pair (l, l + 32) of the tile: one fp32 pair (x[l][t], x[l + 32][t]) feeds one fma.rn.f32x2 per tap, and
-// the pair is formed from the two rows' bf16 words with one shift or mask per element.  Warp w computes frames
-// [t0 + 32w, t0 + 32w + 32): it reads 6 chunks of 8 frames from each of its two rows (46 staged frames feed 32
-// outputs), keeps the 32 accumulator pairs and the 15 weight pairs in registers, and accumulates every output
-// in the same order as the channels-last kernel (bias first, then taps 0..14), so the two layouts agree bit for
-// bit.  Results leave through a per-warp shared box (64 channels x 32 frames, 64-byte swizzle: conflict-free
-// 16-byte writes) and a TMA store, which clips frames past T.
-//
-// The grid is persistent: one CTA per resident slot (SMs x CTAs per SM, so there is no partial second wave), each
-// walking its items (channel block, utterance, time tile; time fastest) through a STAGES-deep ring of TMA boxes and
-// loading a channel block's weights into registers when its channel block changes.  Without lengths a CTA takes a
-// contiguous range of items: every CTA has the same work, consecutive time tiles of one row block follow each other
-// (the 16-frame halo the next tile shares is still in L2) and the weights change at most a few times.  With lengths
-// the items are dealt round robin (item k, k + G, ...), so the tiles past utterance ends, which are not loaded and
-// are only written as zeros, spread evenly.
-template <int WARPS_, int STAGES_, int MINB_, int FPW_ = 32>
-struct CfShape {
-  static constexpr int WARPS = WARPS_, STAGES = STAGES_, MINB = MINB_, FPW = FPW_;
-};
-using CfShapePlain = CfShape<4, 3, 3>;
-using CfShapeGlu = CfShape<4, 2, 2>;
-
-template <class S, bool GLU>
-struct CfCfg {
-  static constexpr int WARPS = S::WARPS;
-  static constexpr int STAGES = S::STAGES;
-  static constexpr int THREADS = 32 * WARPS;
-  static constexpr int CC = 64;                       // channels per tile
-  static constexpr int FPW = S::FPW;                   // output frames per warp (16 or 32)
-  static constexpr int TT = FPW * WARPS;              // output frames per tile
-  static constexpr int BOX_T = TT + 24;               // staged frames, t0 - 8 .. t0 + TT + 15
-  static constexpr int ROW_BYTES = BOX_T * 2;
-  static constexpr int BOX_BYTES = CC * ROW_BYTES;
-  static constexpr int NBOX = GLU ? 2 : 1;
-  static constexpr int OUT_ROW = FPW * 2;             // bytes per channel row of a warp's output box
-  static constexpr int OUT_BYTES = CC * OUT_ROW;      // one warp's output box
-  static constexpr int CHUNKS = (FPW + 2 * HALO + 8) / 8;   // 16-byte chunks a lane reads per row from frame FPW*w
-  static constexpr CUtensorMapSwizzle OUT_SWIZZLE = FPW == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-  static_assert(FPW == 16 || FPW == 32, "output rows of 32 or 64 bytes");
-  static_assert(FPW * (WARPS - 1) + 8 * CHUNKS <= BOX_T, "every warp's window inside the box");
-  static_assert((BOX_T / 8) % 2 == 1, "staged row pitch must be an odd number of 16-byte units");
-  static_assert(BOX_T <= 256, "TMA box extent");
-  static_assert(8 * CHUNKS >= FPW + 2 * HALO + 1, "chunks cover the window");
-};
-
-template <class S, bool GLU>
-struct __align__(1024) CfSmem {
-  using C = CfCfg<S, GLU>;
-  uint8_t out[C::WARPS][C::OUT_BYTES];                // 1024-byte aligned: swizzle atoms
-  uint8_t x[C::STAGES][C::NBOX][C::BOX_BYTES];
-  uint64_t full[C::STAGES];
-  int abort_flag;
-};
-
-struct CfTmaParams {
-  const __nv_bfloat16* w;
-  const __nv_bfloat16* bias;
-  const int* lengths;
-  int B, C, T;
-  int n_tt;            // time tiles per utterance
-  int per_cb;          // items per channel block: B * n_tt
-  int n_items;         // (C / 64) * per_cb
-  int withhold;        // test only: item #k of every CTA armed but never loaded (-1: none)
-};
-
-// fp32 pairs (lo, hi) from the low / high bf16 halves of two words
-__device__ __forceinline__ pk2 pk_lo2(uint32_t a, uint32_t b) {
-  pk2 d;
-  asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tshl.b32 hi, %2, 16;\n\tmov.b64 %0, {lo, hi};\n\t}"
-      : "=l"(d) : "r"(a), "r"(b));
-  return d;
-}
-__device__ __forceinline__ pk2 pk_hi2(uint32_t a, uint32_t b) {
-  pk2 d;
-  asm("{\n\t.reg .b32 lo, hi;\n\tand.b32 lo, %1, 0xFFFF0000;\n\tand.b32 hi, %2, 0xFFFF0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
-      : "=l"(d) : "r"(a), "r"(b));
-  return d;
-}
+// GLU of bf16 words (used by the tensor-core depthwise kernel's converters, dwconv_mma_sm100.cu)
 __device__ __forceinline__ pk2 pk_mul(pk2 a, pk2 b) {
   pk2 d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -445,242 +362,6 @@ __device__ __forceinline__ uint32_t glu_word(uint32_t a, uint32_t g) {
   const pk2 sg = pk_fma(pk_make(0.5f, 0.5f), pk_make(tanh_approx(gh.x), tanh_approx(gh.y)), pk_make(0.5f, 0.5f));
   const float2 r = pk_split(pk_mul(av, sg));
   return pack_bf16x2(r.x, r.y);
-}
-
-template <class S, bool GLU>
-__global__ void __launch_bounds__(CfCfg<S, GLU>::THREADS, S::MINB)
-    dwconv_cf_tma_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmY,
-                         CfTmaParams p) {
-  using Cfg = CfCfg<S, GLU>;
-  constexpr int STAGES = Cfg::STAGES;
-  constexpr int TT = Cfg::TT;
-  constexpr int FPW = Cfg::FPW;
-  constexpr int NIN = FPW + 2 * HALO;                 // input frames per warp
-  extern __shared__ uint8_t smem_raw[];
-  auto& s = *reinterpret_cast<CfSmem<S, GLU>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int T = p.T;
-  const int G = gridDim.x;
-  const int k = blockIdx.x;
-  int first, step, n_items;
-  if (p.lengths) {                                    // round robin
-    first = k;
-    step = G;
-    n_items = p.n_items > k ? (p.n_items - k + G - 1) / G : 0;
-  } else {                                            // contiguous range
-    first = (int)((int64_t)k * p.n_items / G);
-    step = 1;
-    n_items = (int)((int64_t)(k + 1) * p.n_items / G) - first;
-  }
-  constexpr uint32_t kTxBytes = Cfg::NBOX * Cfg::BOX_BYTES;
-
-  auto item = [&](int i, int& c0, int& b, int& t0) {
-    const int g = first + i * step;
-    const int cb = g / p.per_cb;
-    const int r = g - cb * p.per_cb;
-    c0 = cb * Cfg::CC;
-    b = r / p.n_tt;
-    t0 = (r - b * p.n_tt) * TT;
-  };
-  auto len_of = [&](int b) { return p.lengths ? min(max(__ldg(p.lengths + b), 0), T) : T; };
-
-  if (tid == 0) {
-    for (int i = 0; i < STAGES; ++i) mbar_init(&s.full[i], 1);
-    s.abort_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&tmX);
-    tma_prefetch_desc(&tmY);
-  }
-  __syncthreads();
-
-  // producer (thread 0): item i into stage i % STAGES; items whose frames are all padding complete the stage's
-  // phase without a copy
-  auto issue = [&](int i) {
-    const int st = i % STAGES;
-    int c0, b, t0;
-    item(i, c0, b, t0);
-    if (t0 >= len_of(b)) {
-      mbar_arrive(&s.full[st]);
-      return;
-    }
-    mbar_arrive_expect_tx(&s.full[st], kTxBytes);
-    if (i == p.withhold) return;                     // test only: armed, no copy, so the bounded wait runs out
-    tma_load_3d(s.x[st][0], &tmX, &s.full[st], t0 - 8, c0, b);
-    if (GLU) tma_load_3d(s.x[st][GLU ? 1 : 0], &tmX, &s.full[st], t0 - 8, c0 + p.C, b);
-  };
-  int issued = 0;
-  if (tid == 0) {
-    for (; issued < STAGES && issued < n_items; ++issued) issue(issued);
-  }
-
-  // weights of channels c0 + lane and c0 + lane + 32 as fp32 pairs, halved (exact): the accumulator holds x / 2
-  // and silu(x) = h + h * tanh(h)
-  pk2 wr[KW];
-  pk2 bias = 0ull;
-  int w_c0 = -1;
-  auto load_weights = [&](int c0) {
-    const __nv_bfloat16* wa = p.w + (int64_t)(c0 + lane) * KW;
-    const __nv_bfloat16* wb = wa + 32 * KW;
-#pragma unroll
-    for (int j = 0; j < KW; ++j) wr[j] = pk_make(0.5f * __bfloat162float(wa[j]), 0.5f * __bfloat162float(wb[j]));
-    bias = pk_make(0.5f * __bfloat162float(p.bias[c0 + lane]), 0.5f * __bfloat162float(p.bias[c0 + lane + 32]));
-    w_c0 = c0;
-  };
-
-  // this lane's two rows in the warp's output box: rows of OUT_ROW bytes swizzled as the TMA store reads them
-  // (16-byte chunk q of row r at q ^ ((r * OUT_ROW / 128) mod (OUT_ROW / 16)); rows l and l + 32 share the mask)
-  uint8_t* const ob = s.out[warp];
-  const int oxor = ((lane * Cfg::OUT_ROW) >> 7) & (Cfg::OUT_ROW / 16 - 1);
-  uint8_t* const oa = ob + lane * Cfg::OUT_ROW;
-  uint8_t* const obb = ob + (lane + 32) * Cfg::OUT_ROW;
-
-  bool alive = true;
-  for (int i = 0; i < n_items; ++i) {
-    const int st = i % STAGES;
-    int c0, b, t0;
-    item(i, c0, b, t0);
-    if (c0 != w_c0) load_weights(c0);                 // uniform over the CTA
-    const int len = len_of(b);
-    const int tw = t0 + warp * FPW;                   // first output frame of this warp
-    if (alive)
-      alive = mbar_wait_bounded(&s.full[st], (uint32_t)((i / STAGES) & 1), &s.abort_flag, kStatusTimeoutDw);
-    alive = __all_sync(0xffffffffu, alive);           // warp-uniform: the box hand-off below syncs the warp
-    if (alive && tw < T) {
-      if (lane == 0) bulk_wait_group_read<0>();       // the previous store has read this warp's box
-      __syncwarp();
-      uint32_t wa[FPW / 2], wb[FPW / 2];              // output words: frame pairs of row l / row l + 32
-      if (tw >= len) {
-#pragma unroll
-        for (int q = 0; q < FPW / 2; ++q) wa[q] = wb[q] = 0u;
-      } else {
-        auto body = [&](auto masked_tag) {
-          constexpr bool MASKED = decltype(masked_tag)::value;
-          // SiLU of frames f and f + 1 (halved accumulators: silu(x) = h + h tanh(h)), packed per row
-          auto silu_pair = [&](const pk2 (&acc)[FPW], int f) {
-            const float2 h0 = pk_split(acc[f]);
-            const float2 h1 = pk_split(acc[f + 1]);
-            const float2 s0 = pk_split(pk_fma(acc[f], pk_make(tanh_approx(h0.x), tanh_approx(h0.y)), acc[f]));
-            const float2 s1 = pk_split(pk_fma(acc[f + 1], pk_make(tanh_approx(h1.x), tanh_approx(h1.y)), acc[f + 1]));
-            const bool v0 = !MASKED || tw + f < len, v1 = !MASKED || tw + f + 1 < len;
-            wa[f / 2] = pack_bf16x2(v0 ? s0.x : 0.f, v1 ? s1.x : 0.f);
-            wb[f / 2] = pack_bf16x2(v0 ? s0.y : 0.f, v1 ? s1.y : 0.f);
-          };
-          pk2 acc[FPW];
-          const uint8_t* ra = s.x[st][0] + lane * Cfg::ROW_BYTES + warp * (FPW * 2);
-          const uint8_t* rb = ra + 32 * Cfg::ROW_BYTES;
-          const uint8_t* rga = s.x[st][GLU ? 1 : 0] + lane * Cfg::ROW_BYTES + warp * (FPW * 2);
-          const uint8_t* rgb = rga + 32 * Cfg::ROW_BYTES;
-#pragma unroll
-          for (int k = 0; k < Cfg::CHUNKS; ++k) {
-            uint4 va = *reinterpret_cast<const uint4*>(ra + 16 * k);
-            uint4 vb = *reinterpret_cast<const uint4*>(rb + 16 * k);
-            if (GLU) {
-              const uint4 ga = *reinterpret_cast<const uint4*>(rga + 16 * k);
-              const uint4 gb = *reinterpret_cast<const uint4*>(rgb + 16 * k);
-              va = make_uint4(glu_word(va.x, ga.x), glu_word(va.y, ga.y), glu_word(va.z, ga.z), glu_word(va.w, ga.w));
-              vb = make_uint4(glu_word(vb.x, gb.x), glu_word(vb.y, gb.y), glu_word(vb.z, gb.z), glu_word(vb.w, gb.w));
-            }
-            const uint32_t xa[4] = {va.x, va.y, va.z, va.w};
-            const uint32_t xb[4] = {vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int r = 8 * k + e - 1;             // input frame tw - 7 + r
-              if (r < 0 || r >= NIN) continue;
-              pk2 xv = (e & 1) ? pk_hi2(xa[e >> 1], xb[e >> 1]) : pk_lo2(xa[e >> 1], xb[e >> 1]);
-              if (MASKED && tw - HALO + r >= len) xv = 0ull;   // frames past the utterance read as zero
-#pragma unroll
-              for (int f = 0; f < FPW; ++f) {
-                const int j = r - f;
-                if (j >= 0 && j < KW) acc[f] = pk_fma(wr[j], xv, j == 0 ? bias : acc[f]);
-              }
-            }
-          }
-#pragma unroll
-          for (int f = 0; f < FPW; f += 2) silu_pair(acc, f);
-        };
-        if (len < T && tw + FPW + HALO > len)
-          body(std::true_type{});
-        else
-          body(std::false_type{});
-      }
-#pragma unroll
-      for (int q = 0; q < FPW / 8; ++q) {
-        *reinterpret_cast<uint4*>(oa + ((q ^ oxor) << 4)) = make_uint4(wa[4 * q], wa[4 * q + 1], wa[4 * q + 2], wa[4 * q + 3]);
-        *reinterpret_cast<uint4*>(obb + ((q ^ oxor) << 4)) = make_uint4(wb[4 * q], wb[4 * q + 1], wb[4 * q + 2], wb[4 * q + 3]);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_3d(&tmY, ob, tw, c0, b);
-        bulk_commit_group();
-      }
-    }
-    __syncthreads();  // stage st consumed by every warp
-    if (tid == 0 && alive && !s.abort_flag && issued < n_items) {
-      fence_proxy_async_smem();
-      issue(issued);
-      ++issued;
-    }
-  }
-  if (lane == 0) bulk_wait_group<0>();                // stores complete before the shared memory is released
-  if (tid == 0 && s.abort_flag) {
-    // unwinding after a timeout: let the copies still in flight land
-    for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k)
-      mbar_wait_bounded(&s.full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr, kStatusTimeoutDw, 100000000ull);
-  }
-}
-
-template <class S, bool GLU>
-int launch_cf_tma(const DwArgs& a, cudaStream_t stream) {
-  using Cfg = CfCfg<S, GLU>;
-  CUtensorMap tx, ty;
-  {
-    const uint64_t dims[3] = {(uint64_t)a.T, (uint64_t)a.C * (GLU ? 2 : 1), (uint64_t)a.B};
-    const uint64_t strides[2] = {(uint64_t)a.sxC * 2, (uint64_t)a.sxB * 2};
-    const uint32_t box[3] = {(uint32_t)Cfg::BOX_T, (uint32_t)Cfg::CC, 1};
-    int rc = encode_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  }
-  {
-    const uint64_t dims[3] = {(uint64_t)a.T, (uint64_t)a.C, (uint64_t)a.B};
-    const uint64_t strides[2] = {(uint64_t)a.syC * 2, (uint64_t)a.syB * 2};
-    const uint32_t box[3] = {(uint32_t)Cfg::FPW, (uint32_t)Cfg::CC, 1};
-    int rc = encode_tmap(&ty, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.y, dims, strides, box, Cfg::OUT_SWIZZLE);
-    if (rc) return rc;
-  }
-  CfTmaParams p;
-  p.w = a.w;
-  p.bias = a.bias;
-  p.lengths = a.lengths;
-  p.B = a.B;
-  p.C = a.C;
-  p.T = a.T;
-  p.n_tt = (a.T + Cfg::TT - 1) / Cfg::TT;
-  const int64_t per_cb = (int64_t)a.B * p.n_tt;
-  const int64_t items = per_cb * (a.C / Cfg::CC);
-  if (items > (1 << 30)) return (int)cudaErrorInvalidValue;
-  p.per_cb = (int)per_cb;
-  p.n_items = (int)items;
-  p.withhold = a.withhold_tile;
-  auto kern = dwconv_cf_tma_kernel<S, GLU>;
-  const int smem = (int)sizeof(CfSmem<S, GLU>) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return (int)e;
-  // resident CTAs per SM, asked once per device (the same value whichever thread stores it)
-  static std::atomic<int> resident[8];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) dev = 0;
-  int per_sm = dev < 8 ? resident[dev].load(std::memory_order_relaxed) : 0;
-  if (per_sm <= 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::THREADS, smem) != cudaSuccess || per_sm <= 0)
-      per_sm = 1;
-    if (dev < 8) resident[dev].store(per_sm, std::memory_order_relaxed);
-  }
-  const int grid = (int)std::min<int64_t>(items, (int64_t)device_sm_count() * per_sm);
-  kern<<<grid, Cfg::THREADS, smem, stream>>>(tx, ty, p);
-  return (int)cudaGetLastError();
 }
 
 // ----------------------------------------------------------------------------------------------------------------
@@ -789,20 +470,13 @@ int launch_dwconv(const DwArgs& a, cudaStream_t stream) {
   if (!a.glu && !a.lengths && cl_ok(ShapeDense{})) return launch_cl<ShapeDense, false>(a, stream);
   if (cl_ok(ShapeMasked{}))
     return a.glu ? launch_cl<ShapeMasked, true>(a, stream) : launch_cl<ShapeMasked, false>(a, stream);
-  // the channels-first TMA kernel applies when T is innermost in both tensors with 16-byte aligned, non-overlapping
-  // channel rows and C a multiple of 64
-  const int64_t cx = (int64_t)a.C * (a.glu ? 2 : 1);
-  const bool cf_ok = a.sxT == 1 && a.syT == 1 && (a.C % 64) == 0 && (a.sxC % 8) == 0 && (a.sxB % 8) == 0 &&
-                     (a.syC % 8) == 0 && (a.syB % 8) == 0 && a.sxC >= a.T && a.syC >= a.T && a.sxB >= cx * a.sxC &&
-                     a.syB >= (int64_t)a.C * a.syC && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
-  // the plain form on the tensor cores (dwconv_mma_sm100.cu), the GLU form on the CUDA cores
-  const bool mma_ok = a.sxT == 1 && a.syT == 1 && !a.glu && (a.C % 16) == 0 && (a.sxC % 8) == 0 &&
+  // both forms on the tensor cores (dwconv_mma_sm100.cu) when rows are 16-byte aligned, C % 16 == 0 and T % 8 == 0
+  // (the kernel moves whole 8-frame chunks: a ragged row end would be read and written past T)
+  const bool mma_ok = a.sxT == 1 && a.syT == 1 && (a.C % 16) == 0 && (a.T % 8) == 0 && (a.sxC % 8) == 0 &&
                       (a.sxB % 8) == 0 && (a.syC % 8) == 0 && (a.syB % 8) == 0 && a.sxC >= a.T && a.syC >= a.T &&
                       (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
   if (mma_ok) return launch_dwconv_cf_mma(a, stream);
-  if (cf_ok)
-    return a.glu ? launch_cf_tma<CfShapeGlu, true>(a, stream) : launch_cf_tma<CfShapePlain, false>(a, stream);
+  // anything else (a ragged T, unaligned rows, C % 16 != 0) takes the generic kernel, which stores frame by frame
   CfParams p{a.x, a.w, a.bias, a.y, a.lengths, a.sxB, a.sxC, a.sxT, a.syB, a.syC, a.syT, a.C, a.T};
   dim3 grid((a.T + CF_TT - 1) / CF_TT, (a.C + CF_CC - 1) / CF_CC, a.B);
   if (a.glu)

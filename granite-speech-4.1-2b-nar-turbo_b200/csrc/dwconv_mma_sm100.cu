@@ -12,19 +12,27 @@
 // rows overlap by 8 frames, and only D[m, 0..7] is read.  The weights are halved in the table (exact), so D holds
 // y / 2 and silu(y) = h + h tanh(h) with h = D + b / 2.
 //
-// Work item: 8 channels x 1024 frames of one utterance.  Two CTAs per SM (256 tensor-memory columns and ~83 KB of
-// shared memory each), so two independent load -> MMA -> epilogue pipelines overlap on every SM.  Roles (352
-// threads):
-//   warp 0      producer: per item, writes the parts of the 16 staged rows outside the copied range (zeros before
+// GLU form (granite::dwconv_silu_glu, x (B, 2C, T)): the item's value rows and gate rows are staged side by side
+// and converter warps replace each value frame by bf16(a * sigmoid(g)) in place (the arithmetic of the CUDA-core
+// kernels' GLU, one rounding to bf16 as script/cuda_kernels/conv1d.py:70-73), so the value rows become the A
+// operand.  Without lengths the items stay 8 channels wide in 3 stages with one table slot (two CTAs still fit on
+// an SM); with lengths they are 4 channels wide.
+//
+// Work item: 8 channels (GLU form with lengths: 4) x 1024 frames of one utterance.  Two CTAs per SM (at most 256
+// tensor-memory columns and ~110 KB of shared memory each), so two independent load -> MMA -> epilogue pipelines
+// overlap on every SM.  Roles (352 threads; the GLU form adds 4 converter warps):
+//   warp 0      producer: per item, writes the parts of the staged rows outside the copied range (zeros before
 //               frame 0 and from len on, the ragged last chunk of an utterance), then one bulk copy per row for the
 //               rest (16-byte aligned: T % 8 == 0); builds a channel block's 16 Toeplitz tables (from weights
-//               staged in shared memory) into one of two table slots when the block changes; 4 stages
+//               staged in shared memory) into one of two table slots when the block changes (the GLU form
+//               without lengths: one slot); 4 stages (GLU form without lengths: 3)
 //   warps 1-2   MMA issuers (warp 1 also allocates TMEM): each issues the 8 MMAs of its 4 channels per item into
 //               one of two 128-column accumulators (16 columns per channel).  An M=128, N=16 MMA runs in a few
 //               cycles but takes about a hundred to issue, so the issue is split
 //   warps 3-10  epilogue: warp e reads TMEM lane quarter e % 4 (rows 32 (e % 4) .. + 31) and 4 of the channels:
 //               per row 8 consecutive frames of a channel, bias + SiLU, one 16-byte store (a warp writes 512
 //               contiguous bytes of a channel row)
+//   warps 11-14 (GLU form) converters: per item, the GLU of every staged value / gate chunk pair into the value row
 // Frames t >= len read as zero and are written as zero; frames >= T are neither read nor written.
 //
 // Accumulation happens inside the tensor core in fp32, in its own order, so results can differ from the CUDA-core
@@ -39,40 +47,57 @@ namespace gsn {
 namespace dwm_impl {
 
 constexpr int KW = 15;
-constexpr int CT = 8;                        // channels per item
 constexpr int FR = 1024;                     // output frames per item (128 rows x 8)
 constexpr int ROWF = FR + 24;                // staged frames per channel: t0 - 8 .. t0 + 1039
 constexpr int ROW_BYTES = ROWF * 2;          // 2096 = 131 x 16
-constexpr int STAGE_BYTES = CT * ROW_BYTES;
 constexpr int TAB_BYTES = 16 * 32 * 2;       // one channel's Toeplitz table: 16 n x 32 k bf16
-constexpr int STAGES = 4;
 constexpr int NISS = 2;                      // MMA-issuing warps: an N=16 MMA is issued far slower than it runs, so
-constexpr int CPI = CT / NISS;               //   each issuer takes CPI channels of the item
+                                             //   each issuer takes CT / NISS channels of the item
 constexpr int EPI_WARPS = 8;                 // each covers a TMEM lane quarter and CT * 4 / EPI_WARPS channels
-constexpr int EPI_CH = CT * 4 / EPI_WARPS;   // channels per epilogue warp, in batches of EB
-constexpr int EB = EPI_CH < 8 ? EPI_CH : 8;
 constexpr int EPI_W0 = 1 + NISS;             // first epilogue warp
-constexpr int THREADS = 32 * (1 + NISS + EPI_WARPS);
-constexpr uint32_t TMEM_COLS = 2 * CT * 16;  // 2 accumulators x CT channels x 16 columns
-constexpr int MINB = 512 / TMEM_COLS;        // CTAs per SM the tensor memory allows
-static_assert(CPI * NISS == CT && EPI_CH * EPI_WARPS == CT * 4, "channel split");
+constexpr int CONV_W0 = EPI_W0 + EPI_WARPS;  // first converter warp (GLU form)
+constexpr int MINB = 2;                      // CTAs per SM (registers, tensor memory and shared memory allow two)
 constexpr uint32_t IDESC = make_idesc_bf16_f32(128, 16);
 static_assert(ROW_BYTES % 16 == 0, "rows must stay 16-byte aligned");
 
-struct __align__(1024) Smem {
-  uint8_t x[STAGES][STAGE_BYTES];
-  uint8_t tab[2][CT * TAB_BYTES];            // Toeplitz tables of two channel blocks
-  __nv_bfloat16 wst[CT * KW];                // a block's weights, staged for the table build
-  int st_slot[STAGES];                       // table slot of the item in each stage
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
-  uint64_t mma_done;
-  uint32_t tmem_base;
-  int abort_flag;
+// Shapes: the plain form; the GLU form without lengths (contiguous item ranges, so the channel block rarely
+// changes: one table slot leaves room for 8-channel items of value + gate rows at two CTAs per SM); the GLU form
+// with lengths (round-robin items, a new channel block nearly every item: two table slots, 4-channel items).
+enum Form : int { kPlain = 0, kGluDense = 1, kGluMasked = 2 };
+
+template <int FORM>
+struct Cfg {
+  static constexpr bool GLU = FORM != kPlain;
+  static constexpr int CT = FORM == kGluMasked ? 4 : 8;   // channels per item
+  static constexpr int ROWS = GLU ? 2 * CT : CT;         // staged rows per item: value rows, then gate rows
+  static constexpr int STAGE_BYTES = ROWS * ROW_BYTES;
+  static constexpr int STAGES = FORM == kGluDense ? 3 : 4;
+  static constexpr int TSLOTS = FORM == kGluDense ? 1 : 2;   // Toeplitz table slots (channel blocks kept)
+  static constexpr int CPI = CT / NISS;
+  static constexpr int EPI_CH = CT * 4 / EPI_WARPS;  // channels per epilogue warp, in batches of EB
+  static constexpr int EB = EPI_CH < 8 ? EPI_CH : 8;
+  static constexpr int CONV_WARPS = GLU ? 4 : 0;
+  static constexpr int THREADS = 32 * (CONV_W0 + CONV_WARPS);
+  static constexpr uint32_t TMEM_COLS = 2 * CT * 16;   // 2 accumulators x CT channels x 16 columns
+  static_assert(CPI * NISS == CT && EPI_CH * EPI_WARPS == CT * 4, "channel split");
+  static_assert(MINB * TMEM_COLS <= 512, "tensor memory");
+
+  struct __align__(1024) Smem {
+    uint8_t x[STAGES][STAGE_BYTES];
+    uint8_t tab[TSLOTS][CT * TAB_BYTES];     // Toeplitz tables of the last channel blocks
+    __nv_bfloat16 wst[CT * KW];              // a block's weights, staged for the table build
+    int st_slot[STAGES];                     // table slot of the item in each stage
+    uint64_t full[STAGES];                   // the stage's copies landed
+    uint64_t cfull[STAGES];                  // GLU form: the stage's value rows converted
+    uint64_t empty[STAGES];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int abort_flag;
+  };
+  static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory");
 };
-static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory");
 
 struct Params {
   const __nv_bfloat16* x;
@@ -81,6 +106,7 @@ struct Params {
   __nv_bfloat16* y;
   const int* lengths;
   int64_t sxB, sxC, syB, syC;                // element strides (T stride 1)
+  int64_t gate_off;                          // GLU form: elements from a value row to its gate row (C * sxC)
   int B, C, T;
   int n_tt, per_cb, n_items;
   int withhold;                              // test only: item #k of every CTA armed but never copied (-1: none)
@@ -102,7 +128,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-__global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) {
+template <int FORM>
+__global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel(Params p) {
+  using K = Cfg<FORM>;
+  constexpr bool GLU = K::GLU;
+  using Smem = typename K::Smem;
+  constexpr int CT = K::CT, ROWS = K::ROWS, STAGES = K::STAGES, CPI = K::CPI, EPI_CH = K::EPI_CH, EB = K::EB;
+  constexpr uint32_t TMEM_COLS = K::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = warp_id();
@@ -131,6 +163,7 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.full[i], 1);
+      mbar_init(&s.cfull[i], K::CONV_WARPS > 0 ? K::CONV_WARPS : 1);
       mbar_init(&s.empty[i], NISS);
     }
     for (int i = 0; i < 2; ++i) {
@@ -175,12 +208,12 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
         if (lane == 0) mbar_arrive(&s.full[st]);
         continue;
       }
-      // the channel block's Toeplitz tables: kept in one of two slots; a new block takes the slot used longer ago,
+      // the channel block's Toeplitz tables: kept in TSLOTS slots; a new block takes the slot used longer ago,
       // after the MMAs of that slot's last item are done.  Channel c's table holds B[n, k] = w[k - n - 1] / 2 as
       // core matrices (n-group g, k-chunk h) at (2 h + g) * 128 bytes, row n % 8 at 16 (n % 8), element k % 8
-      int slot = c0 == slot_c0[0] ? 0 : (c0 == slot_c0[1] ? 1 : -1);
+      int slot = c0 == slot_c0[0] ? 0 : (K::TSLOTS > 1 && c0 == slot_c0[1] ? 1 : -1);
       if (slot < 0) {
-        slot = slot_last[0] <= slot_last[1] ? 0 : 1;
+        slot = K::TSLOTS == 1 || slot_last[0] <= slot_last[1] ? 0 : 1;
         const int last = slot_last[slot];
         if (last >= 0 && i - last < STAGES) {                // its stage not reused yet: wait for that item's MMAs
           bool got = mbar_wait_bounded(&s.empty[last % STAGES], (uint32_t)((last / STAGES) & 1), abort_flag,
@@ -215,8 +248,9 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
       }
       slot_last[slot] = i;
       if (lane == 0) s.st_slot[st] = slot;                   // read by the issuers after the stage's full barrier
-      // staged frames [t0 - 8, t0 + 1040) of 16 rows: frames [lo, hi8) by bulk copy, the ragged end [hi8, hi) of
-      // an utterance (len % 8 != 0) by a masked 16-byte copy, zeros elsewhere (before frame 0, from len on)
+      // staged frames [t0 - 8, t0 + 1040) of the ROWS rows (GLU form: CT value rows, then their CT gate rows):
+      // frames [lo, hi8) by bulk copy, the ragged end [hi8, hi) of an utterance (len % 8 != 0) by a masked 16-byte
+      // copy, zeros elsewhere (before frame 0, from len on; a zero value and gate give a zero GLU)
       const int f_begin = t0 - 8;
       const int lo = max(f_begin, 0);                        // multiple of 8
       const int hi = min(t0 + FR + 16, len);                 // > lo: t0 < len
@@ -227,13 +261,17 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
       const int head = lo > f_begin ? 1 : 0;
       const int tail0 = (hi8 - f_begin) / 8;                 // first tail chunk of a row
       const int per_row = head + (ROWF / 8 - tail0);
-      for (int q = lane; q < CT * per_row; q += 32) {
+      // element offset of staged row r in x: value channel c0 + r, or the gate row of value channel c0 + r - CT
+      auto row_off = [&](int r) {
+        return (int64_t)b * p.sxB + (int64_t)(c0 + (r < CT ? r : r - CT)) * p.sxC + (r < CT ? 0 : p.gate_off);
+      };
+      for (int q = lane; q < ROWS * per_row; q += 32) {
         const int c = q / per_row, j = q - c * per_row;
         const int ch = (j < head) ? 0 : tail0 + (j - head);  // chunk index within the row
         const int t = f_begin + ch * 8;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (t == hi8 && hi8 < hi) {                          // the ragged end: frames hi8 .. hi - 1 of 8 (in bounds:
-          v = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)b * p.sxB + (int64_t)(c0 + c) * p.sxC + t));
+          v = __ldg(reinterpret_cast<const uint4*>(p.x + row_off(c) + t));
           const int keep = hi - hi8;                         //  hi8 + 8 <= round_up(len, 8) <= T)
           uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -249,10 +287,10 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
       __syncwarp();
       const uint32_t row_bytes = hi8 > lo ? (uint32_t)(hi8 - lo) * 2 : 0u;
       ++issued;
-      if (lane == 0) mbar_arrive_expect_tx(&s.full[st], row_bytes * CT);
+      if (lane == 0) mbar_arrive_expect_tx(&s.full[st], row_bytes * ROWS);
       __syncwarp();
-      if (row_bytes > 0 && lane < CT && i != p.withhold) {   // test only: a withheld item's copies never start
-        const __nv_bfloat16* src = p.x + (int64_t)b * p.sxB + (int64_t)(c0 + lane) * p.sxC + lo;
+      if (row_bytes > 0 && lane < ROWS && i != p.withhold) {   // test only: a withheld item's copies never start
+        const __nv_bfloat16* src = p.x + row_off(lane) + lo;
         bulk_load(xs + lane * ROW_BYTES + (lo - f_begin) * 2, src, row_bytes, &s.full[st]);
       }
     }
@@ -273,7 +311,9 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
       bool got = true;
       if (i >= 2)
         got = mbar_wait_bounded(&s.tempty[acc], (uint32_t)(((i >> 1) - 1) & 1), abort_flag, kStatusTimeoutMma);
-      if (got) got = mbar_wait_bounded(&s.full[st], (uint32_t)((i / STAGES) & 1), abort_flag, kStatusTimeoutMma);
+      if (got)
+        got = mbar_wait_bounded(GLU ? &s.cfull[st] : &s.full[st], (uint32_t)((i / STAGES) & 1), abort_flag,
+                                kStatusTimeoutMma);
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
@@ -302,7 +342,7 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
     if (lane == 0) umma_commit(&s.mma_done);
     __syncwarp();
     mbar_wait_bounded(&s.mma_done, 0, nullptr, kStatusTimeoutMma, 100000000ull);
-  } else {
+  } else if (warp < CONV_W0) {
     // ------------------------------------------------------------------ epilogue
     const int e = warp - EPI_W0;
     const int q = warp & 3;                  // TMEM lane quarter this warp may read
@@ -354,6 +394,32 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.tempty[acc]);
     }
+  } else if constexpr (GLU) {
+    // ------------------------------------------------------------------ converters (GLU form)
+    // every 16-byte chunk of the staged value rows becomes the GLU of itself and the gate chunk CT rows below;
+    // chunks the producer zeroed stay zero (0 * sigmoid(0))
+    const int ct = threadIdx.x - 32 * CONV_W0;
+    constexpr int CHUNKS = ROWF / 8;
+    for (int i = 0; i < n_items; ++i) {
+      const int st = i % STAGES;
+      bool got = mbar_wait_bounded(&s.full[st], (uint32_t)((i / STAGES) & 1), abort_flag, kStatusTimeoutEpilogue);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      int c0, b, t0;
+      item(i, c0, b, t0);
+      if (t0 < len_of(b)) {
+        uint8_t* xs = s.x[st];
+        for (int q = ct; q < CT * CHUNKS; q += 32 * K::CONV_WARPS) {
+          uint4* vp = reinterpret_cast<uint4*>(xs + q * 16);    // row q / CHUNKS, chunk q % CHUNKS: rows are
+          const uint4 g = *reinterpret_cast<const uint4*>(xs + CT * ROW_BYTES + q * 16);   // CHUNKS chunks long
+          const uint4 a = *vp;
+          *vp = make_uint4(glu_word(a.x, g.x), glu_word(a.y, g.y), glu_word(a.z, g.z), glu_word(a.w, g.w));
+        }
+        fence_proxy_async_smem();           // the converted rows, written by this proxy, are read by the MMAs
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.cfull[st]);
+    }
   }
 
   tc_fence_before();
@@ -366,10 +432,12 @@ __global__ void __launch_bounds__(THREADS, MINB) dwconv_cf_mma_kernel(Params p) 
 
 }  // namespace dwm_impl
 
-// channels-first depthwise on the tensor cores; x (B, C, T) with T innermost, C % 16 == 0, T % 8 == 0, 16-byte
-// aligned rows; no GLU form
-int launch_dwconv_cf_mma(const DwArgs& a, cudaStream_t stream) {
+// channels-first depthwise on the tensor cores; x (B, C, T) (GLU form: (B, 2C, T), value rows then gate rows) with T
+// innermost, C % 16 == 0, T % 8 == 0, 16-byte aligned rows
+template <int FORM>
+int launch_cf_mma(const DwArgs& a, cudaStream_t stream) {
   namespace W = dwm_impl;
+  using K = W::Cfg<FORM>;
   W::Params p;
   p.x = a.x;
   p.w = a.w;
@@ -380,22 +448,23 @@ int launch_dwconv_cf_mma(const DwArgs& a, cudaStream_t stream) {
   p.sxC = a.sxC;
   p.syB = a.syB;
   p.syC = a.syC;
+  p.gate_off = (int64_t)a.C * a.sxC;
   p.B = a.B;
   p.C = a.C;
   p.T = a.T;
   p.n_tt = (a.T + W::FR - 1) / W::FR;
   const int64_t per_cb = (int64_t)a.B * p.n_tt;
-  const int64_t items = per_cb * (a.C / W::CT);
+  const int64_t items = per_cb * (a.C / K::CT);
   if (items > (1 << 30)) return (int)cudaErrorInvalidValue;
   p.per_cb = (int)per_cb;
   p.n_items = (int)items;
   p.withhold = a.withhold_tile;
-  const int smem = (int)sizeof(W::Smem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(W::dwconv_cf_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int smem = (int)sizeof(typename K::Smem) + 1024;
+  auto kern = W::dwconv_cf_mma_kernel<FORM>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   // the whole unified L1 / shared array as shared memory, so two CTAs fit on every SM
-  e = cudaFuncSetAttribute(W::dwconv_cf_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           (int)cudaSharedmemCarveoutMaxShared);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return (int)e;
   // one CTA per resident slot: __launch_bounds__ gives MINB CTAs their registers, the tensor memory holds MINB
   // accumulator pairs, and MINB copies of the shared memory fit in the SM's 228 KB (1 KB reserved per CTA)
@@ -404,8 +473,14 @@ int launch_dwconv_cf_mma(const DwArgs& a, cudaStream_t stream) {
   const int64_t slots = (int64_t)device_sm_count() * per_sm;
   const int grid = (int)(items < slots ? items : slots);
   if (grid <= 0) return 0;
-  W::dwconv_cf_mma_kernel<<<grid, W::THREADS, smem, stream>>>(p);
+  kern<<<grid, K::THREADS, smem, stream>>>(p);
   return (int)cudaGetLastError();
+}
+
+int launch_dwconv_cf_mma(const DwArgs& a, cudaStream_t stream) {
+  namespace W = dwm_impl;
+  if (!a.glu) return launch_cf_mma<W::kPlain>(a, stream);
+  return a.lengths ? launch_cf_mma<W::kGluMasked>(a, stream) : launch_cf_mma<W::kGluDense>(a, stream);
 }
 
 }  // namespace gsn

@@ -97,8 +97,8 @@ struct DwArgs {
 };
 
 int launch_dwconv(const DwArgs& args, cudaStream_t stream);
-// the channels-first form on the tensor cores (dwconv_mma_sm100.cu): T innermost in x and y, no GLU, C % 16 == 0,
-// 16-byte aligned rows (element strides of C and B multiples of 8)
+// the channels-first form on the tensor cores (dwconv_mma_sm100.cu), plain or GLU: T innermost in x and y,
+// C % 16 == 0, T % 8 == 0, 16-byte aligned rows (element strides of C and B multiples of 8)
 int launch_dwconv_cf_mma(const DwArgs& args, cudaStream_t stream);
 
 // ---- LayerNorm over the last dim (layernorm.cu) -------------------------------------------------------------
