@@ -44,10 +44,10 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "granite-speech-4.1-2b-nar-turbo_b200"))
 
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-    # the communicator's INIT lines (rank count, devices) go to stderr, so the ranks in use can be checked; NCCL reads
-    # these when the library loads, i.e. before torch is imported below
+    # NCCL's own log on stderr (version, and with this NCCL the communicator lines where it prints them); NCCL reads
+    # these when the library loads, i.e. before torch is imported below.  The bench also prints the process group
+    # (backend, world size, each rank's GPU) from the ranks themselves
     os.environ.setdefault("NCCL_DEBUG", "INFO")
-    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 
 from granite_conv_b200 import dispatch, synth  # noqa: E402
 
@@ -454,10 +454,20 @@ def run_ours(args):
     from granite_conv_b200.weights import prepare_from_params
 
     world, rank, local = _dist_env()
+    pg_info = None
     if world > 1:
         torch.cuda.set_device(local)
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # which GPU every rank drives, from the ranks themselves (one all_gather before any timing)
+        props = torch.cuda.get_device_properties(local)
+        mine = {"rank": rank, "local_rank": local, "device": f"cuda:{local}",
+                "pci_bus_id": f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}"}
+        ranks = [None] * world
+        dist.all_gather_object(ranks, mine)
+        pg_info = {"backend": dist.get_backend(), "world_size": dist.get_world_size(), "ranks": ranks}
+        if rank == 0:
+            print(f"process group: {json.dumps(pg_info)}", file=sys.stderr, flush=True)
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
     L = _lib.lib()
@@ -934,6 +944,7 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "int8 x int8 (s32 accumulate), bf16 in/out" if w8a8 else ("bf16" if not int8 else "bf16 x int8-weight"), "data": "synthetic",
             "config": dict(_config(args, world), padded_frames_per_s=padded_all * args.steps / (ms / 1e3)),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+            **({"process_group": pg_info} if pg_info else {}),
             "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
