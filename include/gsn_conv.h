@@ -43,7 +43,9 @@ const char* gsn_last_error_string(void);
  * (script/cuda_kernels/conv1d.py:102-114) and its kernel dwconv1d_silu_bf16 (conv1d.py:21-42):
  *   y[b,c,t] = silu(bias[c] + sum_{j<K} weight[c,j] * x[b,c,t-K/2+j]), zero padding outside [0,T).
  * x, y: logical (B, C, T) bf16 with element strides (sxB, sxC, sxT) / (syB, syC, syT); channels-last
- * (sxC == 1) and channels-first (sxT == 1) both work, other strides take a slower generic path.  weight:
+ * (sxC == 1) and channels-first (sxT == 1) both work.  Channels-first with 16-byte aligned rows (strides of C and
+ * B multiples of 8), T % 8 == 0 and C % 16 == 0 runs on the tensor cores (the reference call site's contiguous
+ * (B, C, T) at T on the 8-frame grid); other strides and a ragged T take a slower generic path.  weight:
  * (C, 1, K) bf16 contiguous, K must be 15; bias: (C,) bf16.  lengths: NULL or int32[B]; frames t >= lengths[b]
  * read as zero and are written as zero (the reference op has no lengths). */
 int gsn_dwconv_silu_bf16(const void* x, const void* weight, const void* bias, void* y, int B, int C, int T, int K,
