@@ -348,29 +348,40 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
     const int q = warp & 3;                  // TMEM lane quarter this warp may read
     const int cg = e >> 2;                   // channels EPI_CH cg .. EPI_CH cg + EPI_CH - 1 of the item
     const int m = q * 32 + lane;             // row: frames t0 + 8 m .. + 7
+    int bias_c0 = -1;                        // channel block whose halved biases are in bh_all
+    float bh_all[EPI_CH];
     for (int i = 0; i < n_items; ++i) {
       const int acc = i & 1;
+      // the item's length and (when its channel block changed) biases are read before the accumulator wait, so
+      // their latency overlaps it
+      int c0, b, t0;
+      item(i, c0, b, t0);
+      const int len = len_of(b);
+      if (!GLU && c0 != bias_c0) {           // (the GLU forms have no registers to spare: they load per batch)
+#pragma unroll
+        for (int cc = 0; cc < EPI_CH; ++cc) bh_all[cc] = 0.5f * __bfloat162float(__ldg(p.bias + c0 + EPI_CH * cg + cc));
+        bias_c0 = c0;
+      }
       bool got = mbar_wait_bounded(&s.tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, kStatusTimeoutEpilogue);
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
-      int c0, b, t0;
-      item(i, c0, b, t0);
-      const int len = len_of(b);
       const int tf = t0 + 8 * m;             // this lane's first frame
       const bool live = t0 < len;            // warp-uniform: the MMAs ran
       const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * CT * 16);
+#pragma unroll
       for (int cb8 = 0; cb8 < EPI_CH; cb8 += EB) {
         const int cfirst = EPI_CH * cg + cb8;              // first of this batch's EB channels
         __nv_bfloat16* yrow = p.y + (int64_t)b * p.syB + (int64_t)(c0 + cfirst) * p.syC + tf;
-        // the batch's accumulator columns and biases in flight at once, one wait
+        // the batch's accumulator columns in flight at once, one wait
         uint32_t v[EB][8];
         float bh[EB];
         if (live) {
 #pragma unroll
           for (int cc = 0; cc < EB; ++cc) tmem_ld8(trow + (uint32_t)(16 * (cfirst + cc)), v[cc]);
 #pragma unroll
-          for (int cc = 0; cc < EB; ++cc) bh[cc] = 0.5f * __bfloat162float(p.bias[c0 + cfirst + cc]);
+          for (int cc = 0; cc < EB; ++cc)
+            bh[cc] = GLU ? 0.5f * __bfloat162float(__ldg(p.bias + c0 + cfirst + cc)) : bh_all[cb8 + cc];
           tmem_wait_ld();
 #pragma unroll
           for (int cc = 0; cc < EB; ++cc) tmem_regs_ready<8>(v[cc]);

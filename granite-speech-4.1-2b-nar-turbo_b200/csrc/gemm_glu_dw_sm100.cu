@@ -391,6 +391,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int acc = local & 1;
           const uint32_t use_par = (uint32_t)((local >> 1) & 1);
           ++local;
+          const int r = q * 32 + lane;
+          const bool valid = t0 + r < len;
+          // this row's LayerNorm statistics / activation scale, loaded ahead of the accumulator wait so that their
+          // latency is not on the GLU step's path (padding rows have none; their GLU row is zero anyway)
+          float rs = 1.f, rsm = 0.f;
+          if (LNF && valid) {
+            const float2 st = __ldg(p.row_stats + (int64_t)b * p.T + t0 + r);
+            rs = st.x;
+            rsm = st.y;
+          }
+          if (A8 && valid) rs = __ldg(p.row_scale + (int64_t)b * p.T + t0 + r);
           if (ok) {
             bool got = mbar_wait_bounded(&s.tfull[acc], use_par, abort_flag, kStatusTimeoutEpilogue);
             ok = __shfl_sync(0xffffffffu, got, 0);
@@ -398,17 +409,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (ok) {
             tc_fence_after();
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-            const int r = q * 32 + lane;
-            const bool valid = t0 + r < len;
             uint8_t* wrow = s.win + (2 * HALO + r) * WPITCH;
-            // LayerNorm folded in: this row's statistics (padding rows have none; their GLU row is zero anyway)
-            float rs = 1.f, rsm = 0.f;
-            if (LNF && valid) {
-              const float2 st = __ldg(p.row_stats + (int64_t)b * p.T + t0 + r);
-              rs = st.x;
-              rsm = st.y;
-            }
-            if (A8 && valid) rs = __ldg(p.row_scale + (int64_t)b * p.T + t0 + r);
+            const float rsh = 0.5f * rs;                 // bf16 weights: the halved column scale is 0.5
             const int nsub = whole ? 2 : 1;              // 32-channel sub-tiles of this warp
             for (int uu = 0; uu < nsub; ++uu) {
               const int cb = whole ? grp * 64 + uu * 32 : grp * 32;   // first of the sub-tile's 32 GLU channels
@@ -428,13 +430,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                   const int kk = c + z;
                   float a, g;
                   const int ga = gate_col + cb + kk;
-                  if (LNF) {
+                  if (LNF && !SCALED) {
+                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rsh, fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
+                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rsh, fmaf(-rsm, s.vc[ga], s.vb[ga]));
+                  } else if (LNF) {
                     a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rs * s.vs[cb + kk],
                              fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
                     g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rs * s.vs[ga], fmaf(-rsm, s.vc[ga], s.vb[ga]));
                   } else if (A8) {
                     a = fmaf((float)(int32_t)va[kk >> 4][kk & 15] * rs, s.vs[cb + kk], s.vb[cb + kk]);
                     g = fmaf((float)(int32_t)vg[kk >> 4][kk & 15] * rs, s.vs[ga], s.vb[ga]);
+                  } else if (!SCALED) {
+                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), 0.5f, s.vb[cb + kk]);
+                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), 0.5f, s.vb[ga]);
                   } else {
                     a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
                     g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[ga], s.vb[ga]);
