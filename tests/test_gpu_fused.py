@@ -124,50 +124,3 @@ def test_fused_vs_oracle():
     for b, L in enumerate(lens):
         assert_bf16_close(d[b, :L], ref[b, :L], f"fused utterance {b}")
 
-
-_SINGLE_CTA_SCRIPT = r"""
-import sys, numpy as np, torch
-sys.path[:0] = sys.argv[3].split("|")
-from granite_conv_b200 import ops, synth
-from granite_conv_b200.weights import prepare_from_params
-B, T = int(sys.argv[1].split(",")[0]), int(sys.argv[1].split(",")[1])
-lens = [int(v) for v in sys.argv[1].split(",")[2:]] or None
-p = prepare_from_params(synth.make_params(40 + T, w_std=0.05), device="cuda")
-a = torch.from_numpy(synth.make_activations(41 + T, (B * T, synth.D_MODEL))).to("cuda").to(torch.bfloat16)
-lt = None if lens is None else torch.tensor(lens, dtype=torch.int32, device="cuda")
-d = ops.gemm1_glu_dwconv(a, p.w1_glu, p.b1_glu, p.dw_w, p.dw_b, B, T, lengths=lt)
-torch.cuda.synchronize()
-np.save(sys.argv[2], d.view(torch.int16).cpu().numpy())
-"""
-
-
-@pytest.mark.parametrize("B,T,lens", [
-    (2, 256, None),
-    (5, 512, [0, 1, 127, 129, 512]),                     # odd batch: the last pair's second CTA has no utterance
-    (6, 1536, [1536, 641, 640, 639, 64, 1500]),          # pairs of unequal length
-    (10, 384, None),                                     # 80 pair units on the resident pairs: a split last pass
-])
-def test_cta_pairs_equal_single_ctas(B, T, lens, tmp_path):
-    """The CTA-pair kernel (this process) against the single-CTA kernel (a process with GSN_FUSED_PAIR=0): the
-    same bits on every frame, the same length rules."""
-    import os
-    import subprocess
-    import sys
-
-    from granite_conv_b200 import ops as _ops
-    spec = ",".join(str(v) for v in [B, T] + (lens or []))
-    out = tmp_path / "single.npy"
-    env = dict(os.environ, GSN_FUSED_PAIR="0")
-    paths = "|".join(p for p in sys.path if p)
-    subprocess.run([sys.executable, "-c", _SINGLE_CTA_SCRIPT, spec, str(out), paths], env=env, check=True,
-                   timeout=300)
-    ref = torch.from_numpy(np.load(out)).to(DEV).view(torch.bfloat16)
-    p = _prep(40 + T)
-    a = torch.from_numpy(synth.make_activations(41 + T, (B * T, synth.D_MODEL))).to(DEV).to(torch.bfloat16)
-    lt = None if lens is None else torch.tensor(lens, dtype=torch.int32, device=DEV)
-    d = _ops.gemm1_glu_dwconv(a, p.w1_glu, p.b1_glu, p.dw_w, p.dw_b, B, T, lengths=lt)
-    torch.cuda.synchronize()
-    dv, rv = d.view(B, T, -1), ref.view(B, T, -1)
-    for b in range(B):
-        end = T if lens is None else min(T, -(-int(lens[b]) // 128) * 128)
-        assert torch.equal(dv[b, :end], rv[b, :end]), f"utterance {b}: frames [0, {end})"
