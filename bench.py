@@ -947,10 +947,30 @@ def run_ours(args):
             **({"process_group": pg_info} if pg_info else {}),
             "gpu_launches": launches,
         }
-        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
-    return 0
+    return line if rank == 0 else None
+
+
+# The other configurations of the conv-module path, measured after the headline on one GPU so that every bench run
+# carries them: the depthwise kernel alone (channels-last rows as the standalone op's layout, and the reference
+# call site's channels-first layout, plain and GLU), one bf16 module, the int8-weight module and the W8A8 module.
+SECONDARY_WORKLOADS = ("dw", "dw_cf", "dw_cf_glu", "module", "module_i8", "module_w8a8")
+
+
+def secondary_configs(args) -> dict:
+    out = {}
+    for w in SECONDARY_WORKLOADS:
+        a = argparse.Namespace(**vars(args))
+        a.workload, a.steps, a.warmup, a.no_cpu, a.no_e2e = w, 20, 5, True, True
+        ln = run_ours(a)
+        r = ln["roofline"]
+        out[w] = {"config": ln["config"]["workload"], "value": ln["value"], "unit": ln["unit"], "dtype": ln["dtype"],
+                  "kernel": r["kernel"], "achieved": r["achieved"], "peak": r["peak"], "roofline_unit": r["unit"],
+                  "frac": r["frac"], "bound": r["bound"], "per_launch_us": r["per_launch_ms"] * 1e3,
+                  "peak_source": r.get("peak_source"), "clocks": ln["clocks"], "steps": 20, "warmup": 5,
+                  "gpu_launches": ln["gpu_launches"]}
+    return out
 
 
 def _tile_rows(c, tile=128):
@@ -1269,13 +1289,21 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="stack on one GPU: skip the other configurations measured after the headline")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: --warmup raised to 3", file=sys.stderr)
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    return run_ours(args)
+    line = run_ours(args)
+    if line is None:
+        return 0
+    if args.workload == "stack" and line["n_gpus"] == 1 and not args.no_configs:
+        line["other_configs"] = secondary_configs(args)
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 if __name__ == "__main__":

@@ -422,6 +422,36 @@ __global__ void __launch_bounds__(THREADS, 1)
               tmem_wait_ld_dep(va[0], va[1]);
               tmem_wait_ld_dep(vg[0], vg[1]);
               uint32_t o[16];
+              if constexpr (!SCALED && !A8) {
+                // bf16 weights: four columns at a time, the column parameters as 16-byte shared loads and the
+                // arithmetic on fp32 pairs (each lane of an f32x2 FMA is the fmaf of the general form below)
+                const pk2 rsh2 = pk_make(rsh, rsh), nrsm2 = pk_make(-rsm, -rsm), half2 = pk_make(0.5f, 0.5f);
+#pragma unroll
+                for (int c = 0; c < 32; c += 4) {
+                  const float4 ba = *reinterpret_cast<const float4*>(&s.vb[cb + c]);
+                  const float4 bg = *reinterpret_cast<const float4*>(&s.vb[gate_col + cb + c]);
+                  pk2 ia[2] = {pk_make(ba.x, ba.y), pk_make(ba.z, ba.w)};
+                  pk2 ig[2] = {pk_make(bg.x, bg.y), pk_make(bg.z, bg.w)};
+                  if constexpr (LNF) {
+                    const float4 ca = *reinterpret_cast<const float4*>(&s.vc[cb + c]);
+                    const float4 cg = *reinterpret_cast<const float4*>(&s.vc[gate_col + cb + c]);
+                    ia[0] = pk_fma(nrsm2, pk_make(ca.x, ca.y), ia[0]);
+                    ia[1] = pk_fma(nrsm2, pk_make(ca.z, ca.w), ia[1]);
+                    ig[0] = pk_fma(nrsm2, pk_make(cg.x, cg.y), ig[0]);
+                    ig[1] = pk_fma(nrsm2, pk_make(cg.z, cg.w), ig[1]);
+                  }
+#pragma unroll
+                  for (int z = 0; z < 2; ++z) {
+                    const int kk = c + 2 * z;
+                    const pk2 xa = pk_make(__uint_as_float(va[kk >> 4][kk & 15]), __uint_as_float(va[kk >> 4][(kk & 15) + 1]));
+                    const pk2 xg = pk_make(__uint_as_float(vg[kk >> 4][kk & 15]), __uint_as_float(vg[kk >> 4][(kk & 15) + 1]));
+                    const pk2 a2 = pk_fma(xa, LNF ? rsh2 : half2, ia[z]);
+                    const float2 g2 = pk_split(pk_fma(xg, LNF ? rsh2 : half2, ig[z]));
+                    const float2 h2 = pk_split(pk_fma(a2, pk_make(tanh_approx(g2.x), tanh_approx(g2.y)), a2));
+                    o[kk >> 1] = valid ? pack_bf16x2(h2.x, h2.y) : 0u;
+                  }
+                }
+              } else {
 #pragma unroll
               for (int c = 0; c < 32; c += 2) {
                 float h2[2];
@@ -450,6 +480,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                   h2[z] = fmaf(a, tanh_approx(g), a);
                 }
                 o[c >> 1] = valid ? pack_bf16x2(h2[0], h2[1]) : 0u;
+              }
               }
 #pragma unroll
               for (int c = 0; c < 4; ++c)
