@@ -21,8 +21,8 @@
 //               depthwise kernel, so the result is bit-identical to GEMM -> GLU tensor -> depthwise kernel; the
 //               warp's 16 x 128 outputs leave through a staging box in shared memory and one TMA store (boxes
 //               that would start before frame 0 or reach past the written range use plain stores);
-//               (3) window rows 128..141 move to rows 0..13 for the next tile.  After the last tile a flush pass
-//               computes the final 7 frames with zero GLU rows on the right.
+//               (3) the first epilogue warp moves window rows 128..141 to rows 0..13 for the next tile.  After
+//               the last tile a flush pass computes the final 7 frames with zero GLU rows on the right.
 // Lengths: GLU rows of frames t >= len[b] are zero, depthwise frames in [len, roundup128(len)) are written as
 // zero (the residual GEMM reads whole 128-row tiles), frames beyond are never touched.
 #include <type_traits>
@@ -422,65 +422,61 @@ __global__ void __launch_bounds__(THREADS, 1)
               tmem_wait_ld_dep(va[0], va[1]);
               tmem_wait_ld_dep(vg[0], vg[1]);
               uint32_t o[16];
-              if constexpr (!SCALED && !A8) {
-                // bf16 weights: four columns at a time, the column parameters as 16-byte shared loads and the
-                // arithmetic on fp32 pairs (each lane of an f32x2 FMA is the fmaf of the general form below)
-                const pk2 rsh2 = pk_make(rsh, rsh), nrsm2 = pk_make(-rsm, -rsm), half2 = pk_make(0.5f, 0.5f);
+              // four columns at a time: the column parameters as 16-byte shared loads, the arithmetic on fp32 pairs
+              // (each lane of an f32x2 FMA is one fmaf; a product alone is an FMA with a -0 addend, which rounds
+              // like the multiply).  Per column: a = x * m + i, with m = 1/2 (bf16 weights), rstd / 2 (LayerNorm
+              // folded), rstd * s / 2 (both) or s / 2 (scaled weights; W8A8: x = the s32 sum times the row scale),
+              // and i = b / 2 - rstd * mean * colsum * m' (LayerNorm folded) or b / 2
+              const pk2 rs2 = pk_make(rs, rs), rsh2 = pk_make(rsh, rsh), nrsm2 = pk_make(-rsm, -rsm);
+              const pk2 half2 = pk_make(0.5f, 0.5f), nz2 = pk_make(-0.0f, -0.0f);
 #pragma unroll
-                for (int c = 0; c < 32; c += 4) {
-                  const float4 ba = *reinterpret_cast<const float4*>(&s.vb[cb + c]);
-                  const float4 bg = *reinterpret_cast<const float4*>(&s.vb[gate_col + cb + c]);
-                  pk2 ia[2] = {pk_make(ba.x, ba.y), pk_make(ba.z, ba.w)};
-                  pk2 ig[2] = {pk_make(bg.x, bg.y), pk_make(bg.z, bg.w)};
+              for (int c = 0; c < 32; c += 4) {
+                const float4 ba = *reinterpret_cast<const float4*>(&s.vb[cb + c]);
+                const float4 bg = *reinterpret_cast<const float4*>(&s.vb[gate_col + cb + c]);
+                pk2 ia[2] = {pk_make(ba.x, ba.y), pk_make(ba.z, ba.w)};
+                pk2 ig[2] = {pk_make(bg.x, bg.y), pk_make(bg.z, bg.w)};
+                if constexpr (LNF) {
+                  const float4 ca = *reinterpret_cast<const float4*>(&s.vc[cb + c]);
+                  const float4 cg = *reinterpret_cast<const float4*>(&s.vc[gate_col + cb + c]);
+                  ia[0] = pk_fma(nrsm2, pk_make(ca.x, ca.y), ia[0]);
+                  ia[1] = pk_fma(nrsm2, pk_make(ca.z, ca.w), ia[1]);
+                  ig[0] = pk_fma(nrsm2, pk_make(cg.x, cg.y), ig[0]);
+                  ig[1] = pk_fma(nrsm2, pk_make(cg.z, cg.w), ig[1]);
+                }
+                pk2 ma[2] = {LNF ? rsh2 : half2, LNF ? rsh2 : half2}, mg[2] = {ma[0], ma[1]};
+                if constexpr (SCALED) {
+                  const float4 sa = *reinterpret_cast<const float4*>(&s.vs[cb + c]);
+                  const float4 sg = *reinterpret_cast<const float4*>(&s.vs[gate_col + cb + c]);
+                  ma[0] = pk_make(sa.x, sa.y);
+                  ma[1] = pk_make(sa.z, sa.w);
+                  mg[0] = pk_make(sg.x, sg.y);
+                  mg[1] = pk_make(sg.z, sg.w);
                   if constexpr (LNF) {
-                    const float4 ca = *reinterpret_cast<const float4*>(&s.vc[cb + c]);
-                    const float4 cg = *reinterpret_cast<const float4*>(&s.vc[gate_col + cb + c]);
-                    ia[0] = pk_fma(nrsm2, pk_make(ca.x, ca.y), ia[0]);
-                    ia[1] = pk_fma(nrsm2, pk_make(ca.z, ca.w), ia[1]);
-                    ig[0] = pk_fma(nrsm2, pk_make(cg.x, cg.y), ig[0]);
-                    ig[1] = pk_fma(nrsm2, pk_make(cg.z, cg.w), ig[1]);
-                  }
 #pragma unroll
-                  for (int z = 0; z < 2; ++z) {
-                    const int kk = c + 2 * z;
-                    const pk2 xa = pk_make(__uint_as_float(va[kk >> 4][kk & 15]), __uint_as_float(va[kk >> 4][(kk & 15) + 1]));
-                    const pk2 xg = pk_make(__uint_as_float(vg[kk >> 4][kk & 15]), __uint_as_float(vg[kk >> 4][(kk & 15) + 1]));
-                    const pk2 a2 = pk_fma(xa, LNF ? rsh2 : half2, ia[z]);
-                    const float2 g2 = pk_split(pk_fma(xg, LNF ? rsh2 : half2, ig[z]));
-                    const float2 h2 = pk_split(pk_fma(a2, pk_make(tanh_approx(g2.x), tanh_approx(g2.y)), a2));
-                    o[kk >> 1] = valid ? pack_bf16x2(h2.x, h2.y) : 0u;
+                    for (int z = 0; z < 2; ++z) {
+                      ma[z] = pk_fma(rs2, ma[z], nz2);
+                      mg[z] = pk_fma(rs2, mg[z], nz2);
+                    }
                   }
                 }
-              } else {
-#pragma unroll
-              for (int c = 0; c < 32; c += 2) {
-                float h2[2];
 #pragma unroll
                 for (int z = 0; z < 2; ++z) {
-                  const int kk = c + z;
-                  float a, g;
-                  const int ga = gate_col + cb + kk;
-                  if (LNF && !SCALED) {
-                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rsh, fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
-                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rsh, fmaf(-rsm, s.vc[ga], s.vb[ga]));
-                  } else if (LNF) {
-                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), rs * s.vs[cb + kk],
-                             fmaf(-rsm, s.vc[cb + kk], s.vb[cb + kk]));
-                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), rs * s.vs[ga], fmaf(-rsm, s.vc[ga], s.vb[ga]));
-                  } else if (A8) {
-                    a = fmaf((float)(int32_t)va[kk >> 4][kk & 15] * rs, s.vs[cb + kk], s.vb[cb + kk]);
-                    g = fmaf((float)(int32_t)vg[kk >> 4][kk & 15] * rs, s.vs[ga], s.vb[ga]);
-                  } else if (!SCALED) {
-                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), 0.5f, s.vb[cb + kk]);
-                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), 0.5f, s.vb[ga]);
+                  const int kk = c + 2 * z;
+                  const uint32_t a0 = va[kk >> 4][kk & 15], a1 = va[kk >> 4][(kk & 15) + 1];
+                  const uint32_t g0 = vg[kk >> 4][kk & 15], g1 = vg[kk >> 4][(kk & 15) + 1];
+                  pk2 xa, xg;
+                  if constexpr (A8) {
+                    xa = pk_fma(pk_make((float)(int32_t)a0, (float)(int32_t)a1), rs2, nz2);
+                    xg = pk_fma(pk_make((float)(int32_t)g0, (float)(int32_t)g1), rs2, nz2);
                   } else {
-                    a = fmaf(__uint_as_float(va[kk >> 4][kk & 15]), s.vs[cb + kk], s.vb[cb + kk]);
-                    g = fmaf(__uint_as_float(vg[kk >> 4][kk & 15]), s.vs[ga], s.vb[ga]);
+                    xa = pk_make(__uint_as_float(a0), __uint_as_float(a1));
+                    xg = pk_make(__uint_as_float(g0), __uint_as_float(g1));
                   }
-                  h2[z] = fmaf(a, tanh_approx(g), a);
+                  const pk2 a2 = pk_fma(xa, ma[z], ia[z]);
+                  const float2 g2 = pk_split(pk_fma(xg, mg[z], ig[z]));
+                  const float2 h2 = pk_split(pk_fma(a2, pk_make(tanh_approx(g2.x), tanh_approx(g2.y)), a2));
+                  o[kk >> 1] = valid ? pack_bf16x2(h2.x, h2.y) : 0u;
                 }
-                o[c >> 1] = valid ? pack_bf16x2(h2[0], h2[1]) : 0u;
-              }
               }
 #pragma unroll
               for (int c = 0; c < 4; ++c)
@@ -559,16 +555,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           else
             dw_rows(std::integral_constant<int, FPW / 2>{});
         }
-        epi_bar();
-        if (!flush) {
-          // (3) the tile's last 14 rows become the next window's left halo
-          if (et < 2 * HALO * 16) {
-            const int r = et >> 4, c = et & 15;
+        if (!flush && e == 0) {
+          // (3) the tile's last 14 rows become the next window's left halo.  Window rows 0..13 are read by this
+          // warp alone (output frames i < 16), so it moves them as soon as its own depthwise rows are done; the
+          // barrier below then orders the move before the next tile's GLU rows are written
+          __syncwarp();
+          for (int q2 = lane; q2 < 2 * HALO * 16; q2 += 32) {
+            const int r = q2 >> 4, c = q2 & 15;
             *reinterpret_cast<uint4*>(s.win + r * WPITCH + c * 16) =
                 *reinterpret_cast<const uint4*>(s.win + (BM + r) * WPITCH + c * 16);
           }
-          epi_bar();
         }
+        epi_bar();
       }
     }
     if (lane == 0) bulk_wait_group<0>();   // this warp's output boxes have landed before the CTA ends
