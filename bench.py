@@ -64,9 +64,9 @@ OUT_FLOP_PER_FRAME = 2 * HEADS * DIM_HEAD * D           # 2.097 MFLOP
 ATTN_FLOP_PER_QUERY_KEY = 3 * 2 * DIM_HEAD * HEADS      # 6144
 # DRAM bytes (read + write) of the fused up_conv + GLU + depthwise kernel (LayerNorm folded) per row of the 128-row
 # tiles it computes, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the module workload's
-# B=48, T=1536 chunk: 72.87 + 82.37 MB over 31,104 rows.  The traffic of a launch scales with the rows it computes.
+# B=48, T=1536 chunk: 72.66 + 84.82 MB over 31,104 rows.  The traffic of a launch scales with the rows it computes.
 # A constant: it is re-captured whenever the kernel changes (the command is in the kernel's ncu summary).
-GEMM1DW_DRAM_BYTES_PER_ROW = 4991
+GEMM1DW_DRAM_BYTES_PER_ROW = 5063
 DW_BYTES_PER_FRAME = 2 * I * 2                # read + write bf16: 8192 B
 DW_GLU_BYTES_PER_FRAME = 3 * I * 2            # GLU form: read value + gate, write: 12288 B
 DW_WORKLOADS = ("dw", "dw_cf", "dw_cf_glu")
