@@ -561,16 +561,19 @@ def run_ours(args):
         cnt_buf = torch.empty(max(c.B for c in chunks), dtype=torch.int32, device=dev)
         key_ws = torch.empty(int(L.gsn_bpe_head_workspace_bytes(1, max_pp)), dtype=torch.uint8, device=dev)
     act = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]   # ping-pong buffers
+    stats_buf = torch.empty((max_m, D // 256, 2), dtype=torch.float32, device=dev)   # chained layers' row statistics
     act2 = [torch.empty((c.B, c.T, D), dtype=torch.bfloat16, device=dev) for c in chunks]
 
     layer_events = []      # per recorded layer: (events[4], chunk) around layernorm, gemm1 + dwconv, gemm2
     widen_events = []      # int8: per recorded layer, the events around the weight widening
     w8_events = []         # W8A8: per recorded module call, (start, end, chunk)
 
-    def layer_kernels(x, out, c, p, lens, record):
+    def layer_kernels(x, out, c, p, lens, record, li=0, n_li=1):
         """The kernels of one conv module (the same launches the module op makes for T on the 128 grid): bf16
-        weights: LayerNorm statistics, up_conv + GLU + depthwise + SiLU on the raw frames with the LayerNorm folded
-        in, down_conv + residual (gsn_conv_module_lnfold_bf16); int8 weights (widened to bf16 once, when the layer was
+        weights, layer li of n_li chained as ConvModuleStack runs them (gsn_conv_module_lnfold_chain_bf16): LayerNorm
+        statistics (first layer only; later layers read the row statistics the previous down_conv wrote), up_conv +
+        GLU + depthwise + SiLU on the raw frames with the LayerNorm folded in, down_conv + residual (writing the row
+        statistics of its output unless it is the last layer); int8 weights (widened to bf16 once, when the layer was
         prepared): LayerNorm, the fused up_conv kernel on the LayerNorm output with the column scales, down_conv +
         residual (gsn_conv_module_i8w_widened).  CUDA events between them when `record`."""
         M = c.padded_frames
@@ -595,10 +598,11 @@ def run_ours(args):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if record:
             ev[0].record(stream)
+        has_ln = int8 or li == 0
         if int8:
             _lib.check(L.gsn_layernorm_bf16(x.data_ptr(), D, p.ln_w.data_ptr(), p.ln_b.data_ptr(), tp, D, M, D,
                                             p.ln_eps, lp, T, sp), "layernorm")
-        else:
+        elif has_ln:
             _lib.check(L.gsn_layernorm_stats_bf16(x.data_ptr(), D, tp, M, D, p.ln_eps, lp, T, sp), "ln_stats")
         if record:
             ev[1].record(stream)
@@ -606,22 +610,30 @@ def run_ours(args):
             _lib.check(L.gsn_gemm1_glu_dwconv_bf16(tp, p.w1w_glu.data_ptr(), p.s1_glu.data_ptr(), p.b1_glu.data_ptr(),
                                                    p.dw_w.data_ptr(), p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp,
                                                    sp), "gemm1_dw")
-        else:
+        elif has_ln:
             _lib.check(L.gsn_gemm1_lnfold_glu_dwconv_bf16(x.data_ptr(), p.w1g_glu.data_ptr(), p.b1g_glu.data_ptr(),
                                                           p.c1_glu.data_ptr(), tp, p.dw_w.data_ptr(),
                                                           p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp, sp),
                        "gemm1_dw")
+        else:
+            _lib.check(L.gsn_gemm1_lnfold_partials_glu_dwconv_bf16(
+                x.data_ptr(), p.w1g_glu.data_ptr(), p.b1g_glu.data_ptr(), p.c1_glu.data_ptr(), stats_buf.data_ptr(),
+                p.ln_eps, p.dw_w.data_ptr(), p.dw_b.data_ptr(), dp, c.B, T, D, 2 * I, lp, sp), "gemm1_dw")
         if record:
             ev[2].record(stream)
         if int8:
             _lib.check(L.gsn_gemm2_residual_bf16s(dp, p.w2w.data_ptr(), p.s2.data_ptr(), p.b2.data_ptr(),
                                                   x.data_ptr(), D, out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
+        elif li + 1 < n_li:
+            _lib.check(L.gsn_gemm2_residual_stats_bf16(dp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
+                                                       out.data_ptr(), D, M, I, D, lp, T, stats_buf.data_ptr(), sp),
+                       "gemm2")
         else:
             _lib.check(L.gsn_gemm2_residual_bf16(dp, p.w2.data_ptr(), p.b2.data_ptr(), x.data_ptr(), D,
                                                  out.data_ptr(), D, M, I, D, lp, T, sp), "gemm2")
         if record:
             ev[3].record(stream)
-            layer_events.append((ev, c))
+            layer_events.append((ev, c, has_ln))
 
     def ff_kernels(x, out, c, p, lens, record):
         """The three launches of gsn_ff_half_bf16: LayerNorm, up_proj + SiLU, down_proj + half-step residual."""
@@ -807,7 +819,7 @@ def run_ours(args):
                         dst = act2[ci]
                         n += 3
                 else:
-                    layer_kernels(src, dst, c, p, lens_dev[ci], record)
+                    layer_kernels(src, dst, c, p, lens_dev[ci], record, li, len(layers))
                     n += 4 if w8a8 else 3
                 src = dst
             if workload == "ctc":
@@ -1104,12 +1116,16 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
         names = ("widen_i8",) + names
         tot["widen_i8"] = sum(a.elapsed_time(b) for a, b in widen_events) * len(layer_events) / len(widen_events)
         work["widen_i8"] = 3.0 * (2 * I * D + D * I) * len(layer_events)
-    for ev, c in layer_events:
+    ln_launches = 0
+    for ev, c, has_ln in layer_events:
         for k, n in enumerate(names[-3:]):
-            tot[n] += ev[k].elapsed_time(ev[k + 1])
+            if k > 0 or has_ln:
+                tot[n] += ev[k].elapsed_time(ev[k + 1])
         valid = c.valid_frames
         rows = _tile_rows(c)
-        work[ln_name] += valid * (2 * D * 2 if ln_name == "layernorm" else D * 2 + 8)
+        if has_ln:
+            ln_launches += 1
+            work[ln_name] += valid * (2 * D * 2 if ln_name == "layernorm" else D * 2 + 8)
         work["gemm1_glu_dw"] += rows * GEMM1_FLOP_PER_FRAME
         work["gemm2_residual"] += rows * GEMM2_FLOP_PER_FRAME
     all_ms = sum(tot.values())
@@ -1118,8 +1134,9 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
         tensor = n.startswith("gemm")
         ach = work[n] / (tot[n] / 1e3) / (1e12 if tensor else 1e9)
         pk = peaks["bf16_tflops_sustained"] if tensor else peaks["hbm_gbs"]
-        out[n] = {"ms_per_launch": tot[n] / len(layer_events), "share": tot[n] / all_ms, "achieved": ach,
-                  "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
+        launches = ln_launches if n == ln_name else len(layer_events)
+        out[n] = {"ms_per_launch": tot[n] / max(1, launches), "launches": launches, "share": tot[n] / all_ms,
+                  "achieved": ach, "unit": "TFLOP/s" if tensor else "GB/s", "peak": pk, "frac": ach / pk}
     out["gemm1_glu_dw"]["rows_per_launch"] = work["gemm1_glu_dw"] / GEMM1_FLOP_PER_FRAME / len(layer_events)
     return out
 

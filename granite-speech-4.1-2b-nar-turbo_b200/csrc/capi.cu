@@ -222,15 +222,18 @@ static int gemm1(const void* a, const void* w, const float* scale, const float* 
 
 static int gemm2(const void* d, const void* w, const float* scale, const float* b, const void* res, int64_t ld_res,
                  void* out, int64_t ld_out, int M, int K, int N, const int32_t* lengths, int T, int i8,
-                 int scaled, gsn_stream_t stream, const char* name) {
+                 int scaled, gsn_stream_t stream, const char* name, float* row_partials = nullptr) {
   if (int rc = check_gemm(name, d, w, b, out, M, K, N)) return rc < 0 ? ok() : rc;
   if (res && !aligned(res, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: residual must be 16-byte aligned", name);
   if (scaled && (!scale || !aligned(scale, 16))) return fail(GSN_ERR_INVALID_ARG, "%s: scale pointer", name);
   if (ld_out % 8 || ld_out < N || (res && (ld_res % 8 || ld_res < N)))
     return fail(GSN_ERR_UNSUPPORTED, "%s: row strides must be >= N and multiples of 8", name);
   if (int rc = check_lengths(name, lengths, T, M)) return rc;
+  if (row_partials && (N % 256 || !aligned(row_partials, 8)))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: row partials need N %% 256 == 0 and 8-byte alignment", name);
   GemmArgs g{(const __nv_bfloat16*)d, w, b, scaled ? scale : nullptr, (const __nv_bfloat16*)res,
              (__nv_bfloat16*)out, ld_out, ld_res, M, N, K, i8, lengths, T};
+  g.row_partials = (float2*)row_partials;
   return finish(launch_gemm(g, kEpiResidual, (cudaStream_t)stream), name);
 }
 
@@ -254,6 +257,14 @@ int gsn_gemm2_residual_bf16(const void* d, const void* w2, const float* b2, cons
                             gsn_stream_t stream) {
   return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 0, 0, stream,
                "gsn_gemm2_residual_bf16");
+}
+
+int gsn_gemm2_residual_stats_bf16(const void* d, const void* w2, const float* b2, const void* residual,
+                                  int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N,
+                                  const int32_t* lengths, int T, float* row_partials, gsn_stream_t stream) {
+  if (!row_partials && M > 0) return fail(GSN_ERR_INVALID_ARG, "gsn_gemm2_residual_stats_bf16: null row_partials");
+  return gemm2(d, w2, nullptr, b2, residual, ld_res, out, ld_out, M, K, N, lengths, T, 0, 0, stream,
+               "gsn_gemm2_residual_stats_bf16", row_partials);
 }
 
 int gsn_gemm2_residual_i8w(const void* d, const void* w2q, const float* s2, const float* b2, const void* residual,
@@ -306,6 +317,29 @@ int gsn_gemm1_lnfold_glu_dwconv_bf16(const void* x, const void* w1g_glu, const f
     return fail(GSN_ERR_UNSUPPORTED, "%s: x, w1g, d, b1g, c1 must be 16-byte aligned, row_stats 8-byte", name);
   GemmDwArgs g{(const __nv_bfloat16*)x, (const __nv_bfloat16*)w1g_glu, b1g_glu, nullptr, (const __nv_bfloat16*)dw_w,
                (const __nv_bfloat16*)dw_b, (__nv_bfloat16*)d, lengths, B, T, K, N, (const float2*)row_stats, c1_glu};
+  return finish(launch_gemm_glu_dw(g, (cudaStream_t)stream), name);
+}
+
+int gsn_gemm1_lnfold_partials_glu_dwconv_bf16(const void* x, const void* w1g_glu, const float* b1g_glu,
+                                              const float* c1_glu, const float* row_partials, float ln_eps,
+                                              const void* dw_w, const void* dw_b, void* d, int B, int T, int K,
+                                              int N, const int32_t* lengths, gsn_stream_t stream) {
+  const char* name = "gsn_gemm1_lnfold_partials_glu_dwconv_bf16";
+  if (B < 0 || T < 0 || K <= 0 || N <= 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d K=%d N=%d", name, B, T, K, N);
+  if ((int64_t)B * T == 0) return ok();
+  if ((int64_t)B * T > (int64_t)0x7fffffff) return fail(GSN_ERR_UNSUPPORTED, "%s: B*T too large", name);
+  if (!x || !w1g_glu || !b1g_glu || !c1_glu || !row_partials || !dw_w || !dw_b || !d)
+    return fail(GSN_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (T % 128 || K % 256 || K > 2048 || N % 256)
+    return fail(GSN_ERR_UNSUPPORTED, "%s: needs T %% 128 == 0, K %% 256 == 0, K <= 2048, N %% 256 == 0 (T=%d K=%d N=%d)",
+                name, T, K, N);
+  if (!aligned(x, 16) || !aligned(w1g_glu, 16) || !aligned(d, 16) || !aligned(b1g_glu, 16) || !aligned(c1_glu, 16) ||
+      !aligned(row_partials, 8) || !aligned(dw_w, 2) || !aligned(dw_b, 2))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: x, w1g, d, b1g, c1 must be 16-byte aligned, row_partials 8-byte", name);
+  GemmDwArgs g{(const __nv_bfloat16*)x, (const __nv_bfloat16*)w1g_glu, b1g_glu, nullptr, (const __nv_bfloat16*)dw_w,
+               (const __nv_bfloat16*)dw_b, (__nv_bfloat16*)d, lengths, B, T, K, N, nullptr, c1_glu};
+  g.row_partials = (const float2*)row_partials;
+  g.ln_eps = ln_eps;
   return finish(launch_gemm_glu_dw(g, (cudaStream_t)stream), name);
 }
 
@@ -690,11 +724,13 @@ static int conv_module(const void* x, const void* ln_w, const void* ln_b, const 
   return finish(rc, name);
 }
 
-int gsn_conv_module_lnfold_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
-                                const void* dw_w, const void* dw_b, const void* w2, const float* b2,
-                                const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
-                                float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
-  const char* name = "gsn_conv_module_lnfold_bf16";
+// The LayerNorm-folded module: row statistics (a launch, or the previous layer's row partials), the fused up_conv
+// kernel, down_conv + residual (writing the next layer's row partials when stats_out is given).
+static int lnfold_module(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                         const void* dw_w, const void* dw_b, const void* w2, const float* b2, const int32_t* lengths,
+                         int add_residual, void* out, int B, int T, int D, int inner, float ln_eps,
+                         const float* stats_in, float* stats_out, void* workspace, size_t workspace_bytes,
+                         gsn_stream_t stream, const char* name) {
   if (B < 0 || T < 0) return fail(GSN_ERR_INVALID_ARG, "%s: B=%d T=%d", name, B, T);
   if ((int64_t)B * T == 0) return ok();
   if (!x || !w1g_glu || !b1g_glu || !c1_glu || !dw_w || !dw_b || !w2 || !b2 || !out)
@@ -709,19 +745,45 @@ int gsn_conv_module_lnfold_bf16(const void* x, const void* w1g_glu, const float*
     return fail(GSN_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", name, workspace_bytes, need);
   if (!aligned(workspace, 256)) return fail(GSN_ERR_UNSUPPORTED, "%s: workspace must be 256-byte aligned", name);
   if (!aligned(x, 16) || !aligned(out, 16)) return fail(GSN_ERR_UNSUPPORTED, "%s: x/out must be 16-byte aligned", name);
+  if ((stats_in && !aligned(stats_in, 8)) || (stats_out && !aligned(stats_out, 8)))
+    return fail(GSN_ERR_UNSUPPORTED, "%s: row partials must be 8-byte aligned", name);
   // workspace: d = the depthwise output [M, inner], then the row statistics [M] x (rstd, rstd * mean)
   __nv_bfloat16* d = (__nv_bfloat16*)workspace;
   float2* stats = (float2*)((char*)workspace + align256((size_t)M * inner * 2));
   const cudaStream_t st = (cudaStream_t)stream;
-  int rc = launch_ln_stats((const __nv_bfloat16*)x, D, stats, M, D, ln_eps, lengths, T, st);
-  if (rc) return finish(rc, name);
+  int rc = 0;
+  if (!stats_in) {
+    rc = launch_ln_stats((const __nv_bfloat16*)x, D, stats, M, D, ln_eps, lengths, T, st);
+    if (rc) return finish(rc, name);
+  }
   GemmDwArgs gd{(const __nv_bfloat16*)x, (const __nv_bfloat16*)w1g_glu, b1g_glu, nullptr, (const __nv_bfloat16*)dw_w,
-                (const __nv_bfloat16*)dw_b, d, lengths, B, T, D, 2 * inner, stats, c1_glu};
+                (const __nv_bfloat16*)dw_b, d, lengths, B, T, D, 2 * inner, stats_in ? nullptr : stats, c1_glu};
+  gd.row_partials = (const float2*)stats_in;
+  gd.ln_eps = ln_eps;
   rc = launch_gemm_glu_dw(gd, st);
   if (rc) return finish(rc, name);
   GemmArgs g2{d, w2, b2, nullptr, add_residual ? (const __nv_bfloat16*)x : nullptr, (__nv_bfloat16*)out, D, D, M, D,
               inner, 0, lengths, T};
+  g2.row_partials = (float2*)stats_out;
   return finish(launch_gemm(g2, kEpiResidual, st), name);
+}
+
+int gsn_conv_module_lnfold_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                                const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
+                                float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  return lnfold_module(x, w1g_glu, b1g_glu, c1_glu, dw_w, dw_b, w2, b2, lengths, add_residual, out, B, T, D, inner,
+                       ln_eps, nullptr, nullptr, workspace, workspace_bytes, stream, "gsn_conv_module_lnfold_bf16");
+}
+
+int gsn_conv_module_lnfold_chain_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                      const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                                      const int32_t* lengths, int add_residual, void* out, int B, int T, int D,
+                                      int inner, float ln_eps, const float* stats_in, float* stats_out,
+                                      void* workspace, size_t workspace_bytes, gsn_stream_t stream) {
+  return lnfold_module(x, w1g_glu, b1g_glu, c1_glu, dw_w, dw_b, w2, b2, lengths, add_residual, out, B, T, D, inner,
+                       ln_eps, stats_in, stats_out, workspace, workspace_bytes, stream,
+                       "gsn_conv_module_lnfold_chain_bf16");
 }
 
 int gsn_conv_module_bf16(const void* x, const void* ln_w, const void* ln_b, const void* w1_glu,

@@ -61,6 +61,8 @@ struct Params {
   const float2* row_stats;    // LayerNorm folded in: per-row (rstd, rstd * mean), rows b * T + t
   const float* colsum;        // LayerNorm folded in: [N] column sums of W'
   const float* row_scale;     // A8: per-row scale of the int8 activations, rows b * T + t
+  const float2* row_partials; // LayerNorm folded in, instead of row_stats: per row K / 256 blocks of (mean, M2)
+  float ln_eps;
   int B, T, K, N;
 };
 
@@ -152,10 +154,12 @@ struct Units {
 };
 
 // SCALED: per-column scale on the accumulator (int8 weights widened to bf16).  LNF: LayerNorm folded in -- A holds
-// the raw frames, W the weights times gamma, and the accumulator becomes rstd * (acc - mean * colsum) + bias.
+// the raw frames, W the weights times gamma, and the accumulator becomes rstd * (acc - mean * colsum) + bias; with
+// LNF = 1 the row statistics come as (rstd, rstd * mean), with LNF = 2 as the previous residual GEMM's per-block
+// (mean, M2), merged here.
 // A8 (W8A8): A and W are int8 (128 per K-block, the same bytes per stage as 64 bf16), kind::i8 MMAs with s32
 // accumulators; the epilogue takes fp32(acc) * row_scale * col_scale + bias, as the standalone int8 GEMM does.
-template <bool SCALED, bool LNF, bool A8 = false>
+template <bool SCALED, int LNF, bool A8 = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_glu_dw_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmW64, const __grid_constant__ CUtensorMap tmD, Params p) {
@@ -397,9 +401,30 @@ __global__ void __launch_bounds__(THREADS, 1)
           // latency is not on the GLU step's path (padding rows have none; their GLU row is zero anyway)
           float rs = 1.f, rsm = 0.f;
           if (LNF && valid) {
-            const float2 st = __ldg(p.row_stats + (int64_t)b * p.T + t0 + r);
-            rs = st.x;
-            rsm = st.y;
+            if constexpr (LNF == 2) {
+              // merge the row's 256-column blocks of equal counts one by one (Chan et al.): block j moves the mean
+              // by delta / (j + 1) and adds its M2 plus delta^2 * 256 j / (j + 1); rstd as the statistics kernel
+              // forms it
+              const float2* pp = p.row_partials + ((int64_t)b * p.T + t0 + r) * (p.K / 256);
+              const int np = p.K / 256;
+              const float2 p0 = __ldg(pp);
+              float mean = p0.x, m2 = p0.y;
+#pragma unroll
+              for (int j = 1; j < 8; ++j) {
+                if (j < np) {
+                  const float2 v = __ldg(pp + j);
+                  const float delta = v.x - mean;
+                  mean = fmaf(delta, 1.0f / (float)(j + 1), mean);
+                  m2 += fmaf(delta * delta, 256.0f * (float)j / (float)(j + 1), v.y);
+                }
+              }
+              rs = rsqrtf(m2 * (1.0f / (float)p.K) + p.ln_eps);
+              rsm = rs * mean;
+            } else {
+              const float2 st = __ldg(p.row_stats + (int64_t)b * p.T + t0 + r);
+              rs = st.x;
+              rsm = st.y;
+            }
           }
           if (A8 && valid) rs = __ldg(p.row_scale + (int64_t)b * p.T + t0 + r);
           if (ok) {
@@ -591,7 +616,7 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   const int esz = a.a_int8 ? 1 : 2;
   const CUtensorMapDataType dt = a.a_int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   if (a.T % G::BM || a.K % kbe || a.N % G::BN) return (int)cudaErrorInvalidValue;
-  if (a.a_int8 && (!a.col_scale || !a.row_scale || a.row_stats)) return (int)cudaErrorInvalidValue;
+  if (a.a_int8 && (!a.col_scale || !a.row_scale || a.row_stats || a.row_partials)) return (int)cudaErrorInvalidValue;
   CUtensorMap tmA, tmW;
   const int64_t M = (int64_t)a.B * a.T;
   {
@@ -628,15 +653,19 @@ int launch_gemm_glu_dw(const GemmDwArgs& a, cudaStream_t stream) {
   p.row_stats = a.row_stats;
   p.colsum = a.colsum;
   p.row_scale = a.row_scale;
+  p.row_partials = a.row_partials;
+  p.ln_eps = a.ln_eps;
   p.B = a.B;
   p.T = a.T;
   p.K = a.K;
   p.N = a.N;
   const int smem = (int)sizeof(G::Smem) + 1024;
-  if (a.row_stats && !a.colsum) return (int)cudaErrorInvalidValue;
-  auto kern = a.a_int8 ? G::gemm_glu_dw_kernel<true, false, true>
-             : a.col_scale ? (a.row_stats ? G::gemm_glu_dw_kernel<true, true> : G::gemm_glu_dw_kernel<true, false>)
-                           : (a.row_stats ? G::gemm_glu_dw_kernel<false, true> : G::gemm_glu_dw_kernel<false, false>);
+  if ((a.row_stats || a.row_partials) && !a.colsum) return (int)cudaErrorInvalidValue;
+  if (a.row_partials && (a.row_stats || a.col_scale || a.K % 256 || a.K > 2048)) return (int)cudaErrorInvalidValue;
+  auto kern = a.a_int8 ? G::gemm_glu_dw_kernel<true, 0, true>
+             : a.col_scale ? (a.row_stats ? G::gemm_glu_dw_kernel<true, 1> : G::gemm_glu_dw_kernel<true, 0>)
+             : a.row_partials ? G::gemm_glu_dw_kernel<false, 2>
+                              : (a.row_stats ? G::gemm_glu_dw_kernel<false, 1> : G::gemm_glu_dw_kernel<false, 0>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return (int)e;
   const int64_t units = (int64_t)a.B * (a.N / G::BN);

@@ -63,6 +63,7 @@ struct KParams {
   unsigned long long* argmax_keys;        // ARGMAX: per row, the best (bf16 logit, lowest column) as one key
   int n_major;                            // walk tiles column block by column block (W read once)
   int withhold_load;                      // test only: operand load #k of every CTA armed but never issued (-1: none)
+  float2* row_partials;                   // RESIDUAL: per row and 256-column block, (mean, M2) of the bf16 output
 };
 
 // 128-row block `blk` of the M range holds at least one valid frame (a block lies inside one utterance)
@@ -75,6 +76,19 @@ __device__ __forceinline__ bool rows_active(const KParams& p, int blk) {
 }
 
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Row statistics of a packed bf16 pair about the shift k (as fp32 pairs in 64-bit registers): with d = x - k,
+// s += d and q += d * d, each lane of the f32x2 FMAs one fmaf (d = x * 1 - k is the rounded difference).
+__device__ __forceinline__ void row_stats_pair(uint32_t w, uint64_t nk2, uint64_t& s2, uint64_t& q2) {
+  asm("{\n\t.reg .b32 lo, hi;\n\t.reg .b64 x, one, d;\n\t"
+      "shl.b32 lo, %2, 16;\n\tand.b32 hi, %2, 0xFFFF0000;\n\tmov.b64 x, {lo, hi};\n\t"
+      "mov.b64 one, 0x3F8000003F800000;\n\t"
+      "fma.rn.f32x2 d, x, one, %3;\n\t"
+      "fma.rn.f32x2 %0, d, one, %0;\n\t"
+      "fma.rn.f32x2 %1, d, d, %1;\n\t}"
+      : "+l"(s2), "+l"(q2)
+      : "r"(w), "l"(nk2));
+}
 
 // The tile list every role of a CTA walks (s = blockIdx.x + k * gridDim.x).  With lengths (B = M / T utterances of
 // T % 128 == 0 frames), the list holds first the tiles of the 128-row blocks that contain valid frames, so those are
@@ -237,11 +251,13 @@ struct Epilogue {
   int M;
   const float* row_scale;
   float rs;                               // A8: this lane's row scale for the current tile
+  float2* row_partials;                   // RESIDUAL: output row statistics per 256-column block, or null
+  int n_part;
   bool has_res;
   int lane, swz;
   uint32_t su;                            // sub-tiles handled so far: buffer su & 1, its use count su >> 1
   uint32_t res_pend;                      // lane 0: buffers whose residual copy is issued and not yet waited for
-  uint32_t res_par[2];                    //   and the phase parity that copy completes
+  uint32_t res_par;                       //   and, bit b, the phase parity buffer b's copy completes
 
   __device__ void init(EpiSmem& e, int ew, const CUtensorMap* o, const CUtensorMap* r, const KParams& p) {
     vb = e.vec[ew][0];
@@ -254,6 +270,8 @@ struct Epilogue {
     M = p.M;
     row_scale = p.row_scale;
     rs = 1.0f;
+    row_partials = EPI == kEpiResidual ? p.row_partials : nullptr;
+    n_part = p.N / BN;
     has_res = EPI == kEpiResidual && p.residual != nullptr;
     alpha = EPI == kEpiResidual ? p.out_scale : 1.0f;
     lengths = p.lengths;
@@ -262,7 +280,7 @@ struct Epilogue {
     swz = (lane >> 1) & 3;
     su = 0;
     res_pend = 0;
-    res_par[0] = res_par[1] = 0;
+    res_par = 0;
   }
 
   // The tile's 256 bias (and scale) values into the warp's slice.  For the GLU they are halved:
@@ -297,7 +315,7 @@ struct Epilogue {
   __device__ void load_residual(uint32_t sub, int col, int row0) {
     const uint32_t buf = sub & 1;
     res_pend |= 1u << buf;
-    res_par[buf] = (sub >> 1) & 1;
+    res_par = (res_par & ~(1u << buf)) | (((sub >> 1) & 1u) << buf);
     mbar_arrive_expect_tx(res0 + buf, BOX_BYTES);
     tma_load_2d(stage0 + buf * BOX_BYTES, tmR, res0 + buf, col, row0);
   }
@@ -348,6 +366,11 @@ struct Epilogue {
       rs = row < M ? __ldg(row_scale + row) : 0.f;
     }
     // SiLU: this lane's row is a padding frame -> zero, so the next GEMM sees what a masked input gives
+    // RESIDUAL with row_partials: the tile row's 256 bf16 outputs as (mean, M2), summed about the row's first output
+    // (a shift near the mean keeps the sum of squares free of cancellation); the next LayerNorm merges the blocks
+    float ps_k = 0.f;
+    uint64_t ps_nk2 = 0;                                // (-k, -k)
+    uint64_t ps_s2[4] = {0, 0, 0, 0}, ps_q2[4] = {0, 0, 0, 0};   // four independent chains of fp32-pair sums
     bool row_valid = true;
     if (EPI == kEpiSilu && lengths != nullptr) {
       const int row = row0 + lane;
@@ -455,6 +478,17 @@ struct Epilogue {
         w.z = pack_bf16x2(o[c * 8 + 4] + r[4], o[c * 8 + 5] + r[5]);
         w.w = pack_bf16x2(o[c * 8 + 6] + r[6], o[c * 8 + 7] + r[7]);
         *pc = w;
+        if (EPI == kEpiResidual && row_partials != nullptr) {
+          if (u == 0 && c == 0) {
+            ps_k = bf16lo_to_f32(w.x);
+            const uint32_t nk = __float_as_uint(-ps_k);
+            ps_nk2 = ((uint64_t)nk << 32) | nk;
+          }
+          row_stats_pair(w.x, ps_nk2, ps_s2[0], ps_q2[0]);
+          row_stats_pair(w.y, ps_nk2, ps_s2[1], ps_q2[1]);
+          row_stats_pair(w.z, ps_nk2, ps_s2[2], ps_q2[2]);
+          row_stats_pair(w.w, ps_nk2, ps_s2[3], ps_q2[3]);
+        }
       }
       fence_proxy_async_smem();          // the generic-proxy writes are visible to the TMA store
       __syncwarp();
@@ -462,6 +496,18 @@ struct Epilogue {
         tma_store_2d(tmO, sb, ocol0 + u * BOX, row0);
         bulk_commit_group();
       }
+    }
+    if (EPI == kEpiResidual && row_partials != nullptr && row0 + lane < M) {
+      constexpr float inv = 1.0f / BN;
+      float ps_s = 0.f, ps_q = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ps_s += __uint_as_float((uint32_t)ps_s2[i]) + __uint_as_float((uint32_t)(ps_s2[i] >> 32));
+        ps_q += __uint_as_float((uint32_t)ps_q2[i]) + __uint_as_float((uint32_t)(ps_q2[i] >> 32));
+      }
+      const float mt = ps_s * inv;
+      row_partials[(int64_t)(row0 + lane) * n_part + ocol0 / BN] =
+          make_float2(ps_k + mt, fmaxf(fmaf(-ps_s, mt, ps_q), 0.f));
     }
     return true;
   }
@@ -472,7 +518,7 @@ struct Epilogue {
       // after an unwind, residual copies still in flight land before the shared memory is released (bounded)
       for (uint32_t b = 0; b < 2; ++b)
         if (res_pend & (1u << b))
-          mbar_wait_bounded(res0 + b, res_par[b], nullptr, kStatusTimeoutEpilogue, 100000000ull);
+          mbar_wait_bounded(res0 + b, (res_par >> b) & 1u, nullptr, kStatusTimeoutEpilogue, 100000000ull);
     }
     __syncwarp();
   }
@@ -1061,6 +1107,7 @@ KParams make_params(const GemmArgs& a) {
   p.argmax_keys = a.argmax_keys;
   p.n_major = a.n_major;
   p.withhold_load = a.withhold_load;
+  p.row_partials = a.row_partials;
   return p;
 }
 

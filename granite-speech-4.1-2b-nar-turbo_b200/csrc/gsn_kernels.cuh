@@ -43,6 +43,7 @@ struct GemmArgs {
   const float* row_scale = nullptr;   //   acc is scaled by row_scale[m] * col_scale[n] (GLU and RESIDUAL only)
   int withhold_load = -1;        // test only (>= 0): every CTA's producer arms the barrier of its operand load #k
                                  //   without issuing the copies, so the MMA warp's bounded wait runs out
+  float2* row_partials = nullptr;  // RESIDUAL only: [M][N / 256] (mean, M2) of each output row's 256-column blocks
 };
 
 // LINEAR: out = acc + b, 128-row tiles of pure padding skipped (nothing written there)
@@ -79,6 +80,8 @@ struct GemmDwArgs {
   const float* colsum;           // with row_stats: [N] column sums of w
   int a_int8 = 0;                // W8A8: a int8 [B*T, K], w int8 [N, K] (kind::i8), needs col_scale and row_scale
   const float* row_scale = nullptr;
+  const float2* row_partials = nullptr;   // LayerNorm folded in, instead of row_stats: [B*T][K / 256] (mean, M2) of
+  float ln_eps = 0.f;                     //   each row's 256-column blocks, merged here into (rstd, rstd * mean)
 };
 int launch_gemm_glu_dw(const GemmDwArgs& args, cudaStream_t stream);
 

@@ -42,6 +42,12 @@ SIGNATURES = {
                                                 _vp]),
     "gsn_conv_module_lnfold_bf16": (_i32, [_vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _vp, _i32, _vp, _i32, _i32, _i32,
                                            _i32, _f32, _vp, _sz, _vp]),
+    "gsn_gemm2_residual_stats_bf16": (_i32, [_vp, _vp, _fp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp, _i32, _fp,
+                                             _vp]),
+    "gsn_gemm1_lnfold_partials_glu_dwconv_bf16": (_i32, [_vp, _vp, _fp, _fp, _fp, _f32, _vp, _vp, _vp, _i32, _i32,
+                                                         _i32, _i32, _vp, _vp]),
+    "gsn_conv_module_lnfold_chain_bf16": (_i32, [_vp, _vp, _fp, _fp, _vp, _vp, _vp, _fp, _vp, _i32, _vp, _i32, _i32,
+                                                 _i32, _i32, _f32, _fp, _fp, _vp, _sz, _vp]),
     "gsn_gemm_silu_bf16": (_i32, [_vp, _vp, _fp, _vp, _i32, _i32, _i32, _vp, _i32, _vp]),
     "gsn_gemm_residual_scaled_bf16": (_i32, [_vp, _vp, _fp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _i32,
                                              _vp]),

@@ -7,7 +7,7 @@ from typing import List, Optional, Sequence, Tuple
 
 import torch
 
-from . import ops
+from . import _lib, ops
 from .weights import PreparedConvModule
 
 
@@ -24,11 +24,48 @@ class ConvModuleStack:
     def d_model(self) -> int:
         return self.layers[0].d_model
 
+    def chained(self, x: torch.Tensor) -> bool:
+        """Whether the layers run chained: bf16 weights with the LayerNorm folded in and T % 128 == 0."""
+        return (not self.int8 and all(p.has_ln_fold for p in self.layers) and x.dim() == 3
+                and x.shape[1] % 128 == 0 and x.shape[2] % 256 == 0)
+
     def __call__(self, x: torch.Tensor, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """x: bf16 [B, T, D] on the GPU; lengths: int32 [B] on the GPU or None.  Returns bf16 [B, T, D]."""
+        """x: bf16 [B, T, D] on the GPU; lengths: int32 [B] on the GPU or None.  Returns bf16 [B, T, D].
+
+        With LayerNorm-folded bf16 weights the layers are chained (gsn_conv_module_lnfold_chain_bf16): every
+        layer's down_conv + residual also writes its output rows' statistics, which the next layer's folded
+        LayerNorm reads, so only the first layer launches a statistics kernel."""
+        if self.chained(x):
+            return self._run_chained(x, lengths)
         for p in self.layers:
             x = ops.run_conv_module(x, p, lengths=lengths, add_residual=True, int8=self.int8)
         return x
+
+    def _run_chained(self, x: torch.Tensor, lengths: Optional[torch.Tensor]) -> torch.Tensor:
+        if x.dtype != torch.bfloat16 or not x.is_cuda:
+            raise RuntimeError("ConvModuleStack: x must be a bf16 CUDA tensor")
+        B, T, D = x.shape
+        inner = self.layers[0].d_inner
+        x = x.contiguous()
+        lens = None if lengths is None else lengths.to(device=x.device, dtype=torch.int32).contiguous()
+        if B * T == 0:
+            return x.clone()
+        L = _lib.lib()
+        nbytes = int(L.gsn_conv_module_workspace_bytes(B, T, D, inner))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        stats = torch.empty((B * T, D // 256, 2), dtype=torch.float32, device=x.device)   # row partials, reused
+        bufs = [torch.empty_like(x), torch.empty_like(x)]
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        src = x
+        for i, p in enumerate(self.layers):
+            dst = bufs[i % 2]
+            _lib.call("gsn_conv_module_lnfold_chain_bf16", src.data_ptr(), p.w1g_glu.data_ptr(), p.b1g_glu.data_ptr(),
+                      p.c1_glu.data_ptr(), p.dw_w.data_ptr(), p.dw_b.data_ptr(), p.w2.data_ptr(), p.b2.data_ptr(),
+                      None if lens is None else lens.data_ptr(), 1, dst.data_ptr(), B, T, D, inner, float(p.ln_eps),
+                      None if i == 0 else stats.data_ptr(),
+                      stats.data_ptr() if i + 1 < len(self.layers) else None, ws.data_ptr(), nbytes, st)
+            src = dst
+        return src
 
     def run_chunks(self, chunks: Sequence[Tuple[torch.Tensor, Optional[torch.Tensor]]],
                    streams: Optional[Sequence[torch.cuda.Stream]] = None) -> List[torch.Tensor]:

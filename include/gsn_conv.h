@@ -140,6 +140,39 @@ int gsn_conv_module_lnfold_bf16(const void* x, const void* w1g_glu, const float*
                                 const int32_t* lengths, int add_residual, void* out, int B, int T, int D, int inner,
                                 float ln_eps, void* workspace, size_t workspace_bytes, gsn_stream_t stream);
 
+/* ---- a stack of LayerNorm-folded modules: each layer's row statistics from the previous layer's down_conv -------
+ * No counterpart in the reference, which runs every layer's LayerNorm (conformer.py:164,176) on its own.  In a stack
+ * (the encoder's conv modules back to back, conformer.py:207 feeding the next block) the down_conv + residual
+ * epilogue already holds each output row, so it also writes the row's statistics for the next layer's folded
+ * LayerNorm: per row and 256-column block, (mean, M2) = (the block's mean, its sum of squared deviations) of the
+ * bf16 outputs, "row partials" [M][N / 256] fp32 pairs.  The next up_conv kernel merges a row's blocks into
+ * (rstd, rstd * mean) with the equal-count update of Chan et al.; no statistics launch and no extra read of x.
+ * The merged statistics equal the two-pass ones up to fp32 rounding.
+ *
+ * gsn_gemm2_residual_stats_bf16: gsn_gemm2_residual_bf16 that also writes row_partials [M][N / 256] (every row of
+ * the M range, padding rows included).  N % 256 == 0.
+ * gsn_gemm1_lnfold_partials_glu_dwconv_bf16: gsn_gemm1_lnfold_glu_dwconv_bf16 with the row statistics formed from
+ * row_partials [B*T][K / 256] (K % 256 == 0, K <= 2048) and ln_eps instead of read from row_stats.
+ * gsn_conv_module_lnfold_chain_bf16: gsn_conv_module_lnfold_bf16 for one layer of such a stack.  stats_in: the row
+ * partials of x written by the previous layer's call, or NULL (the first layer: a statistics launch as in
+ * gsn_conv_module_lnfold_bf16); stats_out: where to write the row partials of out, or NULL.  Both [B*T][D / 256]
+ * fp32 pairs, 8-byte aligned; they may be the same buffer (the up_conv kernel has read stats_in before the
+ * down_conv kernel writes stats_out, on the same stream).  Workspace as for gsn_conv_module_bf16. */
+int gsn_gemm2_residual_stats_bf16(const void* d, const void* w2, const float* b2, const void* residual,
+                                  int64_t ld_res, void* out, int64_t ld_out, int M, int K, int N,
+                                  const int32_t* lengths, int T, float* row_partials, gsn_stream_t stream);
+
+int gsn_gemm1_lnfold_partials_glu_dwconv_bf16(const void* x, const void* w1g_glu, const float* b1g_glu,
+                                              const float* c1_glu, const float* row_partials, float ln_eps,
+                                              const void* dw_w, const void* dw_b, void* d, int B, int T, int K,
+                                              int N, const int32_t* lengths, gsn_stream_t stream);
+
+int gsn_conv_module_lnfold_chain_bf16(const void* x, const void* w1g_glu, const float* b1g_glu, const float* c1_glu,
+                                      const void* dw_w, const void* dw_b, const void* w2, const float* b2,
+                                      const int32_t* lengths, int add_residual, void* out, int B, int T, int D,
+                                      int inner, float ln_eps, const float* stats_in, float* stats_out,
+                                      void* workspace, size_t workspace_bytes, gsn_stream_t stream);
+
 /* ---- int8 weights widened once per call -------------------------------------------------------------------
  * No counterpart in the reference (its int8 analogue is torchao W8A8, bench_asr.py:92-105).  For large M the
  * weight bytes are negligible next to the activations, so the int8 module widens both weight matrices to bf16
