@@ -188,7 +188,8 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
     // ------------------------------------------------------------------ producer
     int issued = 0;
     bool ok = true;
-    int slot_c0[2] = {-1, -1}, slot_last[2] = {-1, -1};     // table slots: channel block, last item using it
+    int slot_c0a = -1, slot_c0b = -1, slot_lasta = -1, slot_lastb = -1;   // table slots 0 / 1: channel block, last
+                                                                      //   item using it (scalars: kept in registers)
     for (int i = 0; i < n_items && ok; ++i) {
       const int st = i % STAGES;
       if (i >= STAGES) {
@@ -211,10 +212,10 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
       // the channel block's Toeplitz tables: kept in TSLOTS slots; a new block takes the slot used longer ago,
       // after the MMAs of that slot's last item are done.  Channel c's table holds B[n, k] = w[k - n - 1] / 2 as
       // core matrices (n-group g, k-chunk h) at (2 h + g) * 128 bytes, row n % 8 at 16 (n % 8), element k % 8
-      int slot = c0 == slot_c0[0] ? 0 : (K::TSLOTS > 1 && c0 == slot_c0[1] ? 1 : -1);
+      int slot = c0 == slot_c0a ? 0 : (K::TSLOTS > 1 && c0 == slot_c0b ? 1 : -1);
       if (slot < 0) {
-        slot = K::TSLOTS == 1 || slot_last[0] <= slot_last[1] ? 0 : 1;
-        const int last = slot_last[slot];
+        slot = K::TSLOTS == 1 || slot_lasta <= slot_lastb ? 0 : 1;
+        const int last = slot ? slot_lastb : slot_lasta;
         if (last >= 0 && i - last < STAGES) {                // its stage not reused yet: wait for that item's MMAs
           bool got = mbar_wait_bounded(&s.empty[last % STAGES], (uint32_t)((last / STAGES) & 1), abort_flag,
                                        kStatusTimeoutProducer);
@@ -244,9 +245,9 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
               make_uint4(wd[0], wd[1], wd[2], wd[3]);
         }
         __syncwarp();
-        slot_c0[slot] = c0;
+        if (slot) slot_c0b = c0; else slot_c0a = c0;
       }
-      slot_last[slot] = i;
+      if (slot) slot_lastb = i; else slot_lasta = i;
       if (lane == 0) s.st_slot[st] = slot;                   // read by the issuers after the stage's full barrier
       // staged frames [t0 - 8, t0 + 1040) of the ROWS rows (GLU form: CT value rows, then their CT gate rows):
       // frames [lo, hi8) by bulk copy, the ragged end [hi8, hi) of an utterance (len % 8 != 0) by a masked 16-byte
