@@ -209,6 +209,27 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
         if (lane == 0) mbar_arrive(&s.full[st]);
         continue;
       }
+      // staged frames [t0 - 8, t0 + 1040) of the ROWS rows (GLU form: CT value rows, then their CT gate rows):
+      // frames [lo, hi8) by bulk copy, the ragged end [hi8, hi) of an utterance (len % 8 != 0) by a masked 16-byte
+      // copy, zeros elsewhere (before frame 0, from len on; a zero value and gate give a zero GLU)
+      const int f_begin = t0 - 8;
+      const int lo = max(f_begin, 0);                        // multiple of 8
+      const int hi = min(t0 + FR + 16, len);                 // > lo: t0 < len
+      const int hi8 = hi & ~7;
+      uint8_t* xs = s.x[st];
+      // element offset of staged row r in x: value channel c0 + r, or the gate row of value channel c0 + r - CT
+      auto row_off = [&](int r) {
+        return (int64_t)b * p.sxB + (int64_t)(c0 + (r < CT ? r : r - CT)) * p.sxC + (r < CT ? 0 : p.gate_off);
+      };
+      // the bulk copies go first, so their latency runs under the table build and the hand-written chunks; the
+      // stage's phase cannot complete before the arrive below (its one expected arrival), which also sets the
+      // byte count the copies' completions are counted against
+      const uint32_t row_bytes = hi8 > lo ? (uint32_t)(hi8 - lo) * 2 : 0u;
+      ++issued;
+      if (row_bytes > 0 && lane < ROWS && i != p.withhold) {   // test only: a withheld item's copies never start
+        const __nv_bfloat16* src = p.x + row_off(lane) + lo;
+        bulk_load(xs + lane * ROW_BYTES + (lo - f_begin) * 2, src, row_bytes, &s.full[st]);
+      }
       // the channel block's Toeplitz tables: kept in TSLOTS slots; a new block takes the slot used longer ago,
       // after the MMAs of that slot's last item are done.  Channel c's table holds B[n, k] = w[k - n - 1] / 2 as
       // core matrices (n-group g, k-chunk h) at (2 h + g) * 128 bytes, row n % 8 at 16 (n % 8), element k % 8
@@ -221,6 +242,8 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
                                        kStatusTimeoutProducer);
           got = __shfl_sync(0xffffffffu, got, 0);
           if (!got) {
+            // the copies just issued are counted on this stage's barrier, so the unwind below waits for them
+            if (lane == 0) mbar_arrive_expect_tx(&s.full[st], row_bytes * ROWS);
             ok = false;
             break;
           }
@@ -249,23 +272,11 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
       }
       if (slot) slot_lastb = i; else slot_lasta = i;
       if (lane == 0) s.st_slot[st] = slot;                   // read by the issuers after the stage's full barrier
-      // staged frames [t0 - 8, t0 + 1040) of the ROWS rows (GLU form: CT value rows, then their CT gate rows):
-      // frames [lo, hi8) by bulk copy, the ragged end [hi8, hi) of an utterance (len % 8 != 0) by a masked 16-byte
-      // copy, zeros elsewhere (before frame 0, from len on; a zero value and gate give a zero GLU)
-      const int f_begin = t0 - 8;
-      const int lo = max(f_begin, 0);                        // multiple of 8
-      const int hi = min(t0 + FR + 16, len);                 // > lo: t0 < len
-      const int hi8 = hi & ~7;
-      uint8_t* xs = s.x[st];
       // chunks to write by hand: the head chunk (frames -8 .. -1) when t0 = 0, and from hi8 on the tail (the ragged
       // chunk [hi8, hi), then zeros); a tile inside the utterance has neither
       const int head = lo > f_begin ? 1 : 0;
       const int tail0 = (hi8 - f_begin) / 8;                 // first tail chunk of a row
       const int per_row = head + (ROWF / 8 - tail0);
-      // element offset of staged row r in x: value channel c0 + r, or the gate row of value channel c0 + r - CT
-      auto row_off = [&](int r) {
-        return (int64_t)b * p.sxB + (int64_t)(c0 + (r < CT ? r : r - CT)) * p.sxC + (r < CT ? 0 : p.gate_off);
-      };
       for (int q = lane; q < ROWS * per_row; q += 32) {
         const int c = q / per_row, j = q - c * per_row;
         const int ch = (j < head) ? 0 : tail0 + (j - head);  // chunk index within the row
@@ -286,14 +297,8 @@ __global__ void __launch_bounds__(Cfg<FORM>::THREADS, MINB) dwconv_cf_mma_kernel
       }
       fence_proxy_async_smem();               // generic writes (zeros, tables) before the tensor core reads them
       __syncwarp();
-      const uint32_t row_bytes = hi8 > lo ? (uint32_t)(hi8 - lo) * 2 : 0u;
-      ++issued;
       if (lane == 0) mbar_arrive_expect_tx(&s.full[st], row_bytes * ROWS);
       __syncwarp();
-      if (row_bytes > 0 && lane < ROWS && i != p.withhold) {   // test only: a withheld item's copies never start
-        const __nv_bfloat16* src = p.x + row_off(lane) + lo;
-        bulk_load(xs + lane * ROW_BYTES + (lo - f_begin) * 2, src, row_bytes, &s.full[st]);
-      }
     }
     if (!ok && lane == 0) {
       // unwinding: the copies of the last STAGES items may still be in flight
