@@ -1142,8 +1142,12 @@ def _kernel_breakdown(layer_events, peaks, widen_events=(), ln_name="layernorm")
 
 
 def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn=False, block=False, heads=None):
-    """Same work through the public op (torch.ops.granite.conv_module per layer, or granite::feed_forward_half)
-    with each chunk's input copied from pinned host memory and its output copied back inside the timed region."""
+    """Same work through the public API (ConvModuleStack, the feed-forward / attention / block ops, the encoder)
+    with each chunk's input copied from pinned host memory and its output copied back inside the timed region.
+    Consecutive steps are pipelined as a streaming server runs them: a chunk's next upload waits only for the
+    compute that read its device buffer, so the next step's first uploads overlap this step's last chunks; every
+    step still moves all of its inputs and outputs across the host link inside the timed region, which ends when
+    the last step's last download has landed."""
     import torch
 
     from granite_conv_b200 import ConvModuleStack, ops
@@ -1193,11 +1197,21 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
     ld = [torch.empty((c.B,), dtype=torch.int32, device=dev) for c in chunks]
     done = [None] * len(chunks)
 
-    def step():
-        begin = torch.cuda.Event()          # the step's copies start after everything queued before it
-        begin.record(stream)
+    def start():
+        begin = torch.cuda.Event()          # the copies start after everything queued before them (e.g. the start
+        begin.record(stream)                #   event of the timed region)
         copy_in.wait_event(begin)
         comp[1].wait_event(begin)
+
+    def finish():
+        fin = torch.cuda.Event()            # the current stream waits for the last download and the side stream
+        fin.record(copy_out)
+        stream.wait_event(fin)
+        side = torch.cuda.Event()
+        side.record(comp[1])
+        stream.wait_event(side)
+
+    def step():
         for ci in range(len(chunks)):
             cs = comp[ci % 2]
             with torch.cuda.stream(copy_in):
@@ -1216,21 +1230,19 @@ def _e2e(args, chunks, layers, int8, dev, stream, world, barrier, ff=False, attn
                 copy_out.wait_event(done[ci])
                 ho[ci].copy_(y, non_blocking=True)
                 y.record_stream(copy_out)
-        fin = torch.cuda.Event()
-        fin.record(copy_out)
-        stream.wait_event(fin)
-        side = torch.cuda.Event()
-        side.record(comp[1])
-        stream.wait_event(side)
 
+    start()
     for _ in range(max(1, args.warmup)):
         step()
+    finish()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    start()
     for _ in range(args.steps):
         step()
+    finish()
     e1.record(stream)
     barrier()
     ms = e0.elapsed_time(e1)
