@@ -163,3 +163,33 @@ def test_selftest_withheld_validation_without_gpu():
     assert L.gsn_selftest_gemm_withheld_bf16(p, p, p, p, p, 128, 1024, 100, None) == 2     # N % 256
     assert L.gsn_selftest_dwconv_withheld_bf16(p, p, p, p, -1, 8, 8, 64, 8, 1, 64, 8, 1, None) == 1
     assert L.gsn_selftest_gemm_withheld_bf16(None, None, None, None, None, 0, 1024, 1024, None) == 0   # empty
+
+
+def test_chain_entry_points_validate_without_gpu():
+    """The chained-stack entry points reject bad arguments before any CUDA work."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(260)                     # 4-byte aligned only
+    # residual GEMM with row statistics: N must be a multiple of 256, the statistics 8-byte aligned
+    assert L.gsn_gemm2_residual_stats_bf16(p, p, p, p, 1024, p, 1024, 128, 2048, 1024, None, 0, None, None) == 1
+    assert "null row_partials" in _lib.last_error()
+    assert L.gsn_gemm2_residual_stats_bf16(p, p, p, p, 1024, p, 1024, 128, 2048, 1024, None, 0, odd, None) == 2
+    assert "8-byte" in _lib.last_error()
+    # fused kernel with merged statistics: K % 256 == 0 and K <= 2048
+    assert L.gsn_gemm1_lnfold_partials_glu_dwconv_bf16(p, p, p, p, p, 1e-5, p, p, p, 1, 128, 640, 4096, None,
+                                                         None) == 2
+    assert L.gsn_gemm1_lnfold_partials_glu_dwconv_bf16(p, p, p, p, p, 1e-5, p, p, p, 1, 128, 4096, 4096, None,
+                                                         None) == 2
+    assert "K <= 2048" in _lib.last_error()
+    assert L.gsn_gemm1_lnfold_partials_glu_dwconv_bf16(p, p, p, p, None, 1e-5, p, p, p, 1, 128, 1024, 4096, None,
+                                                         None) == 1
+    # one chained layer: misaligned statistics, T off the 128 grid, empty problems
+    nb = L.gsn_conv_module_workspace_bytes(1, 128, 1024, 2048)
+    rc = L.gsn_conv_module_lnfold_chain_bf16(*([p] * 8), None, 1, p, 1, 128, 1024, 2048, 1e-5, odd, None, p, nb,
+                                             None)
+    assert rc == 2 and "8-byte" in _lib.last_error()
+    rc = L.gsn_conv_module_lnfold_chain_bf16(*([p] * 8), None, 1, p, 1, 100, 1024, 2048, 1e-5, None, None, p, nb,
+                                             None)
+    assert rc == 2 and "multiple of 128" in _lib.last_error()
+    assert L.gsn_conv_module_lnfold_chain_bf16(*([None] * 8), None, 1, None, 0, 128, 1024, 2048, 1e-5, None, None,
+                                               None, 0, None) == 0
