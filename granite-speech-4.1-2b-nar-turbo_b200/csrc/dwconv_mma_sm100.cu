@@ -25,7 +25,7 @@
 //               frame 0 and from len on, the ragged last chunk of an utterance), then one bulk copy per row for the
 //               rest (16-byte aligned: T % 8 == 0); builds a channel block's 16 Toeplitz tables (from weights
 //               staged in shared memory) into one of two table slots when the block changes (the GLU form
-//               without lengths: one slot); 4 stages (GLU form without lengths: 3)
+//               without lengths: one slot); 5 stages (GLU form: 3 without lengths, 4 with)
 //   warps 1-2   MMA issuers (warp 1 also allocates TMEM): each issues the 8 MMAs of its 4 channels per item into
 //               one of two 128-column accumulators (16 columns per channel).  An M=128, N=16 MMA runs in a few
 //               cycles but takes about a hundred to issue, so the issue is split
@@ -71,7 +71,7 @@ struct Cfg {
   static constexpr int CT = FORM == kGluMasked ? 4 : 8;   // channels per item
   static constexpr int ROWS = GLU ? 2 * CT : CT;         // staged rows per item: value rows, then gate rows
   static constexpr int STAGE_BYTES = ROWS * ROW_BYTES;
-  static constexpr int STAGES = FORM == kGluDense ? 3 : 4;
+  static constexpr int STAGES = FORM == kGluDense ? 3 : (FORM == kPlain ? 5 : 4);
   static constexpr int TSLOTS = FORM == kGluDense ? 1 : 2;   // Toeplitz table slots (channel blocks kept)
   static constexpr int CPI = CT / NISS;
   static constexpr int EPI_CH = CT * 4 / EPI_WARPS;  // channels per epilogue warp, in batches of EB
