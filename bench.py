@@ -878,6 +878,9 @@ def run_ours(args):
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                 "per_launch_ms": dur, "algorithmic_bytes_per_frame": bpf,
                 "peak_source": f"hbm_gbs of {peaks['source']}"}
+        if workload in ("dw_cf", "dw_cf_glu"):
+            roof["gpu_comparator"] = _dw_torch_eager(xs[0], ys[0], dw_w, dw_b, workload == "dw_cf_glu", stream, dur,
+                                                     frames * bpf)
     elif w8a8:
         dur = sum(a.elapsed_time(b) for a, b, _ in w8_events) / len(w8_events)
         rows = sum(sum(-(-int(L_) // 128) * 128 for L_ in c.lengths) for _, _, c in w8_events) / len(w8_events)
@@ -983,6 +986,38 @@ def secondary_configs(args) -> dict:
                   "peak_source": r.get("peak_source"), "clocks": ln["clocks"], "steps": 20, "warmup": 5,
                   "gpu_launches": ln["gpu_launches"]}
     return out
+
+
+def _dw_torch_eager(x, y_ours, dw_w, dw_b, glu, stream, our_ms, algo_bytes):
+    """The comparison the reference's own depthwise microbenchmark makes (script/cuda_kernels/conv1d.py:118-145),
+    on this GPU: torch's eager ops for the same call -- [F.glu(x, dim=1)], F.conv1d(groups=C, padding=7) (cuDNN) and
+    F.silu, bf16 -- timed with CUDA events over 20 launches after 5 warm-up calls, and their largest difference from
+    this package's output."""
+    import torch
+    import torch.nn.functional as F
+    C = dw_w.shape[0]
+    w3 = dw_w.view(C, 1, -1)
+
+    def eager():
+        h = F.glu(x, dim=1) if glu else x
+        return F.silu(F.conv1d(h, w3, dw_b, padding=w3.shape[-1] // 2, groups=C))
+
+    for _ in range(5):
+        ref = eager()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(20):
+        ref = eager()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    d = (ref.float() - y_ours.float()).abs()
+    return {"what": "torch eager on this GPU: " + ("F.glu, " if glu else "") +
+                    "depthwise F.conv1d (cuDNN) and F.silu in bf16, the reference microbenchmark's comparison",
+            "per_launch_us": ms * 1e3, "achieved_gbs": algo_bytes / (ms / 1e3) / 1e9,
+            "this_kernel_speedup": ms / our_ms,
+            "max_abs_diff": float(d.max()), "max_rel_to_gate": float((d / (2e-2 * ref.float().abs().clamp(min=1.0))).max())}
 
 
 def _tile_rows(c, tile=128):
